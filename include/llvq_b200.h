@@ -1,0 +1,107 @@
+/*
+ * llvq_b200.h -- C ABI of the B200 (sm_100a) Leech-lattice (Λ24) quantizer.
+ *
+ * Plain pointers and sizes only.  Device pointers must be on the codebook's
+ * device; `stream` is a cudaStream_t (NULL = legacy default stream).  Every
+ * GPU entry point is asynchronous on `stream`, never synchronises, and returns
+ * a status code (llvq_status); llvq_last_error() gives the message of the last
+ * failure on the calling thread.
+ *
+ * The drop-in boundary replaces the reference's two NVRTC launchers of
+ * dmnunez1993/llvq-paper-reproduction:
+ *   impl/llvq_cuda_quantize.py:544-602    quantize_lattice_cuda
+ *   impl/llvq_cuda_dequantize.py:221-261  dequantize_lattice_cuda
+ * and the device tables its caller builds
+ *   impl/leech_lattice_vector_quantizer_gpu.py:345-411  _quantize_cuda_metadata
+ *   impl/leech_lattice_vector_quantizer_gpu.py:424-518  _codeword_cuda_metadata
+ */
+#ifndef LLVQ_B200_H
+#define LLVQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct llvq_codebook llvq_codebook;
+
+typedef enum {
+  LLVQ_OK = 0,
+  LLVQ_ERR_INVALID_ARGUMENT = 1, /* the reference raises ValueError (bad device, dtype, shape) */
+  LLVQ_ERR_CUDA = 2,             /* the reference raises RuntimeError(str(CUresult)) */
+  LLVQ_ERR_UNSUPPORTED = 3,      /* codebook the library cannot index in int64 */
+  LLVQ_ERR_OUT_OF_MEMORY = 4,
+  LLVQ_ERR_INDEX_RANGE = 5,      /* the reference raises IndexError */
+  LLVQ_ERR_NOT_A_CODEWORD = 6    /* the reference's encode_codeword raises ValueError */
+} llvq_status;
+
+/* Output kinds of the dequantizer. */
+enum {
+  LLVQ_OUT_INT64 = 0,          /* integer codeword (dequantize_lattice) */
+  LLVQ_OUT_F32 = 1,            /* fp32(1/sqrt 8) * k in fp32: the GPU API's dequantize (_gpu.py:298) */
+  LLVQ_OUT_F32_DOUBLE = 2,     /* the CPU API's double 1/sqrt(8) * k, rounded to fp32 (CPU module :243-245) */
+  LLVQ_OUT_BF16_ROWSCALE = 3   /* bf16(fp32 value * fp16 per-row scale) */
+};
+
+/* Quantizer option flags. */
+enum { LLVQ_FLAG_TABLE_DRIVEN = 1 /* score with the table-driven chains even if generated code exists */ };
+
+/* Codebook from a class list in index order (shell ascending, then the
+ * reference's class order): per class its shell, parity (0 even, 1 odd) and
+ * the 24 absolute values of its leader in descending order.  Builds the Golay
+ * tables, offsets and counts on the host and uploads them to `device`
+ * (device < 0: host-only codebook, usable by the *_host functions).
+ * Replaces the table construction of LeechLatticeVectorQuantizerGpu.__init__
+ * and its two *_cuda_metadata caches (_gpu.py:154-212, :345-518). */
+int llvq_codebook_create(int32_t n_classes, const int32_t* shell, const int32_t* parity, const int32_t* leader,
+                         int device, llvq_codebook** out);
+void llvq_codebook_destroy(llvq_codebook* cb);
+/* total_count (= reference total_count), class count, shell range, and whether
+ * generated scoring code matches this class list (1) or the table-driven path runs (0). */
+int llvq_codebook_info(const llvq_codebook* cb, int64_t* total_count, int32_t* n_classes, int32_t* min_shell,
+                       int32_t* max_shell, int32_t* specialized);
+
+/* Nearest codeword of each 24-D fp32 row: indices[i] is the reference index
+ * (bit-exact with LeechLatticeVectorQuantizer.quantize, ties in its loop
+ * order), best_pair[i] = class_id * 4096 + golay_index and best_score[i] the
+ * fp32 rounding of the reference's fp64 score.  Rows with NaN/Inf get index,
+ * pair -1 and score NaN.  best_pair and best_score double as the hand-over
+ * between the search and finalize kernels.  Replaces quantize_lattice_cuda
+ * (impl/llvq_cuda_quantize.py:544-602). */
+int llvq_quantize(const llvq_codebook* cb, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
+                  float* best_score, void* stream);
+int llvq_quantize_ex(const llvq_codebook* cb, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
+                     float* best_score, uint32_t flags, void* stream);
+
+/* Integer codewords [n,24] of indices [n].  Out-of-range indices give zero
+ * rows and are counted into *error_count (device int, may be NULL).
+ * Replaces dequantize_lattice_cuda (impl/llvq_cuda_dequantize.py:221-261). */
+int llvq_dequantize_lattice(const llvq_codebook* cb, const int64_t* indices, int64_t n, int64_t* out,
+                            int32_t* error_count, void* stream);
+/* Scaled fp32 vectors [n,24] (kind LLVQ_OUT_F32 or LLVQ_OUT_F32_DOUBLE).
+ * Replaces LeechLatticeVectorQuantizerGpu.dequantize on tensors (_gpu.py:290-298). */
+int llvq_dequantize(const llvq_codebook* cb, const int64_t* indices, int64_t n, float* out, int32_t kind,
+                    int32_t* error_count, void* stream);
+/* bf16 weights [n,24] = bf16(dequantize * row_scale[i / blocks_per_row]),
+ * row_scale fp16 bit patterns.  No reference counterpart (the reference has
+ * neither bf16 output nor per-row scales). */
+int llvq_dequantize_bf16(const llvq_codebook* cb, const int64_t* indices, int64_t n, const uint16_t* row_scale_f16,
+                         int64_t blocks_per_row, uint16_t* out_bf16, int32_t* error_count, void* stream);
+
+/* Host-side scalar paths (no GPU needed).
+ * llvq_codeword_host:  LeechLatticeVectorQuantizerGpu.codeword (_gpu.py:262-265)
+ * llvq_encode_host:    LeechLatticeVectorQuantizer.encode_codeword (CPU module :247-280) */
+int llvq_codeword_host(const llvq_codebook* cb, int64_t index, int32_t* out24);
+int llvq_encode_host(const llvq_codebook* cb, const int32_t* codeword24, int64_t* index);
+
+const char* llvq_status_string(int status);
+const char* llvq_last_error(void);
+int llvq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLVQ_B200_H */

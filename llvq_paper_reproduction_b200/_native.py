@@ -1,0 +1,173 @@
+"""ctypes binding of the in-tree CUDA library (include/llvq_b200.h).
+
+The library is the only compute path: if it is missing this module raises at
+import time instead of falling back to anything else.  Status codes map to
+the exception types the reference raises (ValueError, RuntimeError,
+IndexError).
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+from typing import Sequence
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libllvq_b200.so"
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_CUDA = 2
+ERR_UNSUPPORTED = 3
+ERR_OUT_OF_MEMORY = 4
+ERR_INDEX_RANGE = 5
+ERR_NOT_A_CODEWORD = 6
+
+OUT_INT64 = 0
+OUT_F32 = 1
+OUT_F32_DOUBLE = 2
+OUT_BF16_ROWSCALE = 3
+FLAG_TABLE_DRIVEN = 1
+
+# Every symbol the public header declares (checked by the CPU test suite).
+EXPORTS = (
+    "llvq_codebook_create", "llvq_codebook_destroy", "llvq_codebook_info", "llvq_quantize", "llvq_quantize_ex",
+    "llvq_dequantize_lattice", "llvq_dequantize", "llvq_dequantize_bf16", "llvq_codeword_host",
+    "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version",
+)
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m llvq_paper_reproduction_b200.build`")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        vp, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+        P = ctypes.POINTER
+        sig = {
+            "llvq_codebook_create": (ctypes.c_int, [i32, vp, vp, vp, ctypes.c_int, P(vp)]),
+            "llvq_codebook_destroy": (None, [vp]),
+            "llvq_codebook_info": (ctypes.c_int, [vp, P(i64), P(i32), P(i32), P(i32), P(i32)]),
+            "llvq_quantize": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, vp]),
+            "llvq_quantize_ex": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, ctypes.c_uint32, vp]),
+            "llvq_dequantize_lattice": (ctypes.c_int, [vp, vp, i64, vp, vp, vp]),
+            "llvq_dequantize": (ctypes.c_int, [vp, vp, i64, vp, i32, vp, vp]),
+            "llvq_dequantize_bf16": (ctypes.c_int, [vp, vp, i64, vp, i64, vp, vp, vp]),
+            "llvq_codeword_host": (ctypes.c_int, [vp, i64, vp]),
+            "llvq_encode_host": (ctypes.c_int, [vp, vp, P(i64)]),
+            "llvq_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+            "llvq_last_error": (ctypes.c_char_p, []),
+            "llvq_version": (ctypes.c_int, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def check(status: int, what: str) -> None:
+    """Raise the exception type the reference raises for this failure."""
+    if status == OK:
+        return
+    lib = load()
+    msg = f"{what}: {lib.llvq_status_string(status).decode()}: {lib.llvq_last_error().decode()}"
+    if status == ERR_INDEX_RANGE:
+        raise IndexError(msg)
+    if status in (ERR_INVALID_ARGUMENT, ERR_NOT_A_CODEWORD, ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    if status == ERR_OUT_OF_MEMORY:
+        raise MemoryError(msg)
+    raise RuntimeError(msg)
+
+
+class NativeCodebook:
+    """Owner of one llvq_codebook handle (tables on one device, or host-only
+    when device < 0)."""
+
+    def __init__(self, shells: Sequence[int], parities: Sequence[int], leaders: Sequence[Sequence[int]],
+                 device: int = -1):
+        lib = load()
+        n = len(shells)
+        sh = np.ascontiguousarray(shells, dtype=np.int32)
+        pa = np.ascontiguousarray(parities, dtype=np.int32)
+        le = np.ascontiguousarray(leaders, dtype=np.int32).reshape(n, 24)
+        h = ctypes.c_void_p()
+        check(lib.llvq_codebook_create(n, sh.ctypes.data, pa.ctypes.data, le.ctypes.data, int(device),
+                                       ctypes.byref(h)), "llvq_codebook_create")
+        self._lib = lib
+        self.handle = h.value
+        self.device = int(device)
+        total, ncls, lo, hi, spec = ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32(), \
+            ctypes.c_int32()
+        check(lib.llvq_codebook_info(self.handle, ctypes.byref(total), ctypes.byref(ncls), ctypes.byref(lo),
+                                     ctypes.byref(hi), ctypes.byref(spec)), "llvq_codebook_info")
+        self.total_count = total.value
+        self.n_classes = ncls.value
+        self.min_shell = lo.value
+        self.max_shell = hi.value
+        self.specialized = bool(spec.value)
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h:
+            try:
+                self._lib.llvq_codebook_destroy(h)
+            except Exception:  # interpreter teardown
+                pass
+            self.handle = None
+
+    # ---- host paths
+    def codeword(self, index: int) -> tuple[int, ...]:
+        out = (ctypes.c_int32 * 24)()
+        check(self._lib.llvq_codeword_host(self.handle, int(index), out), "llvq_codeword_host")
+        return tuple(out)
+
+    def encode(self, vector: Sequence[int]) -> int:
+        v = (ctypes.c_int32 * 24)(*[int(a) for a in vector])
+        idx = ctypes.c_int64()
+        check(self._lib.llvq_encode_host(self.handle, v, ctypes.byref(idx)), "llvq_encode_host")
+        return idx.value
+
+    # ---- device paths (raw pointers; the callers own allocation and streams)
+    def quantize(self, x_ptr: int, n: int, idx_ptr: int, pair_ptr: int, score_ptr: int, stream: int,
+                 flags: int = 0) -> None:
+        check(self._lib.llvq_quantize_ex(self.handle, x_ptr, n, idx_ptr, pair_ptr, score_ptr, flags, stream),
+              "llvq_quantize")
+
+    def dequantize_lattice(self, idx_ptr: int, n: int, out_ptr: int, err_ptr: int | None, stream: int) -> None:
+        check(self._lib.llvq_dequantize_lattice(self.handle, idx_ptr, n, out_ptr, err_ptr, stream),
+              "llvq_dequantize_lattice")
+
+    def dequantize(self, idx_ptr: int, n: int, out_ptr: int, kind: int, err_ptr: int | None, stream: int) -> None:
+        check(self._lib.llvq_dequantize(self.handle, idx_ptr, n, out_ptr, kind, err_ptr, stream), "llvq_dequantize")
+
+    def dequantize_bf16(self, idx_ptr: int, n: int, scale_ptr: int, blocks_per_row: int, out_ptr: int,
+                        err_ptr: int | None, stream: int) -> None:
+        check(self._lib.llvq_dequantize_bf16(self.handle, idx_ptr, n, scale_ptr, blocks_per_row, out_ptr, err_ptr,
+                                             stream), "llvq_dequantize_bf16")
+
+
+_CACHE: dict = {}
+
+
+def codebook_for(shells, parities, leaders, device: int) -> NativeCodebook:
+    """Codebooks are cached per (class list, device): building one uploads
+    its tables once."""
+    key = (np.asarray(shells, dtype=np.int32).tobytes(), np.asarray(parities, dtype=np.int32).tobytes(),
+           np.asarray(leaders, dtype=np.int32).tobytes(), int(device))
+    cb = _CACHE.get(key)
+    if cb is None:
+        cb = NativeCodebook(shells, parities, leaders, device)
+        _CACHE[key] = cb
+    return cb

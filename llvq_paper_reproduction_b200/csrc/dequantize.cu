@@ -1,0 +1,92 @@
+// Λ24 index -> codeword dequantizer for sm_100a.
+//
+// Reference: LeechLatticeVectorQuantizerGpu.dequantize / dequantize_lattice
+// (impl/leech_lattice_vector_quantizer_gpu.py:267-298) and its NVRTC kernel
+// (impl/llvq_cuda_dequantize.py:78-181); index layout and unranking as in the
+// CPU codeword() path (impl/leech_lattice_vector_quantizer.py:196-245,
+// :774-867).  One thread decodes one index: class by binary search over the
+// class starts, then the mixed-radix split (Golay choice, sign rank,
+// permutation rank), multiset unranking and sign unranking.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "llvq_device.cuh"
+#include "llvq_internal.h"
+
+namespace llvq {
+
+template <int KIND>
+__global__ void dequant_kernel(const int64_t* __restrict__ index, int64_t n, DevBook book, void* __restrict__ out,
+                               const uint16_t* __restrict__ row_scale, int64_t blocks_per_row, int* error_count) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int64_t v = index[i];
+  int y[kDim];
+  bool ok = v >= 0 && v < book.total;
+  if (ok) {
+    const int k = find_class(book.class_start, book.n_classes, v);
+    const DevClass& c = book.cls[k];
+    const int wbase = book.weight_start[c.even_weight];
+    ok = unrank_codeword(
+        c, (uint64_t)(v - c.start),
+        [&](int g) -> uint32_t {
+          return c.parity ? __ldg(book.golay + g) : __ldg(book.golay + __ldg(book.by_weight + wbase + g));
+        },
+        y);
+  }
+  if (!ok) {
+#pragma unroll
+    for (int d = 0; d < kDim; ++d) y[d] = 0;
+    if (error_count) atomicAdd(error_count, 1);
+  }
+  if constexpr (KIND == 0) {
+    longlong2* o = reinterpret_cast<longlong2*>(static_cast<long long*>(out) + i * kDim);
+#pragma unroll
+    for (int d = 0; d < kDim; d += 2) o[d / 2] = make_longlong2(y[d], y[d + 1]);
+  } else if constexpr (KIND == 1 || KIND == 2) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + i * kDim);
+    float f[kDim];
+#pragma unroll
+    for (int d = 0; d < kDim; ++d) {
+      // KIND 1: fp32(1/sqrt 8) * fp32(k) rounded to fp32 (the GPU API's torch
+      // multiply); KIND 2: the double product rounded to fp32 (CPU API).
+      f[d] = KIND == 1 ? __fmul_rn(kLatticeScaleF, (float)y[d]) : (float)(kLatticeScaleD * (double)y[d]);
+    }
+#pragma unroll
+    for (int d = 0; d < kDim; d += 4) o[d / 4] = make_float4(f[d], f[d + 1], f[d + 2], f[d + 3]);
+  } else {
+    const float s = __half2float(__ushort_as_half(row_scale[i / blocks_per_row]));
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + i * kDim);
+    uint32_t w[kDim / 2];
+#pragma unroll
+    for (int d = 0; d < kDim; d += 2) {
+      const float a = __fmul_rn(__fmul_rn(kLatticeScaleF, (float)y[d]), s);
+      const float b = __fmul_rn(__fmul_rn(kLatticeScaleF, (float)y[d + 1]), s);
+      const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+      w[d / 2] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+#pragma unroll
+    for (int d = 0; d < kDim / 2; d += 4) o[d / 4] = make_uint4(w[d], w[d + 1], w[d + 2], w[d + 3]);
+  }
+}
+
+cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t n, void* out, int kind,
+                              const uint16_t* row_scale, int64_t blocks_per_row, int* error_count,
+                              cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  const int threads = 128;
+  const unsigned blocks = (unsigned)((n + threads - 1) / threads);
+  switch (kind) {
+    case 0: dequant_kernel<0><<<blocks, threads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, error_count); break;
+    case 1: dequant_kernel<1><<<blocks, threads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, error_count); break;
+    case 2: dequant_kernel<2><<<blocks, threads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, error_count); break;
+    case 3: dequant_kernel<3><<<blocks, threads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, error_count); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace llvq

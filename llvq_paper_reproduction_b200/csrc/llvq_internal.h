@@ -1,0 +1,55 @@
+// Internal (C++) interfaces between the codebook builder, the kernels and the
+// C-ABI layer.  Not part of the public header.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "llvq_device.cuh"
+
+namespace llvq {
+
+using SearchLauncher = cudaError_t (*)(const float*, int64_t, const DevBook&, long long*, float*, cudaStream_t);
+
+// A generated search specialisation: its class signature, launcher and the
+// window constants of its FFMA chains.
+struct SpecEntry {
+  const int* sig;
+  SearchLauncher launch;
+  const char* name;
+  float l1max, win_mg, win_am;
+};
+
+struct Codebook {
+  int device = -1;
+  int min_shell = 0, max_shell = 0;
+  int64_t total = 0;
+  std::vector<DevClass> cls;           // host copy, global class order
+  std::vector<int64_t> class_start;
+  std::vector<uint32_t> golay;         // lexicographic order
+  std::vector<uint16_t> golay_wrank;
+  std::vector<uint32_t> wlist_word;
+  std::vector<uint16_t> wlist_lex;
+  std::vector<uint16_t> by_weight;
+  int32_t weight_start[25] = {};
+  DevBook dev{};                       // device pointers (valid when device >= 0)
+  void* dev_alloc = nullptr;
+  size_t dev_bytes = 0;
+  const SpecEntry* spec = nullptr;     // generated search code for this class list, or null
+  float rt_l1max = 0, rt_mg = 0, rt_am = 0;  // window constants of the table-driven chains
+};
+
+const SpecEntry* spec_table(int* count);
+
+cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long long* index, long long* pair,
+                            float* score, cudaStream_t stream, bool force_runtime);
+
+// kind: 0 int64 codewords, 1 fp32 (fp32(1/sqrt 8) * k, torch semantics),
+// 2 fp32 (fp32 of the double product), 3 bf16 with per-row fp16 scale.
+cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t n, void* out, int kind,
+                              const uint16_t* row_scale, int64_t blocks_per_row, int* error_count,
+                              cudaStream_t stream);
+
+}  // namespace llvq

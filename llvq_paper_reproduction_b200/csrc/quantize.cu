@@ -1,0 +1,683 @@
+// Λ24 nearest-point quantizer for sm_100a: exact, reference-order argmax over
+// (Golay word, shell, class) as in LeechLatticeVectorQuantizer.quantize
+// (impl/leech_lattice_vector_quantizer.py:282-314), fused with the index
+// encoding (encode_codeword, :247-280).
+//
+// Kernel 1 (search): one CTA per 24-D block at a time (persistent grid), 128
+// threads x 32 Golay words each.  Per block it stages |x| in sorted order, the
+// 3 byte tables that permute a Golay word into that order, and the integer
+// image q = rint(|x| * 2^e) with |q| <= 2^19.  Per word it builds the suffix
+// sums of the sorted (sign-flipped) coordinates in registers and scores every
+// class with the generated FFMA chains (one FFMA per distinct leader value).
+// All suffix sums are exact integers in fp32; only the FFMA chain rounds, so
+// every approximate score is within a proven bound E of the exact real score.
+// The argmax is decided exactly: if a single word holds every pair within
+// W = 2E + 4 (q units) of the best approximate score, that word is handed to
+// kernel 2; otherwise the CTA re-scans all words and scores every pair inside
+// the window with the reference's own fp64 arithmetic (CPython 3.12 sum(), a
+// Neumaier-compensated sum) and the reference loop order for ties.
+//
+// Kernel 2 (finalize): one thread per block.  Re-scores the classes of the
+// chosen word with exact integer projections, resolves the window with the
+// fp64 reference score, builds the winning codeword with the reference's
+// sort/tie rules (solve_even_subclass / solve_odd_subclass, :619-666) and
+// ranks it (rank_class_codeword and friends, :692-889).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cfloat>
+#include <climits>
+#include <cmath>
+#include <cstdint>
+
+#include "llvq_device.cuh"
+#include "llvq_internal.h"
+
+__device__ __forceinline__ float llvq_max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+#include "_gen/search_gen.cuh"
+
+namespace llvq {
+
+constexpr int kSearchThreads = 128;
+constexpr int kWordsPerThread = kNumGolay / kSearchThreads;
+constexpr long long kTagWord = 1ll << 40;
+constexpr long long kTagExact = 2ll << 40;
+
+struct RowShared {
+  float x[kDim];
+  float aval[kDim];     // |q| in ascending (|x|, position) order
+  float lval[48];       // 24 + r -> +aval[r], 23 - r -> -aval[r]
+  uint32_t utab[3][256];
+  int8_t apos[kDim];    // position at each sorted rank
+  int8_t arank[kDim];
+  uint32_t negmask;     // x_d < 0
+  uint32_t nposA;       // sorted-rank image of ~negmask
+  int invalid;
+  float scale;          // 2^e
+  float K;              // sqrt(8) * 2^e in fp32
+  float red[kSearchThreads / 32];
+  double xs_best[kSearchThreads];
+  long long xs_order[kSearchThreads];
+};
+
+// ------------------------------------------------------------ row helpers
+
+// Scale exponent: |q| = |rint(x * 2^e)| <= 2^19.  Clamped so sqrt(8)*2^e*shell
+// stays finite in fp32; a clamped (tiny) row only loses precision, which the
+// exact window pass absorbs.
+__device__ __forceinline__ int row_exponent(float maxabs) {
+  if (!(maxabs > 0.f)) return 0;
+  int E;
+  (void)frexpf(maxabs, &E);  // maxabs < 2^E
+  int e = kQBits - E;
+  if (e > 100) e = 100;
+  if (e < -120) e = -120;
+  return e;
+}
+
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+
+// Proven bound (q units) on |approximate score - exact real score| for any
+// pair, for FFMA chains with window constants (l1max, mg, am): half a unit per
+// unit of leader L1 norm from rounding x to q, plus one fp32 rounding per FFMA
+// of a partial sum bounded by m*K + sum |coef| * (suffix length) * 2^Q.
+__device__ __forceinline__ double window_error(double K, float l1max, float mg, float am) {
+  const double u = 1.0 / 16777216.0;  // 2^-24
+  return 0.5 * l1max + u * K * mg + u * (double)(1 << kQBits) * am * (1.0 + 1e-6);
+}
+
+__device__ __forceinline__ double window_width(float K, const DevBook& b) {
+  return 2.0 * window_error((double)K, b.l1max, b.win_mg, b.win_am) + 4.0;
+}
+
+// CPython 3.12 sum() of the float products x_d * y_d (Neumaier-compensated),
+// then LATTICE_SCALE * proj - shell, every operation separately rounded.
+__device__ double reference_score(const float* x, const int* y, int shell) {
+  double f = __dadd_rn(0.0, __dmul_rn((double)x[0], (double)y[0]));
+  double c = 0.0;
+#pragma unroll
+  for (int d = 1; d < kDim; ++d) {
+    const double xi = __dmul_rn((double)x[d], (double)y[d]);
+    const double t = __dadd_rn(f, xi);
+    if (fabs(f) >= fabs(xi)) c = __dadd_rn(c, __dadd_rn(__dsub_rn(f, t), xi));
+    else c = __dadd_rn(c, __dadd_rn(__dsub_rn(xi, t), f));
+    f = t;
+  }
+  if (c != 0.0 && isfinite(c)) f = __dadd_rn(f, c);
+  return __dsub_rn(__dmul_rn(kLatticeScaleD, f), (double)shell);
+}
+
+// The reference's best codeword of class c for Golay word `word`
+// (solve_even_subclass / solve_odd_subclass).  apos: positions in ascending
+// (|x|, position) order.
+__device__ void build_candidate(const float* x, const int8_t* apos, const DevClass& c, uint32_t word, int* y) {
+  if (c.parity == 0) {
+    int t0 = 0, t1 = 0, first1 = -1;
+    for (int r = 0; r < kDim; ++r) {
+      const int p = apos[r];
+      int m;
+      if ((word >> p) & 1u) {
+        m = c.asc1[t1++];
+        if (first1 < 0) first1 = p;
+      } else {
+        m = c.asc0[t0++];
+      }
+      y[p] = x[p] >= 0.f ? m : -m;
+    }
+    if (c.even_weight > 0) {
+      int neg = 0;
+      for (int d = 0; d < kDim; ++d) neg += ((word >> d) & 1u) && y[d] < 0;
+      if ((neg & 1) != c.required) y[first1] = -y[first1];
+    }
+  } else {
+    float xp[kDim];
+    int ord[kDim];
+    for (int d = 0; d < kDim; ++d) {
+      xp[d] = ((word >> d) & 1u) ? -x[d] : x[d];
+      ord[d] = d;
+    }
+    for (int i = 1; i < kDim; ++i) {  // sort by (x', position), stable
+      const int p = ord[i];
+      int j = i - 1;
+      while (j >= 0 && xp[ord[j]] > xp[p]) {
+        ord[j + 1] = ord[j];
+        --j;
+      }
+      ord[j + 1] = p;
+    }
+    for (int r = 0; r < kDim; ++r) {
+      const int p = ord[r];
+      const int v = c.asc0[r];
+      y[p] = ((word >> p) & 1u) ? -v : v;
+    }
+  }
+}
+
+// ------------------------------------------------------- scoring adapters
+
+// Generated specialisations: everything is a compile-time constant.
+template <class S>
+struct Ops {
+  static constexpr int kNumShells = S::kNumShells;
+  static constexpr int kMinShellC = S::kMinShell;
+  static constexpr bool kHasOdd = S::kHasOdd;
+  template <int W>
+  static constexpr bool has_even() {
+    return W == 0 ? S::kHasEven_w0 : W == 8 ? S::kHasEven_w8 : W == 12 ? S::kHasEven_w12
+                                                                        : W == 16 ? S::kHasEven_w16 : S::kHasEven_w24;
+  }
+  template <int W>
+  static constexpr int r0max() {
+    return W == 0 ? S::kR0Max_w0 : W == 8 ? S::kR0Max_w8 : W == 12 ? S::kR0Max_w12
+                                                                   : W == 16 ? S::kR0Max_w16 : S::kR0Max_w24;
+  }
+  __device__ static float odd_max(const DevBook&, const float (&R)[25], const float* nmk) { return S::odd_max(R, nmk); }
+  template <class F>
+  __device__ static void odd_cands(const DevBook&, const float (&R)[25], const float* nmk, float thr, F&& f) {
+    S::odd_cands(R, nmk, thr, f);
+  }
+  template <int W>
+  __device__ static float even_max(const DevBook&, const float (&R0)[25], const float (&R1)[25], float P0, float P1,
+                                   const float* nmk) {
+    if constexpr (W == 0) return S::even_max_w0(R0, R1, P0, P1, nmk);
+    else if constexpr (W == 8) return S::even_max_w8(R0, R1, P0, P1, nmk);
+    else if constexpr (W == 12) return S::even_max_w12(R0, R1, P0, P1, nmk);
+    else if constexpr (W == 16) return S::even_max_w16(R0, R1, P0, P1, nmk);
+    else return S::even_max_w24(R0, R1, P0, P1, nmk);
+  }
+  template <int W, class F>
+  __device__ static void even_cands(const DevBook&, const float (&R0)[25], const float (&R1)[25], float P0, float P1,
+                                    const float* nmk, float thr, F&& f) {
+    if constexpr (W == 0) S::even_cands_w0(R0, R1, P0, P1, nmk, thr, f);
+    else if constexpr (W == 8) S::even_cands_w8(R0, R1, P0, P1, nmk, thr, f);
+    else if constexpr (W == 12) S::even_cands_w12(R0, R1, P0, P1, nmk, thr, f);
+    else if constexpr (W == 16) S::even_cands_w16(R0, R1, P0, P1, nmk, thr, f);
+    else S::even_cands_w24(R0, R1, P0, P1, nmk, thr, f);
+  }
+};
+
+// Table-driven scoring for any codebook (no generated code): the same FFMA
+// chains read from DevClass::term_*.
+struct RuntimeSpec {};
+constexpr int kRuntimeShells = 64;
+
+__device__ __forceinline__ float runtime_chain(const DevClass& c, const float* R, const float* R0, const float* R1,
+                                               float P0, float P1, const float* nmk, int min_shell) {
+  float acc = nmk[c.shell - min_shell];
+  for (int t = 0; t < c.nterms; ++t) {
+    const int kind = c.term_kind[t], idx = c.term_idx[t];
+    const float v = kind == 0 ? R[idx] : kind == 1 ? R0[idx] : kind == 2 ? R1[idx] : kind == 3 ? P0 : P1;
+    acc = fmaf(c.term_coef[t], v, acc);
+  }
+  return acc;
+}
+
+template <>
+struct Ops<RuntimeSpec> {
+  static constexpr int kNumShells = kRuntimeShells;
+  static constexpr int kMinShellC = -1;
+  static constexpr bool kHasOdd = true;
+  template <int W>
+  static constexpr bool has_even() { return true; }
+  template <int W>
+  static constexpr int r0max() { return kDim - W; }
+  __device__ static float odd_max(const DevBook& b, const float (&R)[25], const float* nmk) {
+    float best = -INFINITY;
+    for (int k = 0; k < b.n_classes; ++k) {
+      const DevClass& c = b.cls[k];
+      if (c.parity != 1) continue;
+      best = fmaxf(best, runtime_chain(c, R, nullptr, nullptr, 0.f, 0.f, nmk, b.min_shell));
+    }
+    return best;
+  }
+  template <class F>
+  __device__ static void odd_cands(const DevBook& b, const float (&R)[25], const float* nmk, float thr, F&& f) {
+    for (int k = 0; k < b.n_classes; ++k) {
+      const DevClass& c = b.cls[k];
+      if (c.parity != 1) continue;
+      const float s = runtime_chain(c, R, nullptr, nullptr, 0.f, 0.f, nmk, b.min_shell);
+      if (s >= thr) f(k, s);
+    }
+  }
+  template <int W>
+  __device__ static float even_max(const DevBook& b, const float (&R0)[25], const float (&R1)[25], float P0, float P1,
+                                   const float* nmk) {
+    float best = -INFINITY;
+    for (int k = 0; k < b.n_classes; ++k) {
+      const DevClass& c = b.cls[k];
+      if (c.parity != 0 || c.even_weight != W) continue;
+      best = fmaxf(best, runtime_chain(c, nullptr, R0, R1, P0, P1, nmk, b.min_shell));
+    }
+    return best;
+  }
+  template <int W, class F>
+  __device__ static void even_cands(const DevBook& b, const float (&R0)[25], const float (&R1)[25], float P0, float P1,
+                                    const float* nmk, float thr, F&& f) {
+    for (int k = 0; k < b.n_classes; ++k) {
+      const DevClass& c = b.cls[k];
+      if (c.parity != 0 || c.even_weight != W) continue;
+      const float s = runtime_chain(c, nullptr, R0, R1, P0, P1, nmk, b.min_shell);
+      if (s >= thr) f(k, s);
+    }
+  }
+};
+
+// ------------------------------------------------------------ word scoring
+
+// Odd classes: R[t] = sum of the t largest x'_i.  The selected entries of the
+// 48-slot sorted list (positives at 24 + rank, negatives at 23 - rank) are
+// exactly one per coordinate; the t largest are the top t set bits.
+__device__ __forceinline__ void odd_sums(const RowShared& sh, uint32_t cA, float (&R)[25]) {
+  const uint32_t posA = cA ^ sh.nposA;
+  const uint32_t negA = ~posA & kFull24;
+  uint64_t m = ((uint64_t)posA << 24) | (uint64_t)(__brev(negA) >> 8);
+  R[0] = 0.f;
+#pragma unroll
+  for (int t = 1; t <= kDim; ++t) {
+    const int j = 63 - __clzll((long long)m);
+    R[t] = R[t - 1] + sh.lval[j];
+    m ^= 1ull << j;
+  }
+}
+
+// Even classes of word weight W: suffix sums of |q| inside (R1) and outside
+// (R0) the word, and the sign-parity penalties.
+template <int W, int N0>
+__device__ __forceinline__ void even_sums(const RowShared& sh, uint32_t c, uint32_t cA, float (&R0)[25],
+                                          float (&R1)[25], float& P0, float& P1) {
+  uint32_t f1 = cA, f0 = ~cA & kFull24;
+  R1[0] = 0.f;
+#pragma unroll
+  for (int t = 1; t <= W; ++t) {
+    const int j = 31 - __clz(f1);
+    R1[t] = R1[t - 1] + sh.aval[j];
+    f1 ^= 1u << j;
+  }
+  R0[0] = 0.f;
+#pragma unroll
+  for (int t = 1; t <= N0; ++t) {
+    const int j = 31 - __clz(f0);
+    R0[t] = R0[t - 1] + sh.aval[j];
+    f0 ^= 1u << j;
+  }
+  const float qmin1 = W ? sh.aval[__ffs(cA) - 1] : 0.f;
+  const int negpar = __popc(c & sh.negmask) & 1;
+  P0 = negpar ? qmin1 : 0.f;  // penalty for classes that need an even count of negatives
+  P1 = negpar ? 0.f : qmin1;  // ... and for those that need an odd count
+}
+
+template <class S, int W>
+__device__ __forceinline__ float even_max_word(const DevBook& b, const RowShared& sh, uint32_t c, uint32_t cA,
+                                               const float* nmk) {
+  if constexpr (!Ops<S>::template has_even<W>()) {
+    return -INFINITY;
+  } else {
+    float R0[25], R1[25], P0, P1;
+    even_sums<W, Ops<S>::template r0max<W>()>(sh, c, cA, R0, R1, P0, P1);
+    return Ops<S>::template even_max<W>(b, R0, R1, P0, P1, nmk);
+  }
+}
+
+template <class S, int W, class F>
+__device__ __forceinline__ void even_cands_word(const DevBook& b, const RowShared& sh, uint32_t c, uint32_t cA,
+                                                const float* nmk, float thr, F&& f) {
+  if constexpr (Ops<S>::template has_even<W>()) {
+    float R0[25], R1[25], P0, P1;
+    even_sums<W, Ops<S>::template r0max<W>()>(sh, c, cA, R0, R1, P0, P1);
+    Ops<S>::template even_cands<W>(b, R0, R1, P0, P1, nmk, thr, f);
+  }
+}
+
+__device__ __forceinline__ uint32_t permute_word(const RowShared& sh, uint32_t c) {
+  return sh.utab[0][c & 255u] | sh.utab[1][(c >> 8) & 255u] | sh.utab[2][c >> 16];
+}
+
+template <class S>
+__device__ __forceinline__ float word_max(const DevBook& b, const RowShared& sh, uint32_t c, const float* nmk) {
+  const uint32_t cA = permute_word(sh, c);
+  float best = -INFINITY;
+  if constexpr (Ops<S>::kHasOdd) {
+    float R[25];
+    odd_sums(sh, cA, R);
+    best = Ops<S>::odd_max(b, R, nmk);
+  }
+  switch (__popc(c)) {
+    case 8: best = fmaxf(best, even_max_word<S, 8>(b, sh, c, cA, nmk)); break;
+    case 12: best = fmaxf(best, even_max_word<S, 12>(b, sh, c, cA, nmk)); break;
+    case 16: best = fmaxf(best, even_max_word<S, 16>(b, sh, c, cA, nmk)); break;
+    case 0: best = fmaxf(best, even_max_word<S, 0>(b, sh, c, cA, nmk)); break;
+    default: best = fmaxf(best, even_max_word<S, 24>(b, sh, c, cA, nmk)); break;
+  }
+  return best;
+}
+
+template <class S, class F>
+__device__ __forceinline__ void word_cands(const DevBook& b, const RowShared& sh, uint32_t c, const float* nmk,
+                                           float thr, F&& f) {
+  const uint32_t cA = permute_word(sh, c);
+  if constexpr (Ops<S>::kHasOdd) {
+    float R[25];
+    odd_sums(sh, cA, R);
+    Ops<S>::odd_cands(b, R, nmk, thr, f);
+  }
+  switch (__popc(c)) {
+    case 8: even_cands_word<S, 8>(b, sh, c, cA, nmk, thr, f); break;
+    case 12: even_cands_word<S, 12>(b, sh, c, cA, nmk, thr, f); break;
+    case 16: even_cands_word<S, 16>(b, sh, c, cA, nmk, thr, f); break;
+    case 0: even_cands_word<S, 0>(b, sh, c, cA, nmk, thr, f); break;
+    default: even_cands_word<S, 24>(b, sh, c, cA, nmk, thr, f); break;
+  }
+}
+
+// ------------------------------------------------------------- the search
+
+// Exact-pass handler for one candidate pair: the reference's codeword and fp64
+// score, kept if it beats (score desc, loop order asc).  Not inlined: the
+// generated scoring code calls it from every class site.
+__device__ __noinline__ void consider_exact(const RowShared& sh, const DevBook& book, uint32_t word, int lex, int k,
+                                            double* best, long long* order) {
+  int y[kDim];
+  const DevClass& cls = book.cls[k];
+  build_candidate(sh.x, sh.apos, cls, word, y);
+  const double s = reference_score(sh.x, y, cls.shell);
+  const long long o = (long long)lex * book.n_classes + k;
+  if (s > *best || (s == *best && o < *order)) {
+    *best = s;
+    *order = o;
+  }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Stage one block: x, validity, scale, sorted |x| order and the word tables.
+__device__ void stage_row(const float* __restrict__ x, int64_t row, RowShared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (tid < 32) {
+    const float v = lane < kDim ? x[row * kDim + lane] : 0.f;
+    if (lane < kDim) sh.x[lane] = v;
+    const unsigned bad = __ballot_sync(0xffffffffu, lane < kDim && !isfinite(v));
+    const unsigned neg = __ballot_sync(0xffffffffu, lane < kDim && v < 0.f);
+    const float mx = warp_max(fabsf(v));
+    if (lane == 0) {
+      sh.invalid = bad != 0;
+      sh.negmask = neg & kFull24;
+      sh.scale = pow2f(row_exponent(mx));
+      sh.K = kSqrt8F * sh.scale;
+    }
+  }
+  __syncthreads();
+  if (tid < kDim && !sh.invalid) {
+    const float ai = fabsf(sh.x[tid]);
+    int r = 0;
+#pragma unroll
+    for (int j = 0; j < kDim; ++j) {
+      const float aj = fabsf(sh.x[j]);
+      r += (aj < ai) || (aj == ai && j < tid);
+    }
+    const float q = rintf(ai * sh.scale);
+    sh.arank[tid] = (int8_t)r;
+    sh.apos[r] = (int8_t)tid;
+    sh.aval[r] = q;
+    sh.lval[24 + r] = q;
+    sh.lval[23 - r] = -q;
+  }
+  __syncthreads();
+  if (!sh.invalid) {
+    for (int i = tid; i < 3 * 256; i += blockDim.x) {
+      const int t = i >> 8, v = i & 255;
+      uint32_t u = 0;
+#pragma unroll
+      for (int bit = 0; bit < 8; ++bit)
+        if ((v >> bit) & 1) u |= 1u << sh.arank[8 * t + bit];
+      sh.utab[t][v] = u;
+    }
+    if (tid == 0) {
+      const uint32_t pos = ~sh.negmask & kFull24;
+      uint32_t u = 0;
+      for (int d = 0; d < kDim; ++d)
+        if ((pos >> d) & 1u) u |= 1u << sh.arank[d];
+      sh.nposA = u;
+    }
+  }
+  __syncthreads();
+}
+
+template <class S>
+__global__ void __launch_bounds__(kSearchThreads) search_kernel(const float* __restrict__ x, int64_t n, DevBook book,
+                                                                long long* tag_out, float* m_out) {
+  __shared__ RowShared sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NS = Ops<S>::kNumShells;
+  const int min_shell = Ops<S>::kMinShellC >= 0 ? Ops<S>::kMinShellC : book.min_shell;
+  for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+    stage_row(x, row, sh);
+    if (sh.invalid) {
+      if (tid == 0) {
+        tag_out[row] = -1;
+        m_out[row] = NAN;
+      }
+      __syncthreads();
+      continue;
+    }
+    float nmk[NS];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) nmk[s] = -(float)(min_shell + s) * sh.K;
+
+    float b1 = -INFINITY, b2 = -INFINITY;
+    int w1 = -1;
+    for (int i = 0; i < kWordsPerThread; ++i) {
+      const int j = i * kSearchThreads + tid;
+      const uint32_t c = __ldg(book.wlist_word + j);
+      const float bw = word_max<S>(book, sh, c, nmk);
+      if (bw > b1) {
+        b2 = b1;
+        b1 = bw;
+        w1 = j;
+      } else {
+        b2 = fmaxf(b2, bw);
+      }
+    }
+    const float wm = warp_max(b1);
+    if (lane == 0) sh.red[warp] = wm;
+    __syncthreads();
+    float M = sh.red[0];
+#pragma unroll
+    for (int w = 1; w < kSearchThreads / 32; ++w) M = fmaxf(M, sh.red[w]);
+    const float thr = __double2float_rd((double)M - window_width(sh.K, book));
+    const int contenders = __syncthreads_count(b1 >= thr);
+    const int second = __syncthreads_or(b2 >= thr);
+    if (contenders == 1 && !second) {
+      if (b1 >= thr) {
+        tag_out[row] = kTagWord | (long long)__ldg(book.wlist_lex + w1);
+        m_out[row] = M;
+      }
+    } else {
+      // Exact pass: every pair inside the window, scored with the reference
+      // arithmetic; ties go to the earliest (Golay word, class) in loop order.
+      double best = -INFINITY;
+      long long order = LLONG_MAX;
+      for (int i = 0; i < kWordsPerThread; ++i) {
+        const int j = i * kSearchThreads + tid;
+        const uint32_t c = __ldg(book.wlist_word + j);
+        const int lex = __ldg(book.wlist_lex + j);
+        word_cands<S>(book, sh, c, nmk, thr,
+                      [&](int k, float) { consider_exact(sh, book, c, lex, k, &best, &order); });
+      }
+      sh.xs_best[tid] = best;
+      sh.xs_order[tid] = order;
+      __syncthreads();
+      if (tid == 0) {
+        for (int t = 1; t < kSearchThreads; ++t) {
+          if (sh.xs_best[t] > best || (sh.xs_best[t] == best && sh.xs_order[t] < order)) {
+            best = sh.xs_best[t];
+            order = sh.xs_order[t];
+          }
+        }
+        const long long lex = order / book.n_classes, k = order % book.n_classes;
+        tag_out[row] = kTagExact | (k << 12) | lex;
+        m_out[row] = (float)best;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------- finalize
+
+__global__ void finalize_kernel(const float* __restrict__ x, int64_t n, DevBook book, const long long* tag_in,
+                                const float* m_in, long long* index_out, long long* pair_out, float* score_out) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= n) return;
+  const long long tag = tag_in[row];
+  if (tag < 0) {
+    index_out[row] = -1;
+    pair_out[row] = -1;
+    score_out[row] = NAN;
+    return;
+  }
+  float xv[kDim];
+  float mx = 0.f;
+  uint32_t neg = 0;
+#pragma unroll
+  for (int d = 0; d < kDim; ++d) {
+    xv[d] = x[row * kDim + d];
+    mx = fmaxf(mx, fabsf(xv[d]));
+    neg |= (uint32_t)(xv[d] < 0.f) << d;
+  }
+  // ascending (|x|, position) order
+  int8_t apos[kDim];
+  for (int d = 0; d < kDim; ++d) apos[d] = (int8_t)d;
+  for (int i = 1; i < kDim; ++i) {
+    const int p = apos[i];
+    const float a = fabsf(xv[p]);
+    int j = i - 1;
+    while (j >= 0 && fabsf(xv[apos[j]]) > a) {
+      apos[j + 1] = apos[j];
+      --j;
+    }
+    apos[j + 1] = (int8_t)p;
+  }
+  const int lex = (int)(tag & 4095);
+  const uint32_t word = book.golay[lex];
+  int best_k = -1;
+  double best = -INFINITY;
+  int y[kDim];
+  if (tag & kTagExact) {
+    best_k = (int)((tag >> 12) & ((1ll << 28) - 1));
+  } else {
+    const float scale = pow2f(row_exponent(mx));
+    const float K = kSqrt8F * scale;
+    const double thr = (double)m_in[row] - window_width(K, book);
+    // exact integer images of the sorted sequences for this word
+    int xs[kDim], f0q[kDim], f1q[kDim];
+    int nxs = 0, n0 = 0, n1 = 0;
+    for (int r = kDim - 1; r >= 0; --r) {  // positives, largest first
+      const int p = apos[r];
+      const int q = (int)rintf(fabsf(xv[p]) * scale);
+      if (((neg >> p) & 1u) == ((word >> p) & 1u)) xs[nxs++] = q;
+      if ((word >> p) & 1u) f1q[n1++] = q; else f0q[n0++] = q;
+    }
+    for (int r = 0; r < kDim; ++r) {  // negatives, least negative first
+      const int p = apos[r];
+      if (((neg >> p) & 1u) != ((word >> p) & 1u)) xs[nxs++] = -(int)rintf(fabsf(xv[p]) * scale);
+    }
+    const int wt = __popc(word);
+    const int negpar = __popc(word & neg) & 1;
+    for (int k = 0; k < book.n_classes; ++k) {
+      const DevClass& c = book.cls[k];
+      long long proj = 0;
+      if (c.parity == 1) {
+        for (int t = 0; t < kDim; ++t) proj += (long long)c.asc0[kDim - 1 - t] * xs[t];
+      } else {
+        if (c.even_weight != wt) continue;
+        for (int t = 0; t < n0; ++t) proj += (long long)c.asc0[n0 - 1 - t] * f0q[t];
+        for (int t = 0; t < n1; ++t) proj += (long long)c.asc1[n1 - 1 - t] * f1q[t];
+        if (wt && negpar != c.required) proj -= 2ll * c.asc1[0] * f1q[n1 - 1];
+      }
+      const double approx = (double)proj - (double)c.shell * (double)K;
+      if (approx < thr) continue;
+      build_candidate(xv, apos, c, word, y);
+      const double s = reference_score(xv, y, c.shell);
+      if (s > best) {  // classes are visited in loop order: strict '>' keeps the first
+        best = s;
+        best_k = k;
+      }
+    }
+  }
+  if (best_k < 0) {  // cannot happen for a finite row; report it as invalid
+    index_out[row] = -1;
+    pair_out[row] = -1;
+    score_out[row] = NAN;
+    return;
+  }
+  const DevClass& c = book.cls[best_k];
+  build_candidate(xv, apos, c, word, y);
+  best = reference_score(xv, y, c.shell);
+  const int choice = c.parity ? lex : (int)book.golay_wrank[lex];
+  index_out[row] = rank_codeword(c, y, word, choice);
+  pair_out[row] = (long long)best_k * kNumGolay + lex;
+  score_out[row] = (float)best;
+}
+
+// ------------------------------------------------------------- launchers
+
+template <class S>
+static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book, long long* tag, float* m,
+                                 cudaStream_t stream) {
+  static int blocks_per_sm = 0, sms = 0;
+  if (!blocks_per_sm) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, search_kernel<S>, kSearchThreads, 0);
+    if (blocks_per_sm < 1) blocks_per_sm = 1;
+  }
+  const int64_t grid = std::min<int64_t>(n, (int64_t)sms * blocks_per_sm);
+  search_kernel<S><<<(unsigned)grid, kSearchThreads, 0, stream>>>(x, n, book, tag, m);
+  return cudaGetLastError();
+}
+
+#define LLVQ_SPEC_ENTRY(NAME)                                                                     \
+  {gen::kSig_##NAME, &launch_search<gen::Spec_##NAME>, #NAME, (float)gen::Spec_##NAME::kL1Max, \
+   (float)gen::Spec_##NAME::kWinMG, (float)gen::Spec_##NAME::kWinAM},
+static const SpecEntry kSpecs[] = {LLVQ_FOR_EACH_SPEC(LLVQ_SPEC_ENTRY)};
+
+const SpecEntry* spec_table(int* count) {
+  *count = (int)(sizeof(kSpecs) / sizeof(kSpecs[0]));
+  return kSpecs;
+}
+
+cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long long* index, long long* pair,
+                            float* score, cudaStream_t stream, bool force_runtime) {
+  if (n <= 0) return cudaSuccess;
+  DevBook book = cb.dev;
+  SearchLauncher launch;
+  if (cb.spec && !force_runtime) {
+    launch = cb.spec->launch;
+    book.l1max = cb.spec->l1max;
+    book.win_mg = cb.spec->win_mg;
+    book.win_am = cb.spec->win_am;
+  } else {
+    launch = &launch_search<RuntimeSpec>;
+    book.l1max = cb.rt_l1max;
+    book.win_mg = cb.rt_mg;
+    book.win_am = cb.rt_am;
+  }
+  cudaError_t err = launch(x, n, book, pair, score, stream);
+  if (err != cudaSuccess) return err;
+  const int threads = 128;
+  const int64_t blocks = (n + threads - 1) / threads;
+  finalize_kernel<<<(unsigned)blocks, threads, 0, stream>>>(x, n, book, pair, score, index, pair, score);
+  return cudaGetLastError();
+}
+
+}  // namespace llvq

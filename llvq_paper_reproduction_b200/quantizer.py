@@ -1,0 +1,264 @@
+"""Drop-in replacement of LeechLatticeVectorQuantizerGpu
+(impl/leech_lattice_vector_quantizer_gpu.py:145-567 of
+dmnunez1993/llvq-paper-reproduction).
+
+Same constructor, attributes and methods; tensor quantize/dequantize run the
+sm_100a kernels of the in-tree CUDA library on torch's current stream.  There
+is no CPU fallback: tensor paths on a non-CUDA device raise ValueError, as the
+reference does.  Scalar host paths (codeword, unrank, encode_codeword) run the
+library's host code.
+"""
+from __future__ import annotations
+
+from bisect import bisect_right
+from math import ceil, log2
+from pathlib import Path
+from typing import Sequence
+
+import torch
+
+from . import _native
+from .tables import (DIM, LATTICE_SCALE, ClassLeader, ClassLocalStructure, LocalDecomposition, RankedCodeword,
+                     build_local_structure, extended_golay_codewords, generate_class_leaders, leech_shell_counts)
+
+
+class LeechLatticeVectorQuantizerGpu:
+    """Implicit shell -> class -> local-symmetry database for Leech codewords,
+    with the quantizer and dequantizer on the GPU."""
+
+    def __init__(self, max_shell: int = 4, leaders: Sequence[ClassLeader] | None = None,
+                 cache_dir: str | Path | None = ".llvq_cache", use_cache: bool = True, verbose: bool = False,
+                 device: str | torch.device | None = None, dtype: torch.dtype = torch.float32,
+                 min_shell: int = 2):
+        if max_shell < 2:
+            raise ValueError("max_shell must be at least 2")
+        if min_shell < 2 or min_shell > max_shell:
+            raise ValueError("min_shell must be in 2..max_shell")
+        self.device = torch.device(device or ("cuda" if torch.cuda.is_available() else "cpu"))
+        self.dtype = dtype
+        if leaders is None:
+            leaders = generate_class_leaders(max_shell, cache_dir=cache_dir, use_cache=use_cache, verbose=verbose,
+                                             min_shell=min_shell)
+        shells = {row.shell for row in leaders}
+        missing = [m for m in range(min_shell, max_shell + 1) if m not in shells]
+        if missing:
+            raise ValueError(f"no class leaders are available for shells: {missing}")
+        self.min_shell = min_shell
+        self.max_shell = max_shell
+        self.golay_codewords = extended_golay_codewords()
+        self.golay_index_by_codeword = {c: i for i, c in enumerate(self.golay_codewords)}
+        key = lambda r: (r.leader, 0 if r.parity == "even" else 1, r.count)  # noqa: E731
+        self.classes_by_shell = {
+            s: tuple(sorted((r for r in leaders if r.shell == s), key=key)) for s in range(min_shell, max_shell + 1)
+        }
+        self.shell_offsets = {}
+        self.class_offsets = {}
+        cursor = 0
+        for s, rows in self.classes_by_shell.items():
+            self.shell_offsets[s] = cursor
+            offs, c = [], 0
+            for r in rows:
+                offs.append(c)
+                c += r.count
+            self.class_offsets[s] = tuple(offs)
+            cursor += c
+        self.local_structures = {
+            s: tuple(build_local_structure(s, i, r, self.golay_codewords) for i, r in enumerate(rows))
+            for s, rows in self.classes_by_shell.items()
+        }
+        self.class_index_by_shell_and_key = {
+            s: {(r.leader, r.parity): i for i, r in enumerate(rows)} for s, rows in self.classes_by_shell.items()
+        }
+        self.shell_counts = {s: sum(r.count for r in rows) for s, rows in self.classes_by_shell.items()}
+        self.cumulative_shell_counts = {s: self.shell_offsets[s] + self.shell_counts[s] for s in self.classes_by_shell}
+        self.total_count = self.cumulative_shell_counts[max_shell]
+        self.shape_bits = ceil(log2(self.total_count)) if self.total_count > 1 else 1
+        self._validate()
+        flat = [st for s in self.classes_by_shell for st in self.local_structures[s]]
+        self._class_shell = [st.shell for st in flat]
+        self._class_parity = [0 if st.leader.parity == "even" else 1 for st in flat]
+        self._class_leader = [st.leader.leader for st in flat]
+        self._host_book = None
+        self._device_book = None
+
+    # ------------------------------------------------------------ native books
+    def _host(self) -> _native.NativeCodebook:
+        if self._host_book is None:
+            self._host_book = _native.codebook_for(self._class_shell, self._class_parity, self._class_leader, -1)
+        return self._host_book
+
+    def _book(self) -> _native.NativeCodebook:
+        if self._device_book is None:
+            index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+            self._device_book = _native.codebook_for(self._class_shell, self._class_parity, self._class_leader,
+                                                     index)
+            if self._device_book.total_count != self.total_count:
+                raise RuntimeError("native codebook disagrees with the host tables")
+        return self._device_book
+
+    @property
+    def specialized(self) -> bool:
+        """True when generated search code exists for this class list."""
+        return self._host().specialized
+
+    # ------------------------------------------------------------ host API
+    def rank_class(self, shell: int, class_index: int, class_local_index: int = 0) -> int:
+        classes = self.classes_by_shell[shell]
+        if class_index < 0 or class_index >= len(classes):
+            raise IndexError(class_index)
+        if class_local_index < 0 or class_local_index >= classes[class_index].count:
+            raise IndexError(class_local_index)
+        return self.shell_offsets[shell] + self.class_offsets[shell][class_index] + class_local_index
+
+    def shell_for_index(self, global_index: int) -> int:
+        ends = [self.cumulative_shell_counts[s] for s in self.classes_by_shell]
+        return self.min_shell + bisect_right(ends, global_index)
+
+    def unrank(self, global_index: int) -> RankedCodeword:
+        if global_index < 0 or global_index >= self.total_count:
+            raise IndexError(global_index)
+        shell = self.shell_for_index(global_index)
+        local = global_index - self.shell_offsets[shell]
+        offs = self.class_offsets[shell]
+        ci = bisect_right(offs, local) - 1
+        return RankedCodeword(global_index, shell, local, ci, local - offs[ci], offs[ci],
+                              self.classes_by_shell[shell][ci])
+
+    def decompose_local_index(self, ranked: RankedCodeword) -> LocalDecomposition:
+        st = self.local_structures[ranked.shell][ranked.class_index]
+        cur = ranked.class_local_index
+        perm = cur % st.permutation_count
+        cur //= st.permutation_count
+        sign = cur % st.sign_count
+        golay = cur // st.sign_count
+        return LocalDecomposition(golay, self.golay_codewords[st.golay_codeword_indices[golay]], sign, perm)
+
+    def codeword(self, global_index: int) -> tuple[int, ...]:
+        if global_index < 0 or global_index >= self.total_count:
+            raise IndexError(global_index)
+        return self._host().codeword(int(global_index))
+
+    def encode_codeword(self, vector: Sequence[int]) -> int:
+        """Exact index of a codeword of this database (CPU module :247-280)."""
+        values = tuple(int(v) for v in vector)
+        if len(values) != DIM:
+            raise ValueError(f"expected {DIM} coordinates, got {len(values)}")
+        return self._host().encode(values)
+
+    # ------------------------------------------------------------ dequantize
+    def dequantize_lattice(self, global_index):
+        """Integer Leech representative(s) before the 1/sqrt(8) scale."""
+        if not torch.is_tensor(global_index) and isinstance(global_index, int):
+            return self.codeword(global_index)
+        indices = torch.as_tensor(global_index, dtype=torch.long, device=self.device)
+        shape = indices.shape
+        return self._dequantize_lattice_cuda(indices.reshape(-1)).reshape(*shape, DIM)
+
+    dequantize_lattice_cuda = dequantize_lattice
+
+    def dequantize(self, global_index):
+        """Scaled Leech lattice vector(s): fp32(1/sqrt 8) * k in the API dtype."""
+        if not torch.is_tensor(global_index) and isinstance(global_index, int):
+            return tuple(LATTICE_SCALE * v for v in self.codeword(global_index))
+        indices = torch.as_tensor(global_index, dtype=torch.long, device=self.device)
+        shape = indices.shape
+        flat = indices.reshape(-1).contiguous()
+        if self.dtype != torch.float32:
+            return LATTICE_SCALE * self._dequantize_lattice_cuda(flat).reshape(*shape, DIM).to(self.dtype)
+        self._require_cuda("dequantize")
+        out = torch.empty((flat.shape[0], DIM), dtype=torch.float32, device=self.device)
+        err = self._error_counter()
+        with torch.cuda.device(self.device):
+            self._book().dequantize(flat.data_ptr(), flat.shape[0], out.data_ptr(), _native.OUT_F32, err.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream)
+        self._raise_if_bad(err)
+        return out.reshape(*shape, DIM)
+
+    def dequantize_bf16(self, indices: torch.Tensor, row_scale: torch.Tensor) -> torch.Tensor:
+        """bf16 weights: bf16(dequantize(indices) * row_scale[row]) for indices
+        [rows, blocks_per_row] and fp16 row_scale [rows] (no reference
+        counterpart)."""
+        self._require_cuda("dequantize_bf16")
+        if indices.dim() != 2 or row_scale.shape != (indices.shape[0],) or row_scale.dtype != torch.float16:
+            raise ValueError("expected indices [rows, blocks] and fp16 row_scale [rows]")
+        idx = indices.to(device=self.device, dtype=torch.long).contiguous()
+        sc = row_scale.to(self.device).contiguous()
+        out = torch.empty((idx.shape[0], idx.shape[1] * DIM), dtype=torch.bfloat16, device=self.device)
+        err = self._error_counter()
+        with torch.cuda.device(self.device):
+            self._book().dequantize_bf16(idx.data_ptr(), idx.numel(), sc.data_ptr(), idx.shape[1], out.data_ptr(),
+                                         err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        self._raise_if_bad(err)
+        return out
+
+    def _dequantize_lattice_cuda(self, indices: torch.Tensor) -> torch.Tensor:
+        self._require_cuda("dequantize_lattice_cuda")
+        flat = indices.contiguous()
+        out = torch.empty((flat.shape[0], DIM), dtype=torch.long, device=self.device)
+        err = self._error_counter()
+        with torch.cuda.device(self.device):
+            self._book().dequantize_lattice(flat.data_ptr(), flat.shape[0], out.data_ptr(), err.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream)
+        self._raise_if_bad(err)
+        return out
+
+    def _error_counter(self) -> torch.Tensor:
+        return torch.zeros((1,), dtype=torch.int32, device=self.device)
+
+    @staticmethod
+    def _raise_if_bad(err: torch.Tensor) -> None:
+        # Same host sync and exception as the reference's range check (_gpu.py:418-419).
+        if int(err.item()):
+            raise IndexError("global index outside codebook range")
+
+    def _require_cuda(self, what: str) -> None:
+        if self.device.type != "cuda":
+            raise ValueError(f"{what} requires a CUDA device")
+
+    # ------------------------------------------------------------ quantize
+    def quantize(self, vector):
+        """Quantize real-valued 24-D vector(s) on the GPU (tensor in, int64
+        tensor out; a sequence input returns an int)."""
+        return self.quantize_cuda(vector)
+
+    def quantize_cuda(self, vector, return_details: bool = False, table_driven: bool = False):
+        self._require_cuda("quantize_cuda")
+        tensor_input = torch.is_tensor(vector)
+        x = torch.as_tensor(vector, dtype=self.dtype, device=self.device)
+        if x.shape[-1] != DIM:
+            raise ValueError(f"expected last dimension {DIM}, got {x.shape[-1]}")
+        single = x.ndim == 1
+        shape = x.shape[:-1]
+        xs = x.reshape(-1, DIM).to(torch.float32).contiguous()
+        n = xs.shape[0]
+        indices = torch.empty((n,), dtype=torch.long, device=self.device)
+        best_pair = torch.empty((n,), dtype=torch.long, device=self.device)
+        best_score = torch.empty((n,), dtype=torch.float32, device=self.device)
+        with torch.cuda.device(self.device):
+            self._book().quantize(xs.data_ptr(), n, indices.data_ptr(), best_pair.data_ptr(), best_score.data_ptr(),
+                                  torch.cuda.current_stream().cuda_stream,
+                                  _native.FLAG_TABLE_DRIVEN if table_driven else 0)
+        indices = indices.reshape(shape)
+        if single:
+            indices = indices.reshape(())
+        if return_details:
+            return indices, best_pair.reshape(shape), best_score.reshape(shape)
+        if not tensor_input:
+            return int(indices.item())
+        return indices
+
+    # ------------------------------------------------------------ checks
+    def _validate(self) -> None:
+        theta = leech_shell_counts(self.max_shell)
+        for shell, rows in self.classes_by_shell.items():
+            if sum(r.count for r in rows) != theta[shell]:
+                raise ValueError(f"shell {shell} leaders sum to {sum(r.count for r in rows)}, "
+                                 f"theta series gives {theta[shell]}")
+            for st in self.local_structures[shell]:
+                if st.count != st.leader.count:
+                    raise ValueError(f"shell {shell}, class {st.class_index} has local count {st.count}, "
+                                     f"leader count {st.leader.count}")
+
+
+__all__ = ["LeechLatticeVectorQuantizerGpu", "ClassLeader", "ClassLocalStructure", "LocalDecomposition",
+           "RankedCodeword", "LATTICE_SCALE", "DIM"]
