@@ -1,0 +1,384 @@
+"""Benchmark of the B200 Λ24 quantizer (one JSON line on rank 0).
+
+Primary metric: Λ24 blocks quantized per second on the Gaussian rate-sweep
+workload at 2 bits/dim -- N(0,1) fp32 blocks [16,777,216, 24], seed 1 (+rank),
+codebook shells 2..13 (48-bit index, the reference's quantize semantics,
+bit-exact).  One step = one quantize pass over the whole batch.  Inputs
+(1.6 GB) are larger than L2 (126 MB), so no flush is needed between steps.
+  value  -- device-resident inputs and outputs, timed with CUDA events on the
+            launching stream, barrier + synchronize on both sides, max over ranks.
+  e2e    -- the public API (LeechLatticeVectorQuantizerGpu.quantize) fed from
+            pinned host memory, host->device copy of the blocks and
+            device->host copy of the int64 indices inside the timed region.
+Secondary (rank 0, N=1): dequantizer GB/s on all Llama-3-8B linear shapes
+(291,307,520 random valid indices, seed 3, bf16 weights with fp16 per-row
+scales).
+
+--impl reference times the reference algorithm on the host cores instead:
+the oracle's restatement of LeechLatticeVectorQuantizer.quantize (per-pair
+sorting exactly as the reference), all threads, a bounded sample per step.
+Multi-GPU: `torchrun --nproc-per-node N bench.py --gpus N`; every rank
+quantizes its own batch (weak scaling, no data-path collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Λ₂₄ blocks/sec quantized, dequant GB/s, fused-GEMM TFLOP/s at 1/2/4/8 B200 vs host CPU"
+SMS = 148
+FP32_LANES = 128
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def algorithmic_ops_per_block(min_shell: int, max_shell: int) -> float:
+    """2 ops per distinct nonzero leader magnitude per evaluated (Golay word,
+    class) pair, plus a 24-add prefix sum for each of the 4096 odd and 4096
+    even orderings.  Sorting is not counted."""
+    from llvq_paper_reproduction_b200.tables import codebook_classes
+
+    weights = {0: 1, 8: 759, 12: 2576, 16: 759, 24: 1}
+    ops = 2 * 4096 * 24
+    for c in codebook_classes(max_shell, min_shell=min_shell):
+        distinct = len({v for v in c.leader if v})
+        pairs = 4096 if c.parity else weights[sum(1 for v in c.leader if v % 4 == 2)]
+        ops += 2 * distinct * pairs
+    return float(ops)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.file is None:
+            return {}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {}
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": rows[0][1], "reasons": reasons,
+                "samples": len(rows)}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+
+
+# ----------------------------------------------------------------- CPU side
+
+def cpu_reference_rate(x: np.ndarray, max_shell: int, mode: int = 0) -> tuple[float, int]:
+    """Blocks/s of the oracle restatement of the reference CPU quantizer on
+    the rows of x, all host threads."""
+    from oracle.oracle import OracleBook
+
+    threads = os.cpu_count() or 1
+    ob = OracleBook(max_shell)
+    t0 = time.perf_counter()
+    ob.quantize_batch(x, mode=mode, threads=threads)
+    return x.shape[0] / (time.perf_counter() - t0), threads
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    sample = args.cpu_sample
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn((sample * (args.steps + args.warmup), 24), generator=g, dtype=torch.float32).numpy()
+    rates = []
+    threads = 1
+    for s in range(args.warmup + args.steps):
+        r, threads = cpu_reference_rate(x[s * sample:(s + 1) * sample], args.max_shell)
+        if s >= args.warmup:
+            rates.append(r)
+    value = float(np.mean(rates))
+    desc = (f"{sample} N(0,1) blocks per step from the [16777216, 24] seed-1 workload, shells 2..{args.max_shell}; "
+            "oracle restatement of LeechLatticeVectorQuantizer.quantize with per-pair sorts (mode 0)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "blocks/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sample / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"gaussian N(0,1) fp32 [16777216, 24] seed 1, shells 2..{args.max_shell} "
+                               "(48-bit index), CPU sample", "sample_blocks_per_step": sample},
+        "cpu_baseline": {"value": value, "unit": "blocks/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "blocks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU side
+
+def llama3_dequant_workload(q, device, seed: int = 3):
+    """Random valid indices of every Llama-3-8B linear (uniform shell, class
+    within shell, local index) and fp16 per-row scales, grouped by blocks per
+    row: in-dim 4096 -> 171 blocks (4104), in-dim 14336 -> 598 blocks (14352)."""
+    import torch
+
+    layers = 32
+    groups = {171: layers * (4096 + 1024 + 1024 + 4096 + 14336 + 14336), 598: layers * 4096}
+    g = torch.Generator(device=device).manual_seed(seed)
+    flat = [st for s in q.classes_by_shell for st in q.local_structures[s]]
+    starts, counts = [], []
+    for s in q.classes_by_shell:
+        for i, st in enumerate(q.local_structures[s]):
+            starts.append(q.shell_offsets[s] + q.class_offsets[s][i])
+            counts.append(st.count)
+    shells = sorted(q.classes_by_shell)
+    first = []
+    k = 0
+    for s in shells:
+        first.append(k)
+        k += len(q.classes_by_shell[s])
+    ncls = torch.tensor([len(q.classes_by_shell[s]) for s in shells], device=device)
+    first = torch.tensor(first, device=device)
+    starts = torch.tensor(starts, dtype=torch.long, device=device)
+    counts = torch.tensor(counts, dtype=torch.float64, device=device)
+    out = {}
+    for bpr, rows in groups.items():
+        n = rows * bpr
+        sh = torch.randint(0, len(shells), (n,), generator=g, device=device)
+        cls = first[sh] + (torch.rand(n, generator=g, device=device, dtype=torch.float64) * ncls[sh]).long()
+        del sh
+        local = (torch.rand(n, generator=g, device=device, dtype=torch.float64) * counts[cls]).long()
+        idx = (starts[cls] + local).reshape(rows, bpr)
+        del cls, local
+        scale = (torch.rand(rows, generator=g, device=device) * 0.04 + 0.005).to(torch.float16)
+        out[bpr] = (idx, scale)
+    assert len(flat) == len(starts)
+    return out
+
+
+def run_gpu_arm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    from llvq_paper_reproduction_b200 import LeechLatticeVectorQuantizerGpu
+
+    q = LeechLatticeVectorQuantizerGpu(max_shell=args.max_shell, use_cache=False, device=device)
+    book = q._book()
+    n = args.rows
+    g = torch.Generator(device=device).manual_seed(1 + rank)
+    x = torch.randn((n, 24), generator=g, device=device, dtype=torch.float32)
+    idx = torch.empty(n, dtype=torch.long, device=device)
+    pair = torch.empty(n, dtype=torch.long, device=device)
+    score = torch.empty(n, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        book.quantize(x.data_ptr(), n, idx.data_ptr(), pair.data_ptr(), score.data_ptr(), stream.cuda_stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    value = world * n / (ms / 1000.0)
+
+    # end to end through the public API, pinned host input and output
+    x_host = x.cpu().pin_memory()
+    host_out = torch.empty(n, dtype=torch.long).pin_memory()
+    for _ in range(1):
+        host_out.copy_(q.quantize(x_host))
+    torch.cuda.synchronize()
+    barrier()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 3))
+    e2.record(stream)
+    for _ in range(e2e_steps):
+        r = q.quantize(x_host)
+        host_out.copy_(r, non_blocking=True)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e2.elapsed_time(e3)) / e2e_steps
+    if not torch.equal(host_out, idx.cpu()):
+        raise RuntimeError("end-to-end indices differ from the device-resident run")
+
+    extra = {}
+    if rank == 0 and world == 1 and not args.skip_dequant:
+        extra["dequant"] = dequant_bench(q, device, stream, args)
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_sample > 0:
+        sample = x_host[: args.cpu_sample].numpy()
+        rate, threads = cpu_reference_rate(sample, args.max_shell)
+        cpu = {"value": rate, "unit": "blocks/s", "cores": threads, "kind": "port",
+               "sample": f"first {args.cpu_sample} blocks of the same workload; oracle restatement of "
+                         "LeechLatticeVectorQuantizer.quantize with per-pair sorts (mode 0), all host threads"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    ops = algorithmic_ops_per_block(2, args.max_shell)
+    clk = clocks.summary()
+    peak_tflops = SMS * FP32_LANES * 2 * (clk.get("sm_max_mhz") or 1965.0) * 1e6 / 1e12
+    achieved = ops * n / (ms / 1000.0) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "blocks/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"gaussian N(0,1) fp32 [{n}, 24] per GPU, seed 1+rank, shells 2..{args.max_shell} "
+                               "(48-bit index), bit-exact reference quantize", "blocks_per_gpu": n,
+                   "l2": "inputs (1.6 GB) larger than L2, no flush", "parallelism": f"weak x{world}"},
+        "e2e": {"value": world * n / (e2e_ms / 1000.0), "unit": "blocks/s", "h2d_bytes_per_step": n * 96,
+                "d2h_bytes_per_step": n * 8},
+        "gpu_launches": 2 * args.steps,
+        "roofline": {"bound": "alu", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tflops, "traffic": None,
+                     "note": f"{ops / 1e6:.3f} M algorithmic ops/block (2 per distinct nonzero leader value per "
+                             "evaluated pair + 2x4096x24 prefix adds); peak = 148 SMs x 128 FP32 lanes x 2 x "
+                             "max SM clock (FFMA)"},
+        "clocks": clk,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    line.update(extra)
+    print(json.dumps(line), flush=True)
+
+
+def dequant_bench(q, device, stream, args) -> dict:
+    import torch
+
+    work = llama3_dequant_workload(q, device)
+    book = q._book()
+    outs = {bpr: torch.empty((idx.shape[0], bpr * 24), dtype=torch.bfloat16, device=device)
+            for bpr, (idx, _) in work.items()}
+    n_idx = sum(idx.numel() for idx, _ in work.values())
+    n_rows = sum(idx.shape[0] for idx, _ in work.values())
+
+    def step():
+        for bpr, (idx, scale) in work.items():
+            book.dequantize_bf16(idx.data_ptr(), idx.numel(), scale.data_ptr(), bpr, outs[bpr].data_ptr(), None,
+                                 stream.cuda_stream)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    algo_bytes = n_idx * (8 + 48) + n_rows * 2
+    gbs = algo_bytes / (ms / 1000.0) / 1e9
+    peaks = measured_peaks()
+    del outs, work
+    torch.cuda.empty_cache()
+    return {"value": gbs, "unit": "GB/s", "ms_per_step": ms, "indices": n_idx, "rows": n_rows,
+            "workload": "Llama-3-8B linears (32 layers), random valid int64 indices seed 3, bf16 out, fp16 row scales",
+            "gpu_launches": 2 * args.steps,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                         "note": "56 B per index (8 B int64 index + 48 B bf16) + 2 B per row; peak of "
+                                 + ("fallback" if peaks.get("fallback") else "measured") + " copy bandwidth"}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--rows", type=int, default=16_777_216)
+    ap.add_argument("--max-shell", type=int, default=13)
+    ap.add_argument("--cpu-sample", type=int, default=96)
+    ap.add_argument("--skip-dequant", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -160,11 +160,45 @@ def codewords(ref, rng: random.Random) -> list[dict]:
     return [{"max_shell": 13, "index": i, "codeword": list(q.codeword(i))} for i in picks]
 
 
+def metadata(root: str, shells=(4, 13)) -> dict:
+    """The device metadata dicts the reference's GPU API hands its two CUDA
+    launchers (_quantize_cuda_metadata / _codeword_cuda_metadata), built on a
+    CPU device, with every tensor stored as a nested list plus its dtype."""
+    sys.path.insert(0, root)
+    from impl import leech_lattice_vector_quantizer_gpu as gpu  # noqa: E402
+
+    def dump(d):
+        out = {}
+        for k, v in d.items():
+            if k == "golay_indices":  # ~1M entries, a pure function of the Golay order; tests rebuild it
+                continue
+            if hasattr(v, "tolist"):
+                out[k] = {"dtype": str(v.dtype).replace("torch.", ""), "data": v.tolist()}
+            else:
+                out[k] = v
+        return out
+
+    res = {}
+    for m in shells:
+        q = gpu.LeechLatticeVectorQuantizerGpu(max_shell=m, use_cache=False, device="cpu")
+        res[str(m)] = {"quantize_meta": dump(q._quantize_cuda_metadata()),
+                       "codeword_meta": dump(q._codeword_cuda_metadata()),
+                       "comb": q._binom.tolist()}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--procs", type=int, default=8)
+    ap.add_argument("--only-metadata", action="store_true")
     args = ap.parse_args()
+    (HERE / "reference_metadata.json").write_text(json.dumps({
+        "source": "impl/leech_lattice_vector_quantizer_gpu.py _quantize_cuda_metadata / _codeword_cuda_metadata",
+        "shells": metadata(args.reference),
+    }))
+    if args.only_metadata:
+        return
     ref = _reference_module(args.reference)
     rng = random.Random(7)
 

@@ -1,0 +1,76 @@
+"""GPU dequantizer: integer codewords bit-exact against the oracle's
+codeword(); fp32 outputs bit-exact against the reference API's formulas; bf16
+with per-row fp16 scales bit-exact against the same product done by torch."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden, oracle_book
+
+pytestmark = pytest.mark.gpu
+
+
+def api(m: int):
+    from llvq_paper_reproduction_b200 import LeechLatticeVectorQuantizerGpu
+
+    return LeechLatticeVectorQuantizerGpu(max_shell=m, use_cache=False, device="cuda")
+
+
+def random_indices(total: int, n: int, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, total, size=n, dtype=np.int64)
+
+
+@pytest.mark.parametrize("m", [2, 4, 13])
+def test_lattice_vs_oracle(m):
+    q = api(m)
+    idx = random_indices(q.total_count, 4000, seed=m)
+    idx[:4] = [0, q.total_count - 1, 1103 % q.total_count, 196560 % q.total_count]
+    got = q.dequantize_lattice(torch.from_numpy(idx).cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle_book(m).codeword_batch(idx))
+
+
+def test_reference_codeword_fixtures(reference_tables):
+    q = api(13)
+    rows = reference_tables["codewords"]
+    idx = torch.tensor([r["index"] for r in rows], device="cuda")
+    np.testing.assert_array_equal(q.dequantize_lattice(idx).cpu().numpy(), np.array([r["codeword"] for r in rows]))
+
+
+def test_fp32_kinds_bit_exact():
+    from llvq_paper_reproduction_b200 import _native
+
+    q = api(13)
+    idx = torch.from_numpy(random_indices(q.total_count, 20000, seed=1)).cuda()
+    lat = q.dequantize_lattice(idx)
+    # GPU API semantics (_gpu.py:298): python-float scale times an fp32 tensor
+    want = (0.35355339059327373 * lat.to(torch.float32))
+    got = q.dequantize(idx)
+    assert torch.equal(got, want)
+    # CPU API semantics: the double product rounded to fp32
+    out = torch.empty_like(got)
+    q._book().dequantize(idx.data_ptr(), idx.numel(), out.data_ptr(), _native.OUT_F32_DOUBLE, None,
+                         torch.cuda.current_stream().cuda_stream)
+    want_d = (0.35355339059327373 * lat.cpu().numpy().astype(np.float64)).astype(np.float32)
+    np.testing.assert_array_equal(out.cpu().numpy(), want_d)
+
+
+def test_bf16_rowscale_bit_exact():
+    q = api(13)
+    rows, blocks = 64, 171
+    idx = torch.from_numpy(random_indices(q.total_count, rows * blocks, seed=2).reshape(rows, blocks)).cuda()
+    scale = (torch.rand(rows, device="cuda") * 0.05 + 0.001).to(torch.float16)
+    got = q.dequantize_bf16(idx, scale)
+    ref32 = q.dequantize(idx.reshape(-1)).reshape(rows, blocks * 24) * scale.float()[:, None]
+    assert torch.equal(got, ref32.to(torch.bfloat16))
+
+
+def test_out_of_range_raises():
+    q = api(4)
+    with pytest.raises(IndexError):
+        q.dequantize(torch.tensor([0, q.total_count], device="cuda"))
+    with pytest.raises(IndexError):
+        q.dequantize_lattice(torch.tensor([-1], device="cuda"))
+    assert q.dequantize(torch.empty(0, dtype=torch.long, device="cuda")).shape == (0, 24)

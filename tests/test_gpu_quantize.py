@@ -1,0 +1,172 @@
+"""GPU parity of the sm_100a quantizer against the reference: its recorded
+outputs (golden fixtures) and the oracle on seeded inputs, through the public
+API and the reference-facing shim; plus size-independent properties at the
+full 65,536-block Gaussian workload."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import f32, golden, oracle_book
+
+pytestmark = pytest.mark.gpu
+
+_APIS = {}
+
+
+def api(m: int, lo: int = 2):
+    from llvq_paper_reproduction_b200 import LeechLatticeVectorQuantizerGpu
+
+    key = (m, lo)
+    if key not in _APIS:
+        _APIS[key] = LeechLatticeVectorQuantizerGpu(max_shell=m, min_shell=lo, use_cache=False, device="cuda")
+    return _APIS[key]
+
+
+def gaussian(n: int, seed: int) -> np.ndarray:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn((n, 24), generator=g, dtype=torch.float32).numpy()
+
+
+def run(q, x: np.ndarray, table_driven: bool = False):
+    xt = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+    idx, pair, score = q.quantize_cuda(xt, return_details=True, table_driven=table_driven)
+    torch.cuda.synchronize()
+    return idx.cpu().numpy(), pair.cpu().numpy(), score.cpu().numpy()
+
+
+def test_library_loaded_and_specialized():
+    assert api(13).specialized and api(4).specialized and api(13, 13).specialized
+    assert not api(3).specialized
+
+
+@pytest.mark.parametrize("table_driven", [False, True])
+def test_reference_fixtures(reference_cases, table_driven):
+    """All 225 recorded reference quantize calls, batched per codebook."""
+    by_m: dict[int, list] = {}
+    for case in reference_cases:
+        for m, res in case["results"].items():
+            by_m.setdefault(int(m), []).append((case["name"], f32(case["x"]), res["index"]))
+    for m, rows in sorted(by_m.items()):
+        x = np.stack([r[1] for r in rows])
+        idx, _, _ = run(api(m), x, table_driven)
+        for (name, _, want), got in zip(rows, idx):
+            assert got == want, (name, m, table_driven)
+
+
+@pytest.mark.parametrize("m,lo,n", [(13, 2, 512), (13, 13, 256), (4, 2, 512), (3, 2, 256), (6, 2, 256)])
+def test_gaussian_vs_oracle(m, lo, n):
+    x = gaussian(n, seed=100 + m + lo)
+    idx, pair, score = run(api(m, lo), x)
+    o_idx, o_g, o_k, o_s = oracle_book(m, lo).quantize_batch(x)
+    np.testing.assert_array_equal(idx, o_idx)
+    np.testing.assert_array_equal(pair, o_k.astype(np.int64) * 4096 + o_g)
+    np.testing.assert_array_equal(score, o_s.astype(np.float32))
+
+
+def test_table_driven_equals_generated_m13():
+    x = gaussian(256, seed=7)
+    a = run(api(13), x)[0]
+    b = run(api(13), x, table_driven=True)[0]
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(a, oracle_book(13).quantize_batch(x)[0])
+
+
+def test_degenerate_rows_vs_oracle():
+    """Rows with exact ties: integers, half-integers, repeated |x|, zeros,
+    scaled lattice points and their midpoints (exact-pass window)."""
+    rng = np.random.default_rng(5)
+    rows = [np.zeros(24), np.ones(24), -np.ones(24), np.eye(24)[3] * 2.0]
+    rows += list(rng.integers(-3, 4, size=(24, 24)).astype(np.float64))
+    rows += list((rng.integers(-8, 9, size=(12, 24)) / 2.0))
+    t = np.abs(rng.standard_normal(24))
+    t[1::2] = t[::2]
+    rows.append(t * np.where(rng.random(24) < 0.5, -1, 1))
+    ob = oracle_book(13)
+    for _ in range(8):
+        y = np.array(ob.codeword(int(rng.integers(ob.total_count))), dtype=np.float64) * 0.35355339059327373
+        z = np.array(ob.codeword(int(rng.integers(ob.total_count))), dtype=np.float64) * 0.35355339059327373
+        rows += [y, (y + z) / 2, y * 1.5]
+    x = np.stack(rows).astype(np.float32)
+    for m in (13, 4):
+        np.testing.assert_array_equal(run(api(m), x)[0], oracle_book(m).quantize_batch(x)[0])
+
+
+def test_nonfinite_and_empty():
+    x = gaussian(8, seed=3)
+    x[2, 5] = np.nan
+    x[5, 0] = np.inf
+    idx, pair, score = run(api(13), x)
+    assert idx[2] == -1 and idx[5] == -1 and pair[2] == -1 and np.isnan(score[5])
+    good = [0, 1, 3, 4, 6, 7]
+    np.testing.assert_array_equal(idx[good], oracle_book(13).quantize_batch(x[good])[0])
+    e = api(13).quantize(torch.empty((0, 24), device="cuda"))
+    assert e.shape == (0,)
+
+
+def test_scalar_and_shapes():
+    q = api(4)
+    x = gaussian(6, seed=9)
+    want = oracle_book(4).quantize_batch(x)[0]
+    assert q.quantize(list(map(float, x[0]))) == want[0]  # sequence -> int
+    t = q.quantize(torch.from_numpy(x).cuda().reshape(2, 3, 24))
+    assert t.shape == (2, 3) and t.flatten().tolist() == list(want)
+    with pytest.raises(ValueError):
+        q.quantize(torch.zeros((3, 23), device="cuda"))
+
+
+def test_full_config1_properties():
+    """65,536 N(0,1) blocks (seed 0), shells 2..13: every index is in range,
+    decodes to a codeword that encodes back to it, re-quantizing the
+    dequantized block returns the same index, and a seeded sample equals the
+    oracle."""
+    q = api(13)
+    x = torch.randn((65536, 24), generator=torch.Generator().manual_seed(0), dtype=torch.float32)
+    xd = x.cuda()
+    idx = q.quantize(xd)
+    assert int(idx.min()) >= 0 and int(idx.max()) < q.total_count
+    recon = q.dequantize(idx)
+    again = q.quantize(recon)
+    assert torch.equal(again, idx)
+    sample = np.random.default_rng(0).choice(65536, size=192, replace=False)
+    np.testing.assert_array_equal(idx.cpu().numpy()[sample], oracle_book(13).quantize_batch(x.numpy()[sample])[0])
+    lat = q.dequantize_lattice(idx[sample.tolist()]).cpu().numpy()
+    for i, row in zip(sample, lat):
+        assert q.encode_codeword(row) == int(idx[int(i)])
+
+
+def _meta_tensors(d, device):
+    out = {}
+    for k, v in d.items():
+        out[k] = torch.tensor(v["data"], dtype=getattr(torch, v["dtype"]), device=device) if isinstance(v, dict) else v
+    return out
+
+
+@pytest.mark.parametrize("m", [4, 13])
+def test_reference_shims(m):
+    """quantize_lattice_cuda / dequantize_lattice_cuda called exactly as the
+    reference's GPU API calls them, with its own recorded metadata dicts."""
+    from llvq_paper_reproduction_b200.llvq_cuda_dequantize import dequantize_lattice_cuda
+    from llvq_paper_reproduction_b200.llvq_cuda_quantize import quantize_lattice_cuda
+
+    fx = golden("reference_metadata.json")["shells"][str(m)]
+    meta = _meta_tensors(fx["quantize_meta"], "cuda")
+    rank_meta = _meta_tensors(fx["codeword_meta"], "cuda")
+    comb = torch.tensor(fx["comb"], dtype=torch.long, device="cuda")
+    x = torch.from_numpy(gaussian(128, seed=m)).cuda()
+    n = x.shape[0]
+    indices = torch.empty(n, dtype=torch.long, device="cuda")
+    best_pair = torch.empty(n, dtype=torch.long, device="cuda")
+    best_score = torch.empty(n, dtype=torch.float32, device="cuda")
+    quantize_lattice_cuda(x, indices, best_pair, best_score, meta, rank_meta, comb)
+    out = torch.empty((n, 24), dtype=torch.long, device="cuda")
+    dequantize_lattice_cuda(indices, out, rank_meta, comb)
+    torch.cuda.synchronize()
+    o_idx = oracle_book(m).quantize_batch(x.cpu().numpy())[0]
+    np.testing.assert_array_equal(indices.cpu().numpy(), o_idx)
+    np.testing.assert_array_equal(out.cpu().numpy(), oracle_book(m).codeword_batch(o_idx))
+    with pytest.raises(ValueError):
+        quantize_lattice_cuda(x.double(), indices, best_pair, best_score, meta, rank_meta, comb)
+    with pytest.raises(ValueError):
+        quantize_lattice_cuda(x.cpu(), indices, best_pair, best_score, meta, rank_meta, comb)
