@@ -166,13 +166,12 @@ def run_reference_arm(args) -> None:
 
 # ----------------------------------------------------------------- GPU side
 
-def llama3_dequant_workload(q, device, seed: int = 3):
+def llama3_dequant_workload(q, device, seed: int = 3, layers: int = 32):
     """Random valid indices of every Llama-3-8B linear (uniform shell, class
     within shell, local index) and fp16 per-row scales, grouped by blocks per
     row: in-dim 4096 -> 171 blocks (4104), in-dim 14336 -> 598 blocks (14352)."""
     import torch
 
-    layers = 32
     groups = {171: layers * (4096 + 1024 + 1024 + 4096 + 14336 + 14336), 598: layers * 4096}
     g = torch.Generator(device=device).manual_seed(seed)
     flat = [st for s in q.classes_by_shell for st in q.local_structures[s]]
@@ -327,7 +326,7 @@ def run_gpu_arm(args) -> None:
 def dequant_bench(q, device, stream, args) -> dict:
     import torch
 
-    work = llama3_dequant_workload(q, device)
+    work = llama3_dequant_workload(q, device, layers=args.dequant_layers)
     book = q._book()
     outs = {bpr: torch.empty((idx.shape[0], bpr * 24), dtype=torch.bfloat16, device=device)
             for bpr, (idx, _) in work.items()}
@@ -355,7 +354,8 @@ def dequant_bench(q, device, stream, args) -> dict:
     del outs, work
     torch.cuda.empty_cache()
     return {"value": gbs, "unit": "GB/s", "ms_per_step": ms, "indices": n_idx, "rows": n_rows,
-            "workload": "Llama-3-8B linears (32 layers), random valid int64 indices seed 3, bf16 out, fp16 row scales",
+            "workload": f"Llama-3-8B linears ({args.dequant_layers} layers), random valid int64 indices seed 3, "
+                        "bf16 out, fp16 row scales",
             "gpu_launches": 2 * args.steps,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / peaks["hbm_gbs"], "traffic": None,
@@ -373,6 +373,7 @@ def main():
     ap.add_argument("--max-shell", type=int, default=13)
     ap.add_argument("--cpu-sample", type=int, default=96)
     ap.add_argument("--skip-dequant", action="store_true")
+    ap.add_argument("--dequant-layers", type=int, default=32)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)

@@ -67,9 +67,8 @@ int llvq_codebook_info(const llvq_codebook* cb, int64_t* total_count, int32_t* n
  * (bit-exact with LeechLatticeVectorQuantizer.quantize, ties in its loop
  * order), best_pair[i] = class_id * 4096 + golay_index and best_score[i] the
  * fp32 rounding of the reference's fp64 score.  Rows with NaN/Inf get index,
- * pair -1 and score NaN.  best_pair and best_score double as the hand-over
- * between the search and finalize kernels.  Replaces quantize_lattice_cuda
- * (impl/llvq_cuda_quantize.py:544-602). */
+ * pair -1 and score NaN.  One kernel launch; no scratch memory.  Replaces
+ * quantize_lattice_cuda (impl/llvq_cuda_quantize.py:544-602). */
 int llvq_quantize(const llvq_codebook* cb, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
                   float* best_score, void* stream);
 int llvq_quantize_ex(const llvq_codebook* cb, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,

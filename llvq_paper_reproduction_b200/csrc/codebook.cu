@@ -232,6 +232,7 @@ int build(llvq::Codebook& cb, int32_t n, const int32_t* shell, const int32_t* pa
       c.sign_count = 1ull << sign_shift;
       const u128 p0 = multinomial(c.m0, c.nv0), p1 = multinomial(c.m1, c.nv1);
       if ((p0 * p1) >> 58) return fail(LLVQ_ERR_UNSUPPORTED, "class too large for 64-bit ranks");
+      if (p1 >> 32) return fail(LLVQ_ERR_UNSUPPORTED, "class too large for 32-bit sub-ranks");
       c.f1_perm = (uint64_t)p1;
       c.perm_count = (uint64_t)(p0 * p1);
     }
@@ -291,7 +292,33 @@ int upload(llvq::Codebook& cb, int device) {
   const size_t o_wword = off; off = align256(off + kNumGolay * sizeof(uint32_t));
   const size_t o_wlex = off; off = align256(off + kNumGolay * sizeof(uint16_t));
   const size_t o_byw = off; off = align256(off + kNumGolay * sizeof(uint16_t));
+  const size_t o_dcls = off; off = align256(off + n * sizeof(DecodeClass));
   std::vector<unsigned char> host(off, 0);
+  {
+    std::vector<DecodeClass> dc(n);
+    for (size_t k = 0; k < n; ++k) {
+      const DevClass& c = cb.cls[k];
+      DecodeClass& d = dc[k];
+      d.start = c.start;
+      d.perm_count = c.perm_count;
+      d.inv_perm = 1.0 / (double)c.perm_count;
+      d.f0_perm = c.perm_count / c.f1_perm;
+      d.f1_perm = (uint32_t)c.f1_perm;
+      d.inv_f1 = 1.0 / (double)c.f1_perm;
+      d.meta = (uint32_t)c.parity | ((uint32_t)c.even_weight << 1) | ((uint32_t)c.sign_shift << 6) |
+               ((uint32_t)c.nv0 << 11) | ((uint32_t)c.nv1 << 15);
+      d.golay_base = (uint32_t)cb.weight_start[c.even_weight];
+      d.pad = 0;
+      d.v0 = d.m0 = d.v1 = d.m1 = 0;
+      for (int j = 0; j < kMaxVals; ++j) {
+        d.v0 |= (uint64_t)(uint8_t)(j < c.nv0 ? c.v0[j] : 0) << (8 * j);
+        d.m0 |= (uint64_t)(uint8_t)(j < c.nv0 ? c.m0[j] : 0) << (8 * j);
+        d.v1 |= (uint64_t)(uint8_t)(j < c.nv1 ? c.v1[j] : 0) << (8 * j);
+        d.m1 |= (uint64_t)(uint8_t)(j < c.nv1 ? c.m1[j] : 0) << (8 * j);
+      }
+    }
+    std::memcpy(host.data() + o_dcls, dc.data(), n * sizeof(DecodeClass));
+  }
   std::memcpy(host.data() + o_cls, cb.cls.data(), n * sizeof(DevClass));
   std::memcpy(host.data() + o_start, cb.class_start.data(), n * sizeof(int64_t));
   std::memcpy(host.data() + o_golay, cb.golay.data(), kNumGolay * sizeof(uint32_t));
@@ -323,6 +350,7 @@ int upload(llvq::Codebook& cb, int device) {
   d.wlist_word = reinterpret_cast<const uint32_t*>(base + o_wword);
   d.wlist_lex = reinterpret_cast<const uint16_t*>(base + o_wlex);
   d.by_weight = reinterpret_cast<const uint16_t*>(base + o_byw);
+  d.dcls = reinterpret_cast<const DecodeClass*>(base + o_dcls);
   std::copy(cb.weight_start, cb.weight_start + 25, d.weight_start);
   d.n_classes = (int32_t)n;
   d.min_shell = cb.min_shell;

@@ -58,9 +58,27 @@ struct DevClass {
   int8_t term_idx[16];
 };
 
+// Compact per-class record for the decoders: 96 bytes, read with six 16-byte
+// loads and kept in registers (values and multiplicities packed as bytes,
+// reciprocals for the two per-class divisions).
+struct alignas(16) DecodeClass {
+  int64_t start;
+  uint64_t perm_count;
+  double inv_perm;      // 1.0 / perm_count
+  uint64_t f0_perm;     // perm_count / f1_perm
+  uint32_t f1_perm;     // 1 for odd classes
+  uint32_t meta;        // parity | even_weight << 1 | sign_shift << 6 | nv0 << 11 | nv1 << 15
+  uint32_t golay_base;  // even: start of its weight group in by_weight
+  uint32_t pad;
+  double inv_f1;        // 1.0 / f1_perm
+  uint64_t v0, m0, v1, m1;  // byte j = j-th value / multiplicity (descending values)
+};
+static_assert(sizeof(DecodeClass) == 96, "decode record is six 16-byte loads");
+
 // Everything a kernel needs about one codebook (plain pointers, passed by value).
 struct DevBook {
   const DevClass* cls;
+  const DecodeClass* dcls;        // [n_classes] compact decode records
   const int64_t* class_start;     // [n_classes] (binary search)
   const uint32_t* golay;          // [4096] lexicographic order, bit d = coordinate d
   const uint16_t* golay_wrank;    // [4096] position among the words of equal weight

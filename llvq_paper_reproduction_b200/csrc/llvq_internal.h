@@ -11,7 +11,8 @@
 
 namespace llvq {
 
-using SearchLauncher = cudaError_t (*)(const float*, int64_t, const DevBook&, long long*, float*, cudaStream_t);
+using SearchLauncher = cudaError_t (*)(const float*, int64_t, const DevBook&, long long*, long long*, float*,
+                                       cudaStream_t);
 
 // A generated search specialisation: its class signature, launcher and the
 // window constants of its FFMA chains.

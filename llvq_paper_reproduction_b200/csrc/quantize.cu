@@ -3,25 +3,25 @@
 // (impl/leech_lattice_vector_quantizer.py:282-314), fused with the index
 // encoding (encode_codeword, :247-280).
 //
-// Kernel 1 (search): one CTA per 24-D block at a time (persistent grid), 128
-// threads x 32 Golay words each.  Per block it stages |x| in sorted order, the
-// 3 byte tables that permute a Golay word into that order, and the integer
-// image q = rint(|x| * 2^e) with |q| <= 2^19.  Per word it builds the suffix
-// sums of the sorted (sign-flipped) coordinates in registers and scores every
-// class with the generated FFMA chains (one FFMA per distinct leader value).
-// All suffix sums are exact integers in fp32; only the FFMA chain rounds, so
-// every approximate score is within a proven bound E of the exact real score.
-// The argmax is decided exactly: if a single word holds every pair within
-// W = 2E + 4 (q units) of the best approximate score, that word is handed to
-// kernel 2; otherwise the CTA re-scans all words and scores every pair inside
-// the window with the reference's own fp64 arithmetic (CPython 3.12 sum(), a
-// Neumaier-compensated sum) and the reference loop order for ties.
+// One CTA per 24-D block at a time (persistent grid), 128 threads x 32 Golay
+// words each.  Per block it stages |x| in sorted order, the 3 byte tables that
+// permute a Golay word into that order, and the integer image
+// q = rint(|x| * 2^e) with |q| <= 2^19.  Per word it builds the suffix sums of
+// the sorted (sign-flipped) coordinates in registers and scores every class
+// with the generated FFMA chains (one FFMA per distinct leader value).  All
+// suffix sums are exact integers in fp32; only the FFMA chain rounds, so every
+// approximate score is within a proven bound E of the exact real score.
 //
-// Kernel 2 (finalize): one thread per block.  Re-scores the classes of the
-// chosen word with exact integer projections, resolves the window with the
-// fp64 reference score, builds the winning codeword with the reference's
-// sort/tie rules (solve_even_subclass / solve_odd_subclass, :619-666) and
-// ranks it (rank_class_codeword and friends, :692-889).
+// The argmax is then decided exactly.  If a single word holds every pair
+// within W = 2E + 4 (q units) of the best approximate score, the search kernel
+// hands that word to the finalize kernel (one thread per block), which
+// re-scores the word's pairs inside the window with the reference's own fp64
+// arithmetic (CPython 3.12 sum(), a Neumaier-compensated sum).  Otherwise the
+// whole CTA re-scans all words that way.  Ties go to the earliest (Golay word,
+// class) in the reference loop order.  The winning codeword is rebuilt with
+// the reference's sort/tie rules (solve_even_subclass / solve_odd_subclass,
+// :619-666) and ranked (rank_class_codeword and friends, :692-889).
+// best_pair / best_score carry the hand-over between the two kernels.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -45,8 +45,8 @@ namespace llvq {
 
 constexpr int kSearchThreads = 128;
 constexpr int kWordsPerThread = kNumGolay / kSearchThreads;
-constexpr long long kTagWord = 1ll << 40;
-constexpr long long kTagExact = 2ll << 40;
+constexpr long long kTagWord = 1ll << 40;   // low 12 bits: the word
+constexpr long long kTagExact = 2ll << 40;  // bits 12..39: class, low 12 bits: word
 
 struct RowShared {
   float x[kDim];
@@ -63,6 +63,19 @@ struct RowShared {
   float red[kSearchThreads / 32];
   double xs_best[kSearchThreads];
   long long xs_order[kSearchThreads];
+};
+
+// The same block data for one thread (finalize kernel), without the byte tables.
+struct RowLocal {
+  float x[kDim];
+  float aval[kDim];
+  float lval[48];
+  int8_t apos[kDim];
+  int8_t arank[kDim];
+  uint32_t negmask;
+  uint32_t nposA;
+  float scale;
+  float K;
 };
 
 // ------------------------------------------------------------ row helpers
@@ -272,7 +285,8 @@ struct Ops<RuntimeSpec> {
 // Odd classes: R[t] = sum of the t largest x'_i.  The selected entries of the
 // 48-slot sorted list (positives at 24 + rank, negatives at 23 - rank) are
 // exactly one per coordinate; the t largest are the top t set bits.
-__device__ __forceinline__ void odd_sums(const RowShared& sh, uint32_t cA, float (&R)[25]) {
+template <class Row>
+__device__ __forceinline__ void odd_sums(const Row& sh, uint32_t cA, float (&R)[25]) {
   const uint32_t posA = cA ^ sh.nposA;
   const uint32_t negA = ~posA & kFull24;
   uint64_t m = ((uint64_t)posA << 24) | (uint64_t)(__brev(negA) >> 8);
@@ -287,8 +301,8 @@ __device__ __forceinline__ void odd_sums(const RowShared& sh, uint32_t cA, float
 
 // Even classes of word weight W: suffix sums of |q| inside (R1) and outside
 // (R0) the word, and the sign-parity penalties.
-template <int W, int N0>
-__device__ __forceinline__ void even_sums(const RowShared& sh, uint32_t c, uint32_t cA, float (&R0)[25],
+template <int W, int N0, class Row>
+__device__ __forceinline__ void even_sums(const Row& sh, uint32_t c, uint32_t cA, float (&R0)[25],
                                           float (&R1)[25], float& P0, float& P1) {
   uint32_t f1 = cA, f0 = ~cA & kFull24;
   R1[0] = 0.f;
@@ -311,8 +325,8 @@ __device__ __forceinline__ void even_sums(const RowShared& sh, uint32_t c, uint3
   P1 = negpar ? 0.f : qmin1;  // ... and for those that need an odd count
 }
 
-template <class S, int W>
-__device__ __forceinline__ float even_max_word(const DevBook& b, const RowShared& sh, uint32_t c, uint32_t cA,
+template <class S, int W, class Row>
+__device__ __forceinline__ float even_max_word(const DevBook& b, const Row& sh, uint32_t c, uint32_t cA,
                                                const float* nmk) {
   if constexpr (!Ops<S>::template has_even<W>()) {
     return -INFINITY;
@@ -323,8 +337,8 @@ __device__ __forceinline__ float even_max_word(const DevBook& b, const RowShared
   }
 }
 
-template <class S, int W, class F>
-__device__ __forceinline__ void even_cands_word(const DevBook& b, const RowShared& sh, uint32_t c, uint32_t cA,
+template <class S, int W, class Row, class F>
+__device__ __forceinline__ void even_cands_word(const DevBook& b, const Row& sh, uint32_t c, uint32_t cA,
                                                 const float* nmk, float thr, F&& f) {
   if constexpr (Ops<S>::template has_even<W>()) {
     float R0[25], R1[25], P0, P1;
@@ -337,8 +351,16 @@ __device__ __forceinline__ uint32_t permute_word(const RowShared& sh, uint32_t c
   return sh.utab[0][c & 255u] | sh.utab[1][(c >> 8) & 255u] | sh.utab[2][c >> 16];
 }
 
-template <class S>
-__device__ __forceinline__ float word_max(const DevBook& b, const RowShared& sh, uint32_t c, const float* nmk) {
+__device__ __forceinline__ uint32_t permute_word(const RowLocal& r, uint32_t c) {
+  uint32_t u = 0;
+#pragma unroll
+  for (int d = 0; d < kDim; ++d)
+    if ((c >> d) & 1u) u |= 1u << r.arank[d];
+  return u;
+}
+
+template <class S, class Row>
+__device__ __forceinline__ float word_max(const DevBook& b, const Row& sh, uint32_t c, const float* nmk) {
   const uint32_t cA = permute_word(sh, c);
   float best = -INFINITY;
   if constexpr (Ops<S>::kHasOdd) {
@@ -356,8 +378,8 @@ __device__ __forceinline__ float word_max(const DevBook& b, const RowShared& sh,
   return best;
 }
 
-template <class S, class F>
-__device__ __forceinline__ void word_cands(const DevBook& b, const RowShared& sh, uint32_t c, const float* nmk,
+template <class S, class Row, class F>
+__device__ __forceinline__ void word_cands(const DevBook& b, const Row& sh, uint32_t c, const float* nmk,
                                            float thr, F&& f) {
   const uint32_t cA = permute_word(sh, c);
   if constexpr (Ops<S>::kHasOdd) {
@@ -379,17 +401,32 @@ __device__ __forceinline__ void word_cands(const DevBook& b, const RowShared& sh
 // Exact-pass handler for one candidate pair: the reference's codeword and fp64
 // score, kept if it beats (score desc, loop order asc).  Not inlined: the
 // generated scoring code calls it from every class site.
-__device__ __noinline__ void consider_exact(const RowShared& sh, const DevBook& book, uint32_t word, int lex, int k,
-                                            double* best, long long* order) {
+__device__ __noinline__ void consider_exact(const float* x, const int8_t* apos, const DevBook& book, uint32_t word,
+                                            int lex, int k, double* best, long long* order) {
   int y[kDim];
   const DevClass& cls = book.cls[k];
-  build_candidate(sh.x, sh.apos, cls, word, y);
-  const double s = reference_score(sh.x, y, cls.shell);
+  build_candidate(x, apos, cls, word, y);
+  const double s = reference_score(x, y, cls.shell);
   const long long o = (long long)lex * book.n_classes + k;
   if (s > *best || (s == *best && o < *order)) {
     *best = s;
     *order = o;
   }
+}
+
+// Rebuild the winning codeword, its fp64 reference score and its index.
+__device__ __noinline__ void write_winner(const float* x, const int8_t* apos, const DevBook& book, long long order,
+                                          int64_t row, long long* index_out, long long* pair_out, float* score_out) {
+  const int lex = (int)(order / book.n_classes), k = (int)(order % book.n_classes);
+  const DevClass& c = book.cls[k];
+  const uint32_t word = book.golay[lex];
+  int y[kDim];
+  build_candidate(x, apos, c, word, y);
+  const double s = reference_score(x, y, c.shell);
+  const int choice = c.parity ? lex : (int)book.golay_wrank[lex];
+  index_out[row] = rank_codeword(c, y, word, choice);
+  pair_out[row] = (long long)k * kNumGolay + lex;
+  score_out[row] = (float)s;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -510,7 +547,7 @@ __global__ void __launch_bounds__(kSearchThreads) search_kernel(const float* __r
         const uint32_t c = __ldg(book.wlist_word + j);
         const int lex = __ldg(book.wlist_lex + j);
         word_cands<S>(book, sh, c, nmk, thr,
-                      [&](int k, float) { consider_exact(sh, book, c, lex, k, &best, &order); });
+                      [&](int k, float) { consider_exact(sh.x, sh.apos, book, c, lex, k, &best, &order); });
       }
       sh.xs_best[tid] = best;
       sh.xs_order[tid] = order;
@@ -522,8 +559,7 @@ __global__ void __launch_bounds__(kSearchThreads) search_kernel(const float* __r
             order = sh.xs_order[t];
           }
         }
-        const long long lex = order / book.n_classes, k = order % book.n_classes;
-        tag_out[row] = kTagExact | (k << 12) | lex;
+        tag_out[row] = kTagExact | ((order % book.n_classes) << 12) | (order / book.n_classes);
         m_out[row] = (float)best;
       }
     }
@@ -533,8 +569,13 @@ __global__ void __launch_bounds__(kSearchThreads) search_kernel(const float* __r
 
 // ------------------------------------------------------------- finalize
 
-__global__ void finalize_kernel(const float* __restrict__ x, int64_t n, DevBook book, const long long* tag_in,
-                                const float* m_in, long long* index_out, long long* pair_out, float* score_out) {
+// One thread per block: rebuild the block's sorted data, re-score the handed
+// word's pairs inside the window with the generated code and decide them in
+// fp64, then write index, pair and score.
+template <class S>
+__global__ void __launch_bounds__(128) finalize_kernel(const float* __restrict__ x, int64_t n, DevBook book,
+                                                       const long long* tag_in, const float* m_in,
+                                                       long long* index_out, long long* pair_out, float* score_out) {
   const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= n) return;
   const long long tag = tag_in[row];
@@ -544,95 +585,74 @@ __global__ void finalize_kernel(const float* __restrict__ x, int64_t n, DevBook 
     score_out[row] = NAN;
     return;
   }
-  float xv[kDim];
+  RowLocal r;
   float mx = 0.f;
-  uint32_t neg = 0;
+  r.negmask = 0;
 #pragma unroll
   for (int d = 0; d < kDim; ++d) {
-    xv[d] = x[row * kDim + d];
-    mx = fmaxf(mx, fabsf(xv[d]));
-    neg |= (uint32_t)(xv[d] < 0.f) << d;
+    r.x[d] = x[row * kDim + d];
+    mx = fmaxf(mx, fabsf(r.x[d]));
+    r.negmask |= (uint32_t)(r.x[d] < 0.f) << d;
   }
-  // ascending (|x|, position) order
-  int8_t apos[kDim];
-  for (int d = 0; d < kDim; ++d) apos[d] = (int8_t)d;
-  for (int i = 1; i < kDim; ++i) {
-    const int p = apos[i];
-    const float a = fabsf(xv[p]);
-    int j = i - 1;
-    while (j >= 0 && fabsf(xv[apos[j]]) > a) {
-      apos[j + 1] = apos[j];
-      --j;
+  r.scale = pow2f(row_exponent(mx));
+  r.K = kSqrt8F * r.scale;
+#pragma unroll
+  for (int i = 0; i < kDim; ++i) {
+    const float ai = fabsf(r.x[i]);
+    int rk = 0;
+#pragma unroll
+    for (int j = 0; j < kDim; ++j) {
+      const float aj = fabsf(r.x[j]);
+      rk += (aj < ai) || (aj == ai && j < i);
     }
-    apos[j + 1] = (int8_t)p;
+    r.arank[i] = (int8_t)rk;
   }
-  const int lex = (int)(tag & 4095);
-  const uint32_t word = book.golay[lex];
-  int best_k = -1;
-  double best = -INFINITY;
-  int y[kDim];
+  for (int i = 0; i < kDim; ++i) {
+    const int rk = r.arank[i];
+    const float q = rintf(fabsf(r.x[i]) * r.scale);
+    r.apos[rk] = (int8_t)i;
+    r.aval[rk] = q;
+    r.lval[24 + rk] = q;
+    r.lval[23 - rk] = -q;
+  }
+  {
+    const uint32_t pos = ~r.negmask & kFull24;
+    uint32_t u = 0;
+    for (int d = 0; d < kDim; ++d)
+      if ((pos >> d) & 1u) u |= 1u << r.arank[d];
+    r.nposA = u;
+  }
+  long long order;
   if (tag & kTagExact) {
-    best_k = (int)((tag >> 12) & ((1ll << 28) - 1));
+    order = (tag & 4095) * book.n_classes + ((tag >> 12) & ((1ll << 28) - 1));
   } else {
-    const float scale = pow2f(row_exponent(mx));
-    const float K = kSqrt8F * scale;
-    const double thr = (double)m_in[row] - window_width(K, book);
-    // exact integer images of the sorted sequences for this word
-    int xs[kDim], f0q[kDim], f1q[kDim];
-    int nxs = 0, n0 = 0, n1 = 0;
-    for (int r = kDim - 1; r >= 0; --r) {  // positives, largest first
-      const int p = apos[r];
-      const int q = (int)rintf(fabsf(xv[p]) * scale);
-      if (((neg >> p) & 1u) == ((word >> p) & 1u)) xs[nxs++] = q;
-      if ((word >> p) & 1u) f1q[n1++] = q; else f0q[n0++] = q;
-    }
-    for (int r = 0; r < kDim; ++r) {  // negatives, least negative first
-      const int p = apos[r];
-      if (((neg >> p) & 1u) != ((word >> p) & 1u)) xs[nxs++] = -(int)rintf(fabsf(xv[p]) * scale);
-    }
-    const int wt = __popc(word);
-    const int negpar = __popc(word & neg) & 1;
-    for (int k = 0; k < book.n_classes; ++k) {
-      const DevClass& c = book.cls[k];
-      long long proj = 0;
-      if (c.parity == 1) {
-        for (int t = 0; t < kDim; ++t) proj += (long long)c.asc0[kDim - 1 - t] * xs[t];
-      } else {
-        if (c.even_weight != wt) continue;
-        for (int t = 0; t < n0; ++t) proj += (long long)c.asc0[n0 - 1 - t] * f0q[t];
-        for (int t = 0; t < n1; ++t) proj += (long long)c.asc1[n1 - 1 - t] * f1q[t];
-        if (wt && negpar != c.required) proj -= 2ll * c.asc1[0] * f1q[n1 - 1];
-      }
-      const double approx = (double)proj - (double)c.shell * (double)K;
-      if (approx < thr) continue;
-      build_candidate(xv, apos, c, word, y);
-      const double s = reference_score(xv, y, c.shell);
-      if (s > best) {  // classes are visited in loop order: strict '>' keeps the first
-        best = s;
-        best_k = k;
-      }
+    constexpr int NS = Ops<S>::kNumShells;
+    const int min_shell = Ops<S>::kMinShellC >= 0 ? Ops<S>::kMinShellC : book.min_shell;
+    float nmk[NS];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) nmk[s] = -(float)(min_shell + s) * r.K;
+    const float thr = __double2float_rd((double)m_in[row] - window_width(r.K, book));
+    const int lex = (int)(tag & 4095);
+    const uint32_t c = __ldg(book.golay + lex);
+    double best = -INFINITY;
+    order = LLONG_MAX;
+    word_cands<S>(book, r, c, nmk, thr,
+                  [&](int k, float) { consider_exact(r.x, r.apos, book, c, lex, k, &best, &order); });
+    if (order == LLONG_MAX) {  // cannot happen for a finite row
+      index_out[row] = -1;
+      pair_out[row] = -1;
+      score_out[row] = NAN;
+      return;
     }
   }
-  if (best_k < 0) {  // cannot happen for a finite row; report it as invalid
-    index_out[row] = -1;
-    pair_out[row] = -1;
-    score_out[row] = NAN;
-    return;
-  }
-  const DevClass& c = book.cls[best_k];
-  build_candidate(xv, apos, c, word, y);
-  best = reference_score(xv, y, c.shell);
-  const int choice = c.parity ? lex : (int)book.golay_wrank[lex];
-  index_out[row] = rank_codeword(c, y, word, choice);
-  pair_out[row] = (long long)best_k * kNumGolay + lex;
-  score_out[row] = (float)best;
+  write_winner(r.x, r.apos, book, order, row, index_out, pair_out, score_out);
 }
 
 // ------------------------------------------------------------- launchers
 
 template <class S>
-static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book, long long* tag, float* m,
-                                 cudaStream_t stream) {
+static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book, long long* index, long long* pair,
+                                 float* score, cudaStream_t stream) {
   static int blocks_per_sm = 0, sms = 0;
   if (!blocks_per_sm) {
     int dev;
@@ -642,7 +662,10 @@ static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book,
     if (blocks_per_sm < 1) blocks_per_sm = 1;
   }
   const int64_t grid = std::min<int64_t>(n, (int64_t)sms * blocks_per_sm);
-  search_kernel<S><<<(unsigned)grid, kSearchThreads, 0, stream>>>(x, n, book, tag, m);
+  search_kernel<S><<<(unsigned)grid, kSearchThreads, 0, stream>>>(x, n, book, pair, score);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  finalize_kernel<S><<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(x, n, book, pair, score, index, pair, score);
   return cudaGetLastError();
 }
 
@@ -672,12 +695,7 @@ cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long 
     book.win_mg = cb.rt_mg;
     book.win_am = cb.rt_am;
   }
-  cudaError_t err = launch(x, n, book, pair, score, stream);
-  if (err != cudaSuccess) return err;
-  const int threads = 128;
-  const int64_t blocks = (n + threads - 1) / threads;
-  finalize_kernel<<<(unsigned)blocks, threads, 0, stream>>>(x, n, book, pair, score, index, pair, score);
-  return cudaGetLastError();
+  return launch(x, n, book, index, pair, score, stream);
 }
 
 }  // namespace llvq
