@@ -67,7 +67,8 @@ int llvq_codebook_info(const llvq_codebook* cb, int64_t* total_count, int32_t* n
  * (bit-exact with LeechLatticeVectorQuantizer.quantize, ties in its loop
  * order), best_pair[i] = class_id * 4096 + golay_index and best_score[i] the
  * fp32 rounding of the reference's fp64 score.  Rows with NaN/Inf get index,
- * pair -1 and score NaN.  One kernel launch; no scratch memory.  Replaces
+ * pair -1 and score NaN.  Two kernel launches (search, then finalize);
+ * best_pair / best_score carry the hand-over between them.  Replaces
  * quantize_lattice_cuda (impl/llvq_cuda_quantize.py:544-602). */
 int llvq_quantize(const llvq_codebook* cb, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
                   float* best_score, void* stream);
@@ -88,6 +89,19 @@ int llvq_dequantize(const llvq_codebook* cb, const int64_t* indices, int64_t n, 
  * neither bf16 output nor per-row scales). */
 int llvq_dequantize_bf16(const llvq_codebook* cb, const int64_t* indices, int64_t n, const uint16_t* row_scale_f16,
                          int64_t blocks_per_row, uint16_t* out_bf16, int32_t* error_count, void* stream);
+
+/* Fused dequant-GEMM: y[m, n] = sum_k a[m, k] * W[n, k], where row n of W is
+ * the dequantized indices[n * blocks_per_row + b] (b = 0 .. blocks_per_row-1,
+ * 24 columns each) times row_scale[n] (fp16 bits; NULL means 1).  a: bf16
+ * [m, k] row-major, 16-byte aligned, k % 8 == 0, k <= 24 * blocks_per_row
+ * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  Weights are
+ * decoded straight into shared memory and multiplied on the tcgen05 tensor
+ * cores with fp32 accumulation; they are never written to global memory.
+ * *error_flag (device int, may be NULL) is set to 1 if a tensor-core wait
+ * timed out.  No reference counterpart (the reference has no GEMM). */
+int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
+              const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
+              int32_t* error_flag, void* stream);
 
 /* Host-side scalar paths (no GPU needed).
  * llvq_codeword_host:  LeechLatticeVectorQuantizerGpu.codeword (_gpu.py:262-265)

@@ -34,7 +34,7 @@ FLAG_TABLE_DRIVEN = 1
 EXPORTS = (
     "llvq_codebook_create", "llvq_codebook_destroy", "llvq_codebook_info", "llvq_quantize", "llvq_quantize_ex",
     "llvq_dequantize_lattice", "llvq_dequantize", "llvq_dequantize_bf16", "llvq_codeword_host",
-    "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version",
+    "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version", "llvq_gemm",
 )
 
 _lib = None
@@ -62,6 +62,7 @@ def load() -> ctypes.CDLL:
             "llvq_dequantize_lattice": (ctypes.c_int, [vp, vp, i64, vp, vp, vp]),
             "llvq_dequantize": (ctypes.c_int, [vp, vp, i64, vp, i32, vp, vp]),
             "llvq_dequantize_bf16": (ctypes.c_int, [vp, vp, i64, vp, i64, vp, vp, vp]),
+            "llvq_gemm": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_codeword_host": (ctypes.c_int, [vp, i64, vp]),
             "llvq_encode_host": (ctypes.c_int, [vp, vp, P(i64)]),
             "llvq_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -151,6 +152,11 @@ class NativeCodebook:
 
     def dequantize(self, idx_ptr: int, n: int, out_ptr: int, kind: int, err_ptr: int | None, stream: int) -> None:
         check(self._lib.llvq_dequantize(self.handle, idx_ptr, n, out_ptr, kind, err_ptr, stream), "llvq_dequantize")
+
+    def gemm(self, idx_ptr: int, n_out: int, blocks_per_row: int, scale_ptr: int | None, a_ptr: int, m: int, k: int,
+             y_ptr: int, err_ptr: int | None, stream: int) -> None:
+        check(self._lib.llvq_gemm(self.handle, idx_ptr, n_out, blocks_per_row, scale_ptr, a_ptr, m, k, y_ptr, err_ptr,
+                                  stream), "llvq_gemm")
 
     def dequantize_bf16(self, idx_ptr: int, n: int, scale_ptr: int, blocks_per_row: int, out_ptr: int,
                         err_ptr: int | None, stream: int) -> None:

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -457,6 +458,21 @@ int llvq_dequantize_bf16(const llvq_codebook* h, const int64_t* indices, int64_t
   return on_device(h, [&] {
     return llvq::dequantize_launch(h->cb, indices, n, out_bf16, 3, row_scale_f16, blocks_per_row, error_count,
                                    (cudaStream_t)stream);
+  });
+}
+
+int llvq_gemm(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
+              const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
+              int32_t* error_flag, void* stream) {
+  if (m < 0 || n_out < 0 || blocks_per_row <= 0 || k <= 0 || k % 8 || k > 24 * blocks_per_row)
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes: need k % 8 == 0 and 0 < k <= 24 * blocks_per_row");
+  if (m > 0 && n_out > 0 && (!indices || !a_bf16 || !y || (reinterpret_cast<uintptr_t>(a_bf16) & 15)))
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm pointers: null, or activations not 16-byte aligned");
+  if (m > (int64_t)INT32_MAX || n_out > (int64_t)INT32_MAX || blocks_per_row > (int64_t)INT32_MAX)
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
+  return on_device(h, [&] {
+    return llvq::gemm_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
+                             (cudaStream_t)stream);
   });
 }
 

@@ -147,13 +147,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc::commit(mbar);
       }
-      if (!tc::mbar_wait(mbar, phase, kWaitLimit)) {
-        failed = true;
-        if (error_flag) atomicExch(error_flag, 1);
-      }
+      const bool done = tc::mbar_wait(mbar, phase, kWaitLimit);
       phase ^= 1;
-      __syncthreads();
-      if (failed) break;
+      failed = __syncthreads_or(!done) != 0;  // block-uniform decision
+      if (failed) {
+        if (tid == 0 && error_flag) atomicExch(error_flag, 1);
+        break;
+      }
     }
     if (failed) break;
     // epilogue: TMEM lane = weight row, column = activation row

@@ -53,4 +53,7 @@ cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t 
                               const uint16_t* row_scale, int64_t blocks_per_row, int* error_count,
                               cudaStream_t stream);
 
+cudaError_t gemm_launch(const Codebook& cb, const int64_t* idx, int64_t n_out, int64_t bpr, const uint16_t* rscale,
+                        const void* a, int64_t m, int64_t k, float* y, int* error_flag, cudaStream_t stream);
+
 }  // namespace llvq

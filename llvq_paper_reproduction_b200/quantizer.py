@@ -191,6 +191,33 @@ class LeechLatticeVectorQuantizerGpu:
         self._raise_if_bad(err)
         return out
 
+    def gemm(self, a: torch.Tensor, indices: torch.Tensor, row_scale: torch.Tensor | None = None) -> torch.Tensor:
+        """Fused dequant-GEMM: ``a @ W.T`` in fp32 for bf16 activations ``a``
+        [m, k] and a weight given by its indices [n, blocks] (W[n] =
+        dequantize(indices[n]).flatten()[:k] * row_scale[n]).  The weight is
+        decoded inside the kernel, never materialised (no reference
+        counterpart)."""
+        self._require_cuda("gemm")
+        if a.dim() != 2 or indices.dim() != 2:
+            raise ValueError("expected a [m, k] and indices [n, blocks]")
+        m, k = a.shape
+        n, bpr = indices.shape
+        a16 = a.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        idx = indices.to(device=self.device, dtype=torch.long).contiguous()
+        sc = None
+        if row_scale is not None:
+            if row_scale.shape != (n,):
+                raise ValueError("row_scale must have one entry per weight row")
+            sc = row_scale.to(device=self.device, dtype=torch.float16).contiguous()
+        y = torch.empty((m, n), dtype=torch.float32, device=self.device)
+        err = self._error_counter()
+        with torch.cuda.device(self.device):
+            self._book().gemm(idx.data_ptr(), n, bpr, sc.data_ptr() if sc is not None else None, a16.data_ptr(), m, k,
+                              y.data_ptr(), err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        if int(err.item()):
+            raise RuntimeError("tensor-core wait timed out in the fused dequant-GEMM")
+        return y
+
     def _dequantize_lattice_cuda(self, indices: torch.Tensor) -> torch.Tensor:
         self._require_cuda("dequantize_lattice_cuda")
         flat = indices.contiguous()
