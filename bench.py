@@ -284,6 +284,8 @@ def run_gpu_arm(args) -> None:
     extra = {}
     if rank == 0 and world == 1 and not args.skip_dequant:
         extra["dequant"] = dequant_bench(q, device, stream, args)
+    if rank == 0 and world == 1 and not args.skip_gemm:
+        extra["gemm"] = gemm_bench(q, device, stream, args)
     cpu = None
     if rank == 0 and world == 1 and args.cpu_sample > 0:
         sample = x_host[: args.cpu_sample].numpy()
@@ -363,6 +365,58 @@ def dequant_bench(q, device, stream, args) -> dict:
                                  + ("fallback" if peaks.get("fallback") else "measured") + " copy bandwidth"}}
 
 
+def gemm_bench(q, device, stream, args) -> dict:
+    """Fused dequant-GEMM on the Llama-3-8B MLP shapes: W 14336 x 4096 (171
+    blocks per row) and 4096 x 14336 (598 blocks per row), random valid
+    indices (seed 4) with fp16 row scales, bf16 activations N(0,1) [M, K]."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(4)
+    mats = []
+    for n_out, k in ((14336, 4096), (4096, 14336)):
+        bpr = (k + 23) // 24
+        idx = torch.randint(0, q.total_count, (n_out, bpr), generator=g, device=device)
+        scale = (torch.rand(n_out, generator=g, device=device) * 0.04 + 0.005).to(torch.float16)
+        mats.append((n_out, k, bpr, idx, scale))
+    book = q._book()
+    peaks = measured_peaks()
+    out = {}
+    for m in args.gemm_m:
+        acts = [torch.randn((m, k), generator=g, device=device).to(torch.bfloat16) for _, k, _, _, _ in mats]
+        ys = [torch.empty((m, n), dtype=torch.float32, device=device) for n, _, _, _, _ in mats]
+
+        def step():
+            for (n_out, k, bpr, idx, scale), a, y in zip(mats, acts, ys):
+                book.gemm(idx.data_ptr(), n_out, bpr, scale.data_ptr(), a.data_ptr(), m, k, y.data_ptr(), None,
+                          stream.cuda_stream)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        flops = sum(2.0 * m * n * k for n, k, _, _, _ in mats)
+        tflops = flops / (ms / 1000.0) / 1e12
+        nbytes = sum(n * bpr * 8 + n * 2 + m * k * 2 + m * n * 4 for n, k, bpr, _, _ in mats)
+        t_tensor = flops / (peaks["bf16_tflops"] * 1e12)
+        t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9)
+        bound = "tensor" if t_tensor >= t_hbm else "hbm"
+        out[str(m)] = {"tflops": tflops, "ms": ms,
+                       "roofline": {"bound": bound, "time_frac": max(t_tensor, t_hbm) / (ms / 1000.0),
+                                    "achieved": tflops if bound == "tensor" else nbytes / (ms / 1000.0) / 1e9,
+                                    "peak": peaks["bf16_tflops"] if bound == "tensor" else peaks["hbm_gbs"],
+                                    "unit": "TFLOP/s" if bound == "tensor" else "GB/s"}}
+        del acts, ys
+    return {"workload": "Llama-3-8B MLP weights 14336x4096 + 4096x14336, random valid indices seed 4, fp16 row "
+                        "scales, bf16 activations N(0,1), fp32 out", "by_m": out,
+            "gpu_launches": 2 * args.steps * len(args.gemm_m)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -374,6 +428,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=96)
     ap.add_argument("--skip-dequant", action="store_true")
     ap.add_argument("--dequant-layers", type=int, default=32)
+    ap.add_argument("--skip-gemm", action="store_true")
+    ap.add_argument("--gemm-m", type=int, nargs="+", default=[1, 8, 64, 512, 4096])
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)

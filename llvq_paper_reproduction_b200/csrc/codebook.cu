@@ -307,7 +307,7 @@ int upload(llvq::Codebook& cb, int device) {
       d.f1_perm = (uint32_t)c.f1_perm;
       d.inv_f1 = 1.0 / (double)c.f1_perm;
       d.meta = (uint32_t)c.parity | ((uint32_t)c.even_weight << 1) | ((uint32_t)c.sign_shift << 6) |
-               ((uint32_t)c.nv0 << 11) | ((uint32_t)c.nv1 << 15);
+               ((uint32_t)c.nv0 << 11) | ((uint32_t)c.nv1 << 15) | ((uint32_t)c.required << 19);
       d.golay_base = (uint32_t)cb.weight_start[c.even_weight];
       d.pad = 0;
       d.v0 = d.m0 = d.v1 = d.m1 = 0;

@@ -74,6 +74,16 @@ __device__ __forceinline__ uint32_t unrank_step(uint64_t& rank, uint64_t& N, uin
   } else {
     const uint32_t inv = (uint32_t)sh.inv[rem];
     uint32_t r = (uint32_t)rank, n32 = (uint32_t)N;
+    // The smallest remaining value (tried last) is usually the most frequent
+    // one: test its branch, the top of the rank range, first.
+    const uint32_t last = (uint32_t)(63 - __clzll((long long)cnt)) >> 3;
+    const uint32_t blast = (uint32_t)(((uint64_t)n32 * byte_at(cnt, last)) >> s) * inv;
+    if (r >= n32 - blast) {
+      rank = r - (n32 - blast);
+      N = blast;
+      cnt -= 1ull << (8 * last);
+      return last;
+    }
     for (; j < kMaxVals; ++j) {
       const uint32_t c = byte_at(cnt, j);
       if (!c) continue;
@@ -158,7 +168,7 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, con
       i0 += !odd && !bit;
       y[d] = odd ? (((m & 3) == (bit ? 3 : 1)) ? m : -m) : m;
     }
-    if (!odd) ok = unrank_even_signs(y, sign);
+    if (!odd) ok = unrank_even_signs(y, sign, (meta >> 19) & 1);
   }
   if (!ok) {
 #pragma unroll

@@ -67,7 +67,7 @@ struct alignas(16) DecodeClass {
   double inv_perm;      // 1.0 / perm_count
   uint64_t f0_perm;     // perm_count / f1_perm
   uint32_t f1_perm;     // 1 for odd classes
-  uint32_t meta;        // parity | even_weight << 1 | sign_shift << 6 | nv0 << 11 | nv1 << 15
+  uint32_t meta;        // parity | even_weight << 1 | sign_shift << 6 | nv0 << 11 | nv1 << 15 | required << 19
   uint32_t golay_base;  // even: start of its weight group in by_weight
   uint32_t pad;
   double inv_f1;        // 1.0 / f1_perm
@@ -172,61 +172,70 @@ LLVQ_HD uint64_t lower_sign_count(int f0n, int f1n, int fixed, int need) {
   return 1ull << (f0n + f1n - 1);
 }
 
-// Rank of the sign pattern of even codeword y among the valid patterns of its
-// magnitudes.  Returns UINT64_MAX if the signed sum is not 0 mod 8.
+// Even sign patterns (rank_even_signs / apply_even_signs of the reference,
+// impl/leech_lattice_vector_quantizer.py:804-841): masks over the nonzero
+// coordinates (bit i = i-th nonzero coordinate negative) whose signed sum is
+// 0 mod 8, counted in increasing mask order.  Only coordinates with
+// |v| = 2 (mod 4) -- the Golay word's positions -- move the sum mod 8 (by 4),
+// so a mask is valid iff its count of negative word coordinates has the
+// class's parity.  With p the bit of the first word coordinate, deleting bit
+// p maps the valid masks onto all masks of the remaining bits and preserves
+// their order (masks that agree above p and differ below it agree at p,
+// because no word coordinate lies below p).  So the rank is the mask with bit
+// p deleted, and unranking inserts the bit that fixes the parity.  Without
+// word coordinates (weight-0 classes) every mask is valid and rank = mask.
+
+// Rank of the sign pattern of even codeword y; UINT64_MAX if its signed sum
+// is not 0 mod 8.
 LLVQ_HD uint64_t rank_even_signs(const int* y) {
-  int sum = 0, f0n = 0, f1n = 0, fixed = 0;
+  int sum = 0, nz = 0, p = -1;
+  uint32_t mask = 0;
   for (int d = 0; d < kDim; ++d) {
     sum += y[d];
     const int a = y[d] < 0 ? -y[d] : y[d];
-    if (a) {
-      fixed += a;
-      if ((a & 3) == 2) f1n++; else f0n++;
-    }
+    if (!a) continue;
+    if (p < 0 && (a & 3) == 2) p = nz;
+    if (y[d] < 0) mask |= 1u << nz;
+    nz++;
   }
   if (sum & 7) return UINT64_MAX;
-  uint64_t rank = 0;
-  int high = 0;
-  for (int d = kDim - 1; d >= 0; --d) {
-    const int a = y[d] < 0 ? -y[d] : y[d];
-    if (!a) continue;
-    fixed -= a;  // coordinate d leaves the "lower" set
-    if ((a & 3) == 2) f1n--; else f0n--;
-    if (y[d] < 0) {
-      rank += lower_sign_count(f0n, f1n, fixed & 7, (-(high + a)) & 7);
-      high -= a;
-    } else {
-      high += a;
-    }
-  }
-  return rank;
+  if (p < 0) return mask;
+  return ((uint64_t)(mask >> (p + 1)) << p) | (mask & ((1u << p) - 1u));
 }
 
-// Apply the sign pattern of rank `rank` to the nonnegative magnitudes v.
-LLVQ_HD bool unrank_even_signs(int* v, uint64_t rank) {
-  int f0n = 0, f1n = 0, fixed = 0;
+// Apply the sign pattern of rank `rank` to the nonnegative magnitudes v of an
+// even class whose signed sum must have negative-word-coordinate parity
+// `required`.
+LLVQ_HD bool unrank_even_signs(int* v, uint64_t rank, int required) {
+  int nz = 0, p = -1;
   for (int d = 0; d < kDim; ++d) {
-    if (v[d]) {
-      fixed += v[d];
-      if ((v[d] & 3) == 2) f1n++; else f0n++;
-    }
+    if (!v[d]) continue;
+    if (p < 0 && (v[d] & 3) == 2) p = nz;
+    nz++;
   }
-  int high = 0;
-  for (int d = kDim - 1; d >= 0; --d) {
-    const int a = v[d];
-    if (!a) continue;
-    fixed -= a;
-    if ((a & 3) == 2) f1n--; else f0n--;
-    const uint64_t zero = lower_sign_count(f0n, f1n, fixed & 7, (-(high + a)) & 7);
-    if (rank < zero) {
-      high += a;
-    } else {
-      rank -= zero;
-      high -= a;
-      v[d] = -a;
+  uint32_t mask;
+  if (p < 0) {
+    if (nz < 32 && (rank >> nz)) return false;
+    mask = (uint32_t)rank;
+  } else {
+    if (rank >> (nz - 1)) return false;
+    const uint32_t r = (uint32_t)rank;
+    mask = ((r >> p) << (p + 1)) | (r & ((1u << p) - 1u));
+    int negw = 0, i = 0;
+    for (int d = 0; d < kDim; ++d) {
+      if (!v[d]) continue;
+      if ((v[d] & 3) == 2 && ((mask >> i) & 1u)) negw++;
+      i++;
     }
+    if ((negw & 1) != required) mask |= 1u << p;
   }
-  return rank == 0 && (high & 7) == 0;
+  int i = 0;
+  for (int d = 0; d < kDim; ++d) {
+    if (!v[d]) continue;
+    if ((mask >> i) & 1u) v[d] = -v[d];
+    i++;
+  }
+  return true;
 }
 
 // codeword (integer coordinates, before the 1/sqrt(8) scale) -> global index
@@ -275,7 +284,7 @@ LLVQ_HD bool unrank_codeword(const DevClass& c, uint64_t local, WordOf word_of_c
     if (!unrank_multiset(r1, c.v1, c.m1, c.nv1, n1, c.f1_perm, s1)) return false;
     int i0 = 0, i1 = 0;
     for (int d = 0; d < kDim; ++d) out[d] = ((word >> d) & 1u) ? s1[i1++] : s0[i0++];
-    return unrank_even_signs(out, sign);
+    return unrank_even_signs(out, sign, c.required);
   }
   if (cur >= (uint64_t)kNumGolay) return false;
   const uint32_t word = word_of_choice((int)cur);
