@@ -103,6 +103,15 @@ int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, in
               const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
               int32_t* error_flag, void* stream);
 
+/* Seeded random Hadamard rotation of each row of a [rows, cols] matrix, in
+ * segments of `block` columns (a power of two, <= 4096, dividing cols):
+ * forward out = H (signs * in) / sqrt(block), inverse out = signs * (H in) /
+ * sqrt(block); signs: int8 +-1 per column (device).  in: fp16 (in_is_half)
+ * or fp32; out: fp32 (may alias an fp32 input).  Device: the current one.
+ * No reference counterpart (the reference README lists the rotation only). */
+int llvq_hadamard(const void* in, int32_t in_is_half, float* out, int64_t rows, int64_t cols, int32_t block,
+                  const int8_t* signs, int32_t inverse, void* stream);
+
 /* Host-side scalar paths (no GPU needed).
  * llvq_codeword_host:  LeechLatticeVectorQuantizerGpu.codeword (_gpu.py:262-265)
  * llvq_encode_host:    LeechLatticeVectorQuantizer.encode_codeword (CPU module :247-280) */

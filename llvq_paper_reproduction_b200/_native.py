@@ -35,6 +35,7 @@ EXPORTS = (
     "llvq_codebook_create", "llvq_codebook_destroy", "llvq_codebook_info", "llvq_quantize", "llvq_quantize_ex",
     "llvq_dequantize_lattice", "llvq_dequantize", "llvq_dequantize_bf16", "llvq_codeword_host",
     "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version", "llvq_gemm",
+    "llvq_hadamard",
 )
 
 _lib = None
@@ -63,6 +64,7 @@ def load() -> ctypes.CDLL:
             "llvq_dequantize": (ctypes.c_int, [vp, vp, i64, vp, i32, vp, vp]),
             "llvq_dequantize_bf16": (ctypes.c_int, [vp, vp, i64, vp, i64, vp, vp, vp]),
             "llvq_gemm": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
+            "llvq_hadamard": (ctypes.c_int, [vp, i32, vp, i64, i64, i32, vp, i32, vp]),
             "llvq_codeword_host": (ctypes.c_int, [vp, i64, vp]),
             "llvq_encode_host": (ctypes.c_int, [vp, vp, P(i64)]),
             "llvq_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -162,6 +164,13 @@ class NativeCodebook:
                         err_ptr: int | None, stream: int) -> None:
         check(self._lib.llvq_dequantize_bf16(self.handle, idx_ptr, n, scale_ptr, blocks_per_row, out_ptr, err_ptr,
                                              stream), "llvq_dequantize_bf16")
+
+
+def hadamard(in_ptr: int, in_is_half: bool, out_ptr: int, rows: int, cols: int, block: int, signs_ptr: int,
+             inverse: bool, stream: int) -> None:
+    lib = load()
+    check(lib.llvq_hadamard(in_ptr, int(in_is_half), out_ptr, rows, cols, block, signs_ptr, int(inverse), stream),
+          "llvq_hadamard")
 
 
 _CACHE: dict = {}

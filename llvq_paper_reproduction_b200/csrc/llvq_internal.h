@@ -56,4 +56,7 @@ cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t 
 cudaError_t gemm_launch(const Codebook& cb, const int64_t* idx, int64_t n_out, int64_t bpr, const uint16_t* rscale,
                         const void* a, int64_t m, int64_t k, float* y, int* error_flag, cudaStream_t stream);
 
+cudaError_t hadamard_launch(const void* in, int in_is_half, float* out, int64_t rows, int64_t cols, int block,
+                            const int8_t* signs, int inverse, cudaStream_t stream);
+
 }  // namespace llvq

@@ -1,0 +1,190 @@
+"""Wrappers around the Λ24 quantizer: spherical shaping with a global scale
+(the reference's Gaussian evaluation) and shape-gain quantization with a
+scalar gain code matched to the chi distribution with 24 degrees of freedom.
+
+Spherical shaping follows the reference notebook
+notebooks/recreate_figure1_gaussian_sqnr.ipynb (cells 5 and 7):
+``ideal_gaussian_source_scale`` picks beta = sqrt(24 sigma^2 / E||y/sqrt 8||^2)
+over the finite ball codebook, blocks are quantized as Q(w / beta) and
+reconstructed as beta * dequantize(index); quality is reported as
+SQNR_bits = -1/2 log2(MSE) (impl/gaussian_baseline_quantizers.py:28-29).
+
+Shape-gain has no reference implementation (the reference README lists it
+but the package does not exist); it is defined here as:
+  * shape: the nearest point of one shell m (the reference search restricted
+    to shells m..m, i.e. the largest correlation <x, y>), direction
+    u = y / |y|;
+  * gain: g = <x, u> (the least-squares gain for that direction), coded with
+    a b-bit Lloyd-Max quantizer designed for the chi(24) density scaled by
+    sigma (the norm of a 24-D N(0, sigma^2 I) block);
+  * index = shape_index * 2^b + gain_index, reconstruction g_q * u.
+Every tensor step runs on the GPU; the shape search is the library kernel.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from functools import lru_cache
+
+import numpy as np
+import torch
+
+from .quantizer import LeechLatticeVectorQuantizerGpu
+from .tables import DIM, leech_shell_counts
+
+
+def mse_to_sqnr_bits(mse: float) -> float:
+    """SQNR in bits, -1/2 log2(MSE) (reference: impl/gaussian_baseline_quantizers.py:28-29)."""
+    return -0.5 * math.log2(mse)
+
+
+def mse_to_sqnr_db(mse: float) -> float:
+    return 10.0 * math.log10(1.0 / mse)
+
+
+def ideal_gaussian_source_scale(q: LeechLatticeVectorQuantizerGpu, variance: float = 1.0) -> float:
+    """beta matching the ball codebook's mean squared norm (shell m has squared
+    norm 2m after the 1/sqrt(8) scale) to a 24-D Gaussian source of the given
+    variance."""
+    weighted = sum(2.0 * shell * count for shell, count in q.shell_counts.items())
+    return math.sqrt(DIM * variance / (weighted / q.total_count))
+
+
+class SphericalShaping:
+    """Global-beta quantizer over the ball codebook shells min..max."""
+
+    def __init__(self, quantizer: LeechLatticeVectorQuantizerGpu, variance: float = 1.0):
+        self.q = quantizer
+        self.beta = ideal_gaussian_source_scale(quantizer, variance)
+
+    def quantize(self, w: torch.Tensor) -> torch.Tensor:
+        # true fp32 division by fp32(beta), as numpy evaluates w / beta for a
+        # float32 array (torch's scalar division would multiply by a rounded
+        # reciprocal instead)
+        w = w.to(device=self.q.device, dtype=torch.float32)
+        return self.q.quantize(w / torch.tensor(self.beta, dtype=torch.float32, device=w.device))
+
+    def dequantize(self, indices: torch.Tensor) -> torch.Tensor:
+        return self.beta * self.q.dequantize(indices)
+
+    def evaluate(self, w: torch.Tensor) -> dict:
+        """MSE per dimension and SQNR of w [n, 24] (the notebook's evaluate_spherical_shaping):
+        reconstruction in float64 from the CPU-API dequantized values."""
+        w = w.to(device=self.q.device, dtype=torch.float32)
+        idx = self.quantize(w)
+        lat = self.q.dequantize_lattice(idx).to(torch.float64)
+        recon = self.beta * (lat * (1.0 / math.sqrt(8.0)))
+        err = (w.to(torch.float64) - recon).pow(2).sum().item()
+        mse = err / (w.shape[0] * DIM)
+        return {"indices": idx, "mse": mse, "sqnr_bits": mse_to_sqnr_bits(mse), "sqnr_db": mse_to_sqnr_db(mse),
+                "beta": self.beta, "shape_bits": self.q.shape_bits}
+
+
+# ------------------------------------------------------------------ gain code
+
+@lru_cache(maxsize=64)
+def chi_lloyd_max(bits: int, dof: int = DIM, iters: int = 400) -> tuple[np.ndarray, np.ndarray]:
+    """Lloyd-Max reconstruction levels and decision thresholds (ascending)
+    for the chi distribution with `dof` degrees of freedom (unit sigma).
+
+    The density is evaluated on a fine grid; each iteration places the
+    thresholds at the midpoints of the levels and moves every level to the
+    conditional mean of its cell."""
+    n = 1 << bits
+    grid = np.linspace(1e-6, math.sqrt(dof) + 12.0, 200_001)
+    logpdf = (dof - 1) * np.log(grid) - grid * grid / 2.0
+    pdf = np.exp(logpdf - logpdf.max())
+    cdf = np.cumsum(pdf)
+    first = np.cumsum(pdf * grid)
+    total = cdf[-1]
+    # start from equal-probability cells
+    edges = np.interp(np.linspace(0, total, n + 1), cdf, grid)
+    levels = 0.5 * (edges[:-1] + edges[1:])
+    for _ in range(iters):
+        thr = 0.5 * (levels[:-1] + levels[1:])
+        idx = np.searchsorted(grid, thr)
+        bounds = np.concatenate([[0], idx, [grid.size]])
+        new = np.empty_like(levels)
+        for i in range(n):
+            lo, hi = bounds[i], bounds[i + 1]
+            mass = cdf[hi - 1] - (cdf[lo - 1] if lo else 0.0)
+            mom = first[hi - 1] - (first[lo - 1] if lo else 0.0)
+            new[i] = mom / mass if mass > 0 else levels[i]
+        if np.max(np.abs(new - levels)) < 1e-12:
+            levels = new
+            break
+        levels = new
+    return levels, 0.5 * (levels[:-1] + levels[1:])
+
+
+@dataclass(frozen=True)
+class RateSplit:
+    shell: int
+    shape_bits: int
+    gain_bits: int
+
+    @property
+    def bits_per_dim(self) -> float:
+        return (self.shape_bits + self.gain_bits) / DIM
+
+
+def rate_split(bits_per_dim: float, min_gain_bits: int = 3, max_shape_bits: int = 62) -> RateSplit:
+    """Largest single shell whose index fits the budget with at least
+    `min_gain_bits` left for the gain; the remaining bits go to the gain."""
+    budget = int(round(bits_per_dim * DIM))
+    counts = leech_shell_counts(60)
+    best = None
+    for m in range(2, 61):
+        sb = math.ceil(math.log2(counts[m]))
+        if sb > max_shape_bits or sb + min_gain_bits > budget:
+            break
+        best = RateSplit(m, sb, budget - sb)
+    if best is None:
+        raise ValueError(f"no shell fits {bits_per_dim} bits/dim")
+    return best
+
+
+class ShapeGainQuantizer:
+    """Single-shell shape with a chi-matched scalar gain (no reference
+    counterpart; see the module docstring for the definition)."""
+
+    def __init__(self, shell: int, gain_bits: int, sigma: float = 1.0, device="cuda", use_cache: bool = False):
+        self.shape = LeechLatticeVectorQuantizerGpu(max_shell=shell, min_shell=shell, device=device,
+                                                    use_cache=use_cache)
+        self.shell = shell
+        self.gain_bits = gain_bits
+        self.sigma = sigma
+        levels, thr = chi_lloyd_max(gain_bits)
+        self.levels = torch.tensor(levels * sigma, dtype=torch.float32, device=self.shape.device)
+        self.thresholds = torch.tensor(thr * sigma, dtype=torch.float32, device=self.shape.device)
+        self.norm = math.sqrt(2.0 * shell)  # |y| / sqrt(8) for every point of the shell
+
+    @classmethod
+    def for_rate(cls, bits_per_dim: float, sigma: float = 1.0, device="cuda") -> "ShapeGainQuantizer":
+        split = rate_split(bits_per_dim)
+        return cls(split.shell, split.gain_bits, sigma, device)
+
+    @property
+    def bits(self) -> int:
+        return self.shape.shape_bits + self.gain_bits
+
+    def quantize(self, x: torch.Tensor, row_sigma: torch.Tensor | None = None) -> torch.Tensor:
+        """x [..., 24] -> combined int64 indices.  row_sigma (broadcast to
+        x[..., 0]) rescales the gain code per block, e.g. per weight row."""
+        x = x.to(device=self.shape.device, dtype=torch.float32)
+        sidx = self.shape.quantize(x)
+        u = self.shape.dequantize(sidx) / self.norm
+        g = (x * u).sum(-1)
+        if row_sigma is not None:
+            g = g / row_sigma
+        gidx = torch.bucketize(g.contiguous(), self.thresholds)
+        return sidx * (1 << self.gain_bits) + gidx
+
+    def dequantize(self, indices: torch.Tensor, row_sigma: torch.Tensor | None = None) -> torch.Tensor:
+        indices = indices.to(self.shape.device)
+        gidx = indices & ((1 << self.gain_bits) - 1)
+        sidx = indices >> self.gain_bits
+        g = self.levels[gidx]
+        if row_sigma is not None:
+            g = g * row_sigma
+        return self.shape.dequantize(sidx) * (g / self.norm).unsqueeze(-1)
