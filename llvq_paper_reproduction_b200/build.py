@@ -26,10 +26,12 @@ LIB = PKG / "_lib" / "libllvq_b200.so"
 INCLUDE = PKG.parent / "include"
 
 # Codebooks with generated search code: name, min shell, max shell.
-# 2..13 is the reference's 48-bit (2 bits/dim) codebook; 13..13 the single
-# shell used by the shape-gain quantizer at 2 bits/dim; 2..4 a small codebook
-# for fast parity tests of the generated path.
-SPECS = (("m2_4", 2, 4), ("m2_13", 2, 13), ("s13", 13, 13))
+# 2..13 is the reference's 48-bit (2 bits/dim) codebook; 2..4 a small
+# codebook for fast parity tests of the generated path; single shells 2, 5,
+# 11 and 13 are the shape codebooks of the shape-gain quantizer (1, 1.5 and
+# 2 bits/dim; 13 is the largest shell that fits 48 bits).  Other codebooks
+# run the table-driven chains.
+SPECS = (("m2_4", 2, 4), ("m2_13", 2, 13), ("s2", 2, 2), ("s5", 5, 5), ("s11", 11, 11), ("s13", 13, 13))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",

@@ -43,47 +43,57 @@ constexpr int kAtoms = 3;
 constexpr int kMaxAct = 256;      // activation rows per pass (MMA N)
 constexpr uint32_t kWaitLimit = 1u << 22;
 
-struct GemmShared {
-  uint8_t w[kAtoms][kTileW * 128];   // 16 KB per atom, 1024-byte aligned
-  uint8_t a[kAtoms][kMaxAct * 128];  // 32 KB per atom
-  DecodeShared dec;
-  uint64_t mbar;
-  uint32_t tmem_base;
-  int error;
+// Dynamic shared memory, 1024-byte aligned: the weight tile (3 atoms of
+// 128 rows x 128 B), the activation tile (3 atoms of npad rows x 128 B, sized
+// to the batch so small batches fit several CTAs per SM), the decode tables,
+// the mbarrier and the TMEM address.
+struct GemmLayout {
+  uint32_t a_off, a_atom, dec_off, mbar_off, holder_off, bytes;
+  __host__ __device__ explicit GemmLayout(int npad) {
+    a_off = kAtoms * kTileW * 128;
+    a_atom = (uint32_t)npad * 128;
+    dec_off = a_off + kAtoms * a_atom;
+    mbar_off = (dec_off + (uint32_t)sizeof(DecodeShared) + 15u) & ~15u;
+    holder_off = mbar_off + 8;
+    bytes = holder_off + 8 + 1024;  // + slack for aligning the base
+  }
 };
-
-constexpr size_t kGemmSmem = sizeof(GemmShared) + 1024;  // + alignment slack
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, 2)
     gemm_kernel(DevBook book, const int64_t* __restrict__ idx, int n_out, int bpr, const uint16_t* __restrict__ rscale,
                 const __nv_bfloat16* __restrict__ A, int m_act, int k_in, float* __restrict__ Y, int splits,
                 int passes, int npad, int* error_flag) {
   extern __shared__ uint8_t smem_raw[];
-  GemmShared& sh = *reinterpret_cast<GemmShared*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const GemmLayout L(npad);
+  uint8_t* wt = base;
+  uint8_t* at = base + L.a_off;
+  DecodeShared& dec = *reinterpret_cast<DecodeShared*>(base + L.dec_off);
+  uint64_t* mbar_p = reinterpret_cast<uint64_t*>(base + L.mbar_off);
+  uint32_t* holder = reinterpret_cast<uint32_t*>(base + L.holder_off);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  decode_setup(book, sh.dec);
+  decode_setup(book, dec);
   if (tid == 0) {
-    sh.error = 0;
-    tc::mbar_init(tc::smem_addr(&sh.mbar), 1);
+    tc::mbar_init(tc::smem_addr(mbar_p), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   uint32_t ncols = 32;
   while ((int)ncols < npad) ncols <<= 1;
-  if (warp == 0) tc::tmem_alloc(tc::smem_addr(&sh.tmem_base), ncols);
+  if (warp == 0) tc::tmem_alloc(tc::smem_addr(holder), ncols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = sh.tmem_base;
+  const uint32_t tmem = *holder;
   const uint32_t idesc = tc::idesc_bf16_f32(kTileW, npad);
-  const uint32_t mbar = tc::smem_addr(&sh.mbar);
-  const uint32_t w_base = tc::smem_addr(&sh.w[0][0]);
-  const uint32_t a_base = tc::smem_addr(&sh.a[0][0]);
+  const uint32_t mbar = tc::smem_addr(mbar_p);
+  const uint32_t w_base = tc::smem_addr(wt);
+  const uint32_t a_base = tc::smem_addr(at);
   const float lscale = kLatticeScaleF;
 
   const int n_tiles = (n_out + kTileW - 1) / kTileW;
@@ -107,7 +117,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int gb = c * kChunkBlocks + b;
         int y[kDim];
         if (n0 + r < n_out && gb < bpr) {
-          decode_index(__ldg(idx + (int64_t)(n0 + r) * bpr + gb), book, sh.dec, y);
+          decode_index(__ldg(idx + (int64_t)(n0 + r) * bpr + gb), book, dec, y);
         } else {
 #pragma unroll
           for (int d = 0; d < kDim; ++d) y[d] = 0;
@@ -121,7 +131,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const __nv_bfloat162 h = __floats2bfloat162_rn((float)y[q * 8 + 2 * e], (float)y[q * 8 + 2 * e + 1]);
             pk[e] = *reinterpret_cast<const uint32_t*>(&h);
           }
-          *reinterpret_cast<uint4*>(&sh.w[kk >> 6][swz(r, (kk & 63) >> 3)]) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(wt + (kk >> 6) * (kTileW * 128) + swz(r, (kk & 63) >> 3)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
       // activations: npad rows x 192 columns (zero outside [0, m_act) x [0, k_in))
@@ -131,7 +142,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint4 val = make_uint4(0, 0, 0, 0);
         if (m0 + m < m_act && kg < k_in)
           val = __ldg(reinterpret_cast<const uint4*>(A + (int64_t)(m0 + m) * k_in + kg));
-        *reinterpret_cast<uint4*>(&sh.a[kc >> 3][swz(m, kc & 7)]) = val;
+        *reinterpret_cast<uint4*>(at + (kc >> 3) * L.a_atom + swz(m, kc & 7)) = val;
       }
       tc::fence_proxy_async();
       __syncthreads();
@@ -142,7 +153,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int k = ks * 16;
           const uint32_t off = (uint32_t)((k & 63) * 2);
           const uint64_t ad = tc::desc_sw128(w_base + (uint32_t)(k >> 6) * (kTileW * 128) + off);
-          const uint64_t bd = tc::desc_sw128(a_base + (uint32_t)(k >> 6) * (kMaxAct * 128) + off);
+          const uint64_t bd = tc::desc_sw128(a_base + (uint32_t)(k >> 6) * L.a_atom + off);
           tc::mma_bf16(tmem, ad, bd, idesc, (c > c_begin || ks > 0) ? 1u : 0u);
         }
         tc::commit(mbar);
@@ -193,7 +204,8 @@ cudaError_t gemm_launch(const Codebook& cb, const int64_t* idx, int64_t n_out, i
     int dev;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)GemmLayout(kMaxAct).bytes);
     if (e != cudaSuccess) return e;
     configured = true;
   }
@@ -202,14 +214,19 @@ cudaError_t gemm_launch(const Codebook& cb, const int64_t* idx, int64_t n_out, i
   const int npad = std::max(16, (rows_last + 15) / 16 * 16);
   const int n_tiles = (int)((n_out + kTileW - 1) / kTileW);
   const int chunks = (int)((bpr + kChunkBlocks - 1) / kChunkBlocks);
-  int splits = std::max(1, std::min(chunks, (sms + n_tiles * passes - 1) / (n_tiles * passes)));
+  const GemmLayout L(npad);
+  int per_sm = 1;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_kernel, kGemmThreads, L.bytes);
+  per_sm = std::max(1, per_sm);
+  const int slots = sms * per_sm;
+  int splits = std::max(1, std::min(chunks, (slots + n_tiles * passes - 1) / (n_tiles * passes)));
   if (splits > 1) {
     cudaError_t e = cudaMemsetAsync(y, 0, (size_t)m * (size_t)n_out * sizeof(float), stream);
     if (e != cudaSuccess) return e;
   }
   const int items = n_tiles * splits * passes;
-  const int grid = std::min(items, sms);
-  gemm_kernel<<<grid, kGemmThreads, kGemmSmem, stream>>>(cb.dev, idx, (int)n_out, (int)bpr, rscale,
+  const int grid = std::min(items, slots);
+  gemm_kernel<<<grid, kGemmThreads, L.bytes, stream>>>(cb.dev, idx, (int)n_out, (int)bpr, rscale,
                                                         static_cast<const __nv_bfloat16*>(a), (int)m, (int)k, y,
                                                         splits, passes, npad, error_flag);
   return cudaGetLastError();

@@ -6,11 +6,19 @@
 // the per-class splits by reciprocal multiplication with an exact correction,
 // then one 24-step lexicographic unranking loop shared by both parities (an
 // even class unranks its |v| = 2 mod 4 part, then its |v| = 0 mod 4 part), so
-// warps holding both parities do not diverge there.  Each step finds the value
-// whose branch holds the rank, with branch = N * count / remaining computed
-// exactly: a shift by the power of two of `remaining` and a multiply by the
-// inverse of its odd part (modulo 2^32 once the multinomial N fits 32 bits,
-// modulo 2^64 before).  Then the signs.
+// warps holding both parities do not diverge there.  Lexicographic
+// unranking picks, at each step, the value whose branch [N*C_{j-1}/rem,
+// N*C_j/rem) holds the rank (C = cumulative counts, N the multinomial of
+// what remains, rem the positions left), i.e. the bucket of
+// t = floor(rank * rem / N) among the cumulative counts.  Once N fits 32
+// bits, t is estimated in fp32, the bucket found with a byte-wise compare of
+// the packed cumulative counts, and the choice verified exactly with two
+// 32x32->64 products (a miss, at an fp32 rounding boundary, is stepped to
+// the neighbouring bucket).  The new rank and N are exact divisions by rem:
+// a shift by its power of two and a multiply by the inverse of its odd part
+// (mod 2^32).  Larger N (the first steps of the largest classes) use the
+// 64-bit branch-by-branch scan.  Even-class signs use the closed form of
+// rank_even_signs (llvq_device.cuh) inside the scatter loop.
 #pragma once
 
 #include <cstdint>
@@ -62,7 +70,7 @@ __device__ __forceinline__ uint32_t unrank_step(uint64_t& rank, uint64_t& N, uin
                                                 const DecodeShared& sh) {
   const uint32_t s = sh.shift[rem];
   uint32_t j = 0;
-  if (N >> 32) {
+  if (N >> 32) {  // 64-bit branch-by-branch scan (first steps of the largest classes only)
     const uint64_t inv = sh.inv[rem];
     for (; j < kMaxVals; ++j) {
       const uint64_t c = byte_at(cnt, j);
@@ -71,29 +79,36 @@ __device__ __forceinline__ uint32_t unrank_step(uint64_t& rank, uint64_t& N, uin
       if (rank < br) { N = br; break; }
       rank -= br;
     }
-  } else {
-    const uint32_t inv = (uint32_t)sh.inv[rem];
-    uint32_t r = (uint32_t)rank, n32 = (uint32_t)N;
-    // The smallest remaining value (tried last) is usually the most frequent
-    // one: test its branch, the top of the rank range, first.
-    const uint32_t last = (uint32_t)(63 - __clzll((long long)cnt)) >> 3;
-    const uint32_t blast = (uint32_t)(((uint64_t)n32 * byte_at(cnt, last)) >> s) * inv;
-    if (r >= n32 - blast) {
-      rank = r - (n32 - blast);
-      N = blast;
-      cnt -= 1ull << (8 * last);
-      return last;
-    }
-    for (; j < kMaxVals; ++j) {
-      const uint32_t c = byte_at(cnt, j);
-      if (!c) continue;
-      const uint32_t br = (uint32_t)(((uint64_t)n32 * c) >> s) * inv;
-      if (r < br) { n32 = br; break; }
-      r -= br;
-    }
-    rank = r;
-    N = n32;
+    cnt -= 1ull << (8 * j);
+    return j;
   }
+  const uint32_t inv = (uint32_t)sh.inv[rem];
+  const uint32_t r = (uint32_t)rank, n32 = (uint32_t)N;
+  const uint64_t cum = cnt * 0x0101010101010101ull;  // byte i = c_0 + ... + c_i (sums <= 24)
+  const float q = __fmul_rn(__uint2float_rn(r), __fmul_rn((float)rem, __frcp_rn(__uint2float_rn(n32))));
+  uint32_t t = min((uint32_t)q, (uint32_t)rem - 1u);
+  const uint32_t tb = t * 0x01010101u;
+  j = (__popc(__vcmpleu4((uint32_t)cum, tb)) + __popc(__vcmpleu4((uint32_t)(cum >> 32), tb))) >> 3;
+  const uint64_t x = (uint64_t)r * (uint32_t)rem;
+  uint64_t lo = (uint64_t)n32 * ((uint32_t)((cum << 8) >> (8 * j)) & 0xFFu);
+  uint32_t c = byte_at(cnt, j);
+  uint64_t hi = lo + (uint64_t)n32 * c;
+  // fp32 estimate landed in a neighbouring bucket: step to it (at most 8
+  // buckets exist; j stays in [0, 7])
+  for (int guard = 0; (x < lo || x >= hi) && guard < 2 * kMaxVals; ++guard) {
+    if (x < lo) {
+      if (j == 0) break;
+      --j;
+    } else {
+      if (j == kMaxVals - 1) break;
+      ++j;
+    }
+    c = byte_at(cnt, j);
+    lo = (uint64_t)n32 * ((uint32_t)((cum << 8) >> (8 * j)) & 0xFFu);
+    hi = lo + (uint64_t)n32 * c;
+  }
+  rank = (uint32_t)((x - lo) >> s) * inv;
+  N = (uint32_t)(((uint64_t)n32 * c) >> s) * inv;
   cnt -= 1ull << (8 * j);
   return j;
 }
@@ -156,19 +171,46 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, con
       if (t < 16) seq_lo |= (uint64_t)j << (4 * t);
       else seq_hi |= (uint64_t)j << (4 * (t - 16));
     }
-    int i0 = 0, i1 = 0;
+    // scatter: odd -> step d at position d; even -> the word's positions take
+    // the first (f1) part in order, the others the second (f0) part
+    uint32_t nzmask = 0;
 #pragma unroll
     for (int d = 0; d < kDim; ++d) {
       const bool bit = (word >> d) & 1u;
       const bool part1 = !odd && bit;
-      const int t = odd ? d : (bit ? i1 : nfirst + i0);
+      const int below1 = __popc(word & ((1u << d) - 1u));
+      const int t = odd ? d : (bit ? below1 : nfirst + d - below1);
       const uint32_t nib = (uint32_t)((t < 16 ? seq_lo >> (4 * t) : seq_hi >> (4 * (t - 16))) & 15u);
       const int m = (int)byte_at(part1 ? pv1 : pv0, (int)nib);
-      i1 += part1;
-      i0 += !odd && !bit;
+      nzmask |= (uint32_t)(m != 0) << d;
       y[d] = odd ? (((m & 3) == (bit ? 3 : 1)) ? m : -m) : m;
     }
-    if (!odd) ok = unrank_even_signs(y, sign, (meta >> 19) & 1);
+    if (!odd) {
+      // signs: insert, at the first word coordinate, the bit that gives the
+      // class's parity of negative word coordinates (weight 0: rank = mask)
+      const int nz = __popc(nzmask);
+      uint32_t cmask;
+      if (word) {
+        const int p = __popc(nzmask & ((word & (0u - word)) - 1u));
+        const uint32_t rr = (uint32_t)sign;
+        ok = (sign >> (nz - 1)) == 0;
+        cmask = ((rr >> p) << (p + 1)) | (rr & ((1u << p) - 1u));
+      } else {
+        ok = nz >= 32 || (sign >> nz) == 0;
+        cmask = (uint32_t)sign;
+      }
+      uint32_t neg = 0;
+      int ci = 0;
+#pragma unroll
+      for (int d = 0; d < kDim; ++d) {
+        const bool nzd = (nzmask >> d) & 1u;
+        neg |= (nzd ? (cmask >> ci) & 1u : 0u) << d;
+        ci += nzd;
+      }
+      if (word && (__popc(neg & word) & 1) != (int)((meta >> 19) & 1)) neg ^= word & (0u - word);
+#pragma unroll
+      for (int d = 0; d < kDim; ++d) y[d] = ((neg >> d) & 1u) ? -y[d] : y[d];
+    }
   }
   if (!ok) {
 #pragma unroll
