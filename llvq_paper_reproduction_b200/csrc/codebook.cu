@@ -33,6 +33,7 @@ int fail(int status, const std::string& msg) {
 }
 
 int cuda_fail(cudaError_t e, const char* where) {
+  if (e == cudaErrorMemoryAllocation) return fail(LLVQ_ERR_OUT_OF_MEMORY, std::string(where) + ": out of device memory");
   return fail(LLVQ_ERR_CUDA, std::string(where) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
 }
 
@@ -360,6 +361,10 @@ int upload(llvq::Codebook& cb, int device) {
   return LLVQ_OK;
 }
 
+// Decoded-weight staging of the large-batch GEMM: 32 MiB keeps a chunk of
+// bf16 weights resident in L2 while every activation tile streams over it.
+constexpr int64_t kGemmStagingBudget = 32ll << 20;
+
 // Runs `fn` with the codebook's device current, restoring the caller's device.
 template <class F>
 int on_device(const llvq_codebook* h, F&& fn) {
@@ -471,8 +476,18 @@ int llvq_gemm(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int
   if (m > (int64_t)INT32_MAX || n_out > (int64_t)INT32_MAX || blocks_per_row > (int64_t)INT32_MAX)
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
   return on_device(h, [&] {
-    return llvq::gemm_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
-                             (cudaStream_t)stream);
+    if (m <= llvq::kGemmFusedMaxM)
+      return llvq::gemm_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
+                               (cudaStream_t)stream);
+    // stream-ordered staging buffer, released on the same stream after the GEMM
+    const int64_t bytes = llvq::gemm_staging_bytes(n_out, blocks_per_row, kGemmStagingBudget);
+    void* staging = nullptr;
+    cudaError_t e = cudaMallocAsync(&staging, (size_t)bytes, (cudaStream_t)stream);
+    if (e != cudaSuccess) return e;
+    e = llvq::gemm_staged_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
+                                 staging, bytes, (cudaStream_t)stream);
+    const cudaError_t ef = cudaFreeAsync(staging, (cudaStream_t)stream);
+    return e != cudaSuccess ? e : ef;
   });
 }
 

@@ -62,6 +62,48 @@ __global__ void __launch_bounds__(kDeqThreads) dequant_kernel(const int64_t* __r
   }
 }
 
+// Weight staging for the large-batch GEMM: indices [rows, bpr] -> bf16
+// integer codewords [rows, ldw] (columns >= 24 * bpr zero), one thread per
+// (row, block) plus the padding.
+__global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(const int64_t* __restrict__ index, int rows,
+                                                                       int bpr, int ldw, DevBook book,
+                                                                       __nv_bfloat16* __restrict__ out) {
+  __shared__ DecodeShared sh;
+  decode_setup(book, sh);
+  __syncthreads();
+  const int per_row = ldw / kDim + 1;  // bpr blocks, then zero padding of the row tail
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)rows * per_row) return;
+  const int r = (int)(i / per_row), b = (int)(i % per_row);
+  __nv_bfloat16* o = out + (int64_t)r * ldw;
+  if (b < bpr) {
+    int y[kDim];
+    decode_index(__ldg(index + (int64_t)r * bpr + b), book, sh, y);
+    uint4* dst = reinterpret_cast<uint4*>(o + b * kDim);
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn((float)y[q * 8 + 2 * e], (float)y[q * 8 + 2 * e + 1]);
+        pk[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      dst[q] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  } else if (b == bpr) {
+    for (int c = bpr * kDim; c < ldw; c += 8) *reinterpret_cast<uint4*>(o + c) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+cudaError_t decode_rows_bf16_launch(const Codebook& cb, const int64_t* index, int rows, int bpr, int ldw, void* out,
+                                    cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const int64_t n = (int64_t)rows * (ldw / kDim + 1);
+  decode_rows_bf16_kernel<<<(unsigned)((n + kDeqThreads - 1) / kDeqThreads), kDeqThreads, 0, stream>>>(
+      index, rows, bpr, ldw, cb.dev, static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
 cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t n, void* out, int kind,
                               const uint16_t* row_scale, int64_t blocks_per_row, int* error_count,
                               cudaStream_t stream) {

@@ -32,8 +32,12 @@ def rel_err(y, ref):
     return float(torch.linalg.norm(y - ref) / torch.linalg.norm(ref))
 
 
+# batches above 256 rows take the staged path (decode to bf16, then a
+# pipelined GEMM); (300, 2500, 598, 14336) stages the weights in 3 row chunks
 @pytest.mark.parametrize("m_act,n,bpr,k", [(1, 128, 8, 192), (8, 300, 20, 472), (64, 256, 171, 4096),
-                                           (200, 130, 25, 600), (300, 257, 9, 216), (16, 1024, 598, 14336)])
+                                           (200, 130, 25, 600), (256, 200, 12, 288), (300, 257, 9, 216),
+                                           (16, 1024, 598, 14336), (513, 384, 171, 4096), (300, 2500, 598, 14336),
+                                           (1100, 131, 3, 56)])
 def test_gemm_matches_dequantize_matmul(m_act, n, bpr, k):
     q = api()
     g = torch.Generator(device="cuda").manual_seed(4)
