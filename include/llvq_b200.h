@@ -94,9 +94,12 @@ int llvq_dequantize_bf16(const llvq_codebook* cb, const int64_t* indices, int64_
  * the dequantized indices[n * blocks_per_row + b] (b = 0 .. blocks_per_row-1,
  * 24 columns each) times row_scale[n] (fp16 bits; NULL means 1).  a: bf16
  * [m, k] row-major, 16-byte aligned, k % 8 == 0, k <= 24 * blocks_per_row
- * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  Weights are
- * decoded straight into shared memory and multiplied on the tcgen05 tensor
- * cores with fp32 accumulation; they are never written to global memory.
+ * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  Up to 256
+ * activation rows the weights are decoded straight into shared memory and
+ * multiplied on the tcgen05 tensor cores with fp32 accumulation, never
+ * written to global memory.  Above 256 rows they are decoded chunk by chunk
+ * into a bf16 staging buffer (about 32 MiB, cudaMallocAsync/cudaFreeAsync on
+ * `stream`) that a pipelined tcgen05 GEMM reads from L2.
  * *error_flag (device int, may be NULL) is set to 1 if a tensor-core wait
  * timed out.  No reference counterpart (the reference has no GEMM). */
 int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
