@@ -106,6 +106,27 @@ int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, in
               const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
               int32_t* error_flag, void* stream);
 
+/* llvq_gemm without device allocation.  No counterpart in the reference.
+ * For callers that may not allocate device memory while they run (a serving
+ * engine that reserved the GPU's memory for its own pool, a step that must not
+ * fail on out-of-memory halfway): batches above 256 rows stage the decoded
+ * weights in a fixed LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 MiB) array compiled
+ * into the library, one per device, instead of a cudaMallocAsync buffer;
+ * smaller batches take llvq_gemm's fused kernel, which uses no staging.
+ * Same arguments, results and error flag as llvq_gemm, plus the limit
+ * blocks_per_row <= LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW (2730: one 128-row
+ * tile of rows up to 65536 columns fits the array); wider rows return
+ * LLVQ_ERR_INVALID_ARGUMENT.  The array needs no initial contents.  The first
+ * call on each device does one-time setup (looks up the array's address with
+ * cudaGetSymbolAddress, sets the kernels' shared-memory attributes) and should
+ * come before any stream capture.  Calls that overlap on one device (unordered
+ * streams, concurrent host threads) share the array and race: order them. */
+#define LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 << 20)
+#define LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW 2730
+int llvq_gemm_noalloc(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
+                      const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
+                      int32_t* error_flag, void* stream);
+
 /* Seeded random Hadamard rotation of each row of a [rows, cols] matrix, in
  * segments of `block` columns (a power of two, <= 4096, dividing cols):
  * forward out = H (signs * in) / sqrt(block), inverse out = signs * (H in) /

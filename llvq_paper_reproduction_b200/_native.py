@@ -35,7 +35,7 @@ EXPORTS = (
     "llvq_codebook_create", "llvq_codebook_destroy", "llvq_codebook_info", "llvq_quantize", "llvq_quantize_ex",
     "llvq_dequantize_lattice", "llvq_dequantize", "llvq_dequantize_bf16", "llvq_codeword_host",
     "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version", "llvq_gemm",
-    "llvq_hadamard",
+    "llvq_hadamard", "llvq_gemm_noalloc",
 )
 
 _lib = None
@@ -64,6 +64,7 @@ def load() -> ctypes.CDLL:
             "llvq_dequantize": (ctypes.c_int, [vp, vp, i64, vp, i32, vp, vp]),
             "llvq_dequantize_bf16": (ctypes.c_int, [vp, vp, i64, vp, i64, vp, vp, vp]),
             "llvq_gemm": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
+            "llvq_gemm_noalloc": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_hadamard": (ctypes.c_int, [vp, i32, vp, i64, i64, i32, vp, i32, vp]),
             "llvq_codeword_host": (ctypes.c_int, [vp, i64, vp]),
             "llvq_encode_host": (ctypes.c_int, [vp, vp, P(i64)]),
@@ -159,6 +160,13 @@ class NativeCodebook:
              y_ptr: int, err_ptr: int | None, stream: int) -> None:
         check(self._lib.llvq_gemm(self.handle, idx_ptr, n_out, blocks_per_row, scale_ptr, a_ptr, m, k, y_ptr, err_ptr,
                                   stream), "llvq_gemm")
+
+    def gemm_noalloc(self, idx_ptr: int, n_out: int, blocks_per_row: int, scale_ptr: int | None, a_ptr: int, m: int,
+                     k: int, y_ptr: int, err_ptr: int | None, stream: int) -> None:
+        """llvq_gemm with a static 16 MiB staging array per device instead of a
+        stream-ordered allocation (blocks_per_row <= 2730)."""
+        check(self._lib.llvq_gemm_noalloc(self.handle, idx_ptr, n_out, blocks_per_row, scale_ptr, a_ptr, m, k, y_ptr,
+                                          err_ptr, stream), "llvq_gemm_noalloc")
 
     def dequantize_bf16(self, idx_ptr: int, n: int, scale_ptr: int, blocks_per_row: int, out_ptr: int,
                         err_ptr: int | None, stream: int) -> None:

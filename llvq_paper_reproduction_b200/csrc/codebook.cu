@@ -491,6 +491,35 @@ int llvq_gemm(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int
   });
 }
 
+static_assert(LLVQ_GEMM_NOALLOC_STAGING_BYTES == llvq::kNoAllocStagingBytes, "staging size mismatch");
+static_assert(128 * ((24 * LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW + 63) / 64 * 64) * 2 <= llvq::kNoAllocStagingBytes,
+              "one 128-row tile of the widest rows must fit the static staging buffer");
+
+int llvq_gemm_noalloc(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
+                      const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
+                      int32_t* error_flag, void* stream) {
+  if (m < 0 || n_out < 0 || blocks_per_row <= 0 || k <= 0 || k % 8 || k > 24 * blocks_per_row)
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes: need k % 8 == 0 and 0 < k <= 24 * blocks_per_row");
+  if (blocks_per_row > LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW)
+    return fail(LLVQ_ERR_INVALID_ARGUMENT,
+                "gemm_noalloc: blocks_per_row > 2730 (rows wider than 65536 columns) does not fit the 16 MiB "
+                "static staging buffer; use llvq_gemm");
+  if (m > 0 && n_out > 0 && (!indices || !a_bf16 || !y || (reinterpret_cast<uintptr_t>(a_bf16) & 15)))
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm pointers: null, or activations not 16-byte aligned");
+  if (m > (int64_t)INT32_MAX || n_out > (int64_t)INT32_MAX)
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
+  return on_device(h, [&] {
+    void* staging = nullptr;
+    cudaError_t e = llvq::noalloc_staging(&staging);  // first call on a device: symbol lookup
+    if (e != cudaSuccess) return e;
+    if (m <= llvq::kGemmFusedMaxM)
+      return llvq::gemm_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
+                               (cudaStream_t)stream);
+    return llvq::gemm_staged_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
+                                    error_flag, staging, llvq::kNoAllocStagingBytes, (cudaStream_t)stream);
+  });
+}
+
 int llvq_hadamard(const void* in, int32_t in_is_half, float* out, int64_t rows, int64_t cols, int32_t block,
                   const int8_t* signs, int32_t inverse, void* stream) {
   if (rows < 0 || cols <= 0 || block < 1 || block > 4096 || (block & (block - 1)) || cols % block)

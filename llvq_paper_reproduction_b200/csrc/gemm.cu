@@ -344,6 +344,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, kMaxAct);
 }
 
+// Sets the dynamic shared-memory limits of both GEMM kernels on the current
+// device (the launchers also do this lazily on their first launch).
+cudaError_t gemm_configure_device() {
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)GemmLayout(kMaxAct).bytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(gemm_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmem);
+}
+
 int64_t gemm_staging_ldw(int64_t bpr) { return (24 * bpr + 63) / 64 * 64; }
 
 int64_t gemm_staging_bytes(int64_t n_out, int64_t bpr, int64_t budget) {

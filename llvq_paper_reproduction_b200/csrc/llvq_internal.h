@@ -70,6 +70,12 @@ cudaError_t gemm_staged_launch(const Codebook& cb, const int64_t* idx, int64_t n
                                const uint16_t* rscale, const void* a, int64_t m, int64_t k, float* y,
                                int* error_flag, void* staging, int64_t staging_bytes, cudaStream_t stream);
 
+// Static staging for the no-allocation GEMM entry point: 16 MiB per device,
+// enough for one 128-row tile of rows up to 65536 columns.
+constexpr int64_t kNoAllocStagingBytes = 16ll << 20;
+cudaError_t noalloc_staging(void** ptr);
+cudaError_t gemm_configure_device();
+
 cudaError_t hadamard_launch(const void* in, int in_is_half, float* out, int64_t rows, int64_t cols, int block,
                             const int8_t* signs, int inverse, cudaStream_t stream);
 

@@ -1,0 +1,81 @@
+"""llvq_gemm_noalloc (static staging array, no device allocation) against
+llvq_gemm (stream-ordered staging allocation) on the same inputs.
+
+Above 256 activation rows both run the staged kernels with the same k order
+per output element, so the outputs are compared bit for bit.  Up to 256 rows
+both take the fused kernel, which adds split-K partial sums with atomics in
+no fixed order, so there the outputs agree to fp32 rounding (relative
+Frobenius distance <= 1e-6).  Two calls in a row with different weights check
+that nothing of the first call's staging survives into the second.
+The file name sorts last so the suite also runs it after every other test
+has used the device.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+MAX_BPR = 2730  # LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW
+FUSED_MAX_M = 256  # batches up to this size use the fused kernel (no staging)
+
+
+def _quantizer():
+    from llvq_paper_reproduction_b200 import LeechLatticeVectorQuantizerGpu
+
+    return LeechLatticeVectorQuantizerGpu(max_shell=13, use_cache=False, device="cuda")
+
+
+def _case(q, m, n, bpr, k, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    idx = torch.randint(0, q.total_count, (n, bpr), generator=g, device="cuda")
+    a = torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16)
+    scale = (torch.rand(n, generator=g, device="cuda") * 0.04 + 0.005).to(torch.float16)
+    return idx, a, scale
+
+
+def _run(q, fn_name, idx, a, scale):
+    m, k = a.shape
+    n, bpr = idx.shape
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    err = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    getattr(q._book(), fn_name)(idx.data_ptr(), n, bpr, scale.data_ptr(), a.data_ptr(), m, k, y.data_ptr(),
+                                err.data_ptr(), stream)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return y
+
+
+# (m, n, bpr, k): staged batches (m > 256), one with weights wider than the
+# 16 MiB array holds at once (K = 14336: 512 rows per chunk, 3 chunks), and a
+# fused-kernel batch (m <= 256, no staging).
+CASES = [(300, 1300, 598, 14336), (513, 384, 171, 4096), (1100, 131, 3, 56), (64, 256, 171, 4096)]
+
+
+@pytest.mark.parametrize("m,n,bpr,k", CASES)
+def test_noalloc_matches_gemm_two_calls(m, n, bpr, k):
+    q = _quantizer()
+    first = _case(q, m, n, bpr, k, seed=11)
+    second = _case(q, m, n, bpr, k, seed=12)
+    ref1 = _run(q, "gemm", *first)
+    ref2 = _run(q, "gemm", *second)
+    out1 = _run(q, "gemm_noalloc", *first)
+    out2 = _run(q, "gemm_noalloc", *second)
+    for out, ref in ((out1, ref1), (out2, ref2)):
+        if m > FUSED_MAX_M:
+            assert torch.equal(out, ref)
+        else:
+            assert float(torch.linalg.norm(out - ref) / torch.linalg.norm(ref)) <= 1e-6
+    assert not torch.equal(out1, out2)
+
+
+def test_noalloc_widest_rows_accepted_and_wider_rejected():
+    q = _quantizer()
+    idx, a, scale = _case(q, 260, 130, MAX_BPR, 24 * MAX_BPR, seed=13)
+    assert torch.equal(_run(q, "gemm_noalloc", idx, a, scale), _run(q, "gemm", idx, a, scale))
+    wide = torch.zeros((4, MAX_BPR + 1), dtype=torch.long, device="cuda")
+    a = torch.zeros((300, 64), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="2730"):
+        _run(q, "gemm_noalloc", wide, a, torch.ones(4, dtype=torch.float16, device="cuda"))
