@@ -286,6 +286,8 @@ def run_gpu_arm(args) -> None:
         extra["dequant"] = dequant_bench(q, device, stream, args)
     if rank == 0 and world == 1 and not args.skip_gemm:
         extra["gemm"] = gemm_bench(q, device, stream, args)
+    if rank == 0 and world == 1 and args.sweep_rows > 0:
+        extra["rate_sweep"] = rate_sweep_bench(q, x, device, stream, args)
     cpu = None
     if rank == 0 and world == 1 and args.cpu_sample > 0:
         sample = x_host[: args.cpu_sample].numpy()
@@ -323,6 +325,58 @@ def run_gpu_arm(args) -> None:
         line["cpu_baseline"] = cpu
     line.update(extra)
     print(json.dumps(line), flush=True)
+
+
+def rate_sweep_bench(q, x, device, stream, args) -> dict:
+    """Shape-gain quantization of the same N(0,1) blocks at 1.0 ... 3.0
+    bits/dim (single shell + chi(24)-matched gain code, shaping.rate_split)
+    and the spherical-shaping variant at 2 bits/dim (shells 2..13 ball, global
+    beta): blocks/s of the full quantize call (shape search, gain, index
+    packing) on a sample of the batch, and SQNR in dB of the reconstruction.
+    The sample is the first --sweep-rows blocks, cut so that one rate takes
+    about 10 s when its search is slow (the 2.5 and 3.0 bits/dim shells 23
+    and 32 run the table-driven search)."""
+    import math
+
+    import torch
+
+    from llvq_paper_reproduction_b200.shaping import ShapeGainQuantizer, SphericalShaping
+
+    def timed(fn, rows):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        out = fn(rows)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return out, e0.elapsed_time(e1) / 1000.0
+
+    def sqnr_db(xs, rec):
+        err = (xs.double() - rec.double()).pow(2).sum().item()
+        return 10.0 * math.log10(xs.double().pow(2).sum().item() / err)
+
+    out = {}
+    probe = x[:65536]
+
+    def run(name, quant, dequant, bits):
+        quant(probe[:4096])  # codebook upload and first-launch setup
+        _, t_probe = timed(lambda r: quant(r), probe)
+        rows = int(min(args.sweep_rows, x.shape[0], max(65536, 10.0 / max(t_probe / probe.shape[0], 1e-12))))
+        xs = x[:rows]
+        idx, t = timed(lambda r: quant(r), xs)
+        out[name] = {"bits_per_dim": bits, "blocks": rows, "blocks_per_s": rows / t,
+                     "sqnr_db": sqnr_db(xs, dequant(idx).reshape(xs.shape))}
+
+    for rate in (1.0, 1.5, 2.0, 2.5, 3.0):
+        sg = ShapeGainQuantizer.for_rate(rate, device=device)
+        # (shape, gain) index pairs: 3.0 bits/dim needs 72 bits
+        run(f"shape_gain_{rate}", sg.quantize_parts, lambda p, sg=sg: sg.dequantize_parts(*p), sg.bits / 24)
+        out[f"shape_gain_{rate}"].update({"shell": sg.shell, "gain_bits": sg.gain_bits})
+        del sg
+    sph = SphericalShaping(q)
+    run("spherical_2.0", sph.quantize, sph.dequantize, q.shape_bits / 24)
+    out["spherical_2.0"]["beta"] = sph.beta
+    return {"workload": "the first blocks of the same N(0,1) batch (seed 1); blocks/s of the whole quantize call "
+                        "(search + gain code + packing), SQNR = 10 log10(|x|^2 / |x - x_hat|^2)", "by_rate": out}
 
 
 def dequant_bench(q, device, stream, args) -> dict:
@@ -429,6 +483,8 @@ def main():
     ap.add_argument("--skip-dequant", action="store_true")
     ap.add_argument("--dequant-layers", type=int, default=32)
     ap.add_argument("--skip-gemm", action="store_true")
+    ap.add_argument("--sweep-rows", type=int, default=4_194_304,
+                    help="blocks of the rate sweep sample (0 skips the sweep)")
     ap.add_argument("--gemm-m", type=int, nargs="+", default=[1, 8, 64, 512, 4096])
     args = ap.parse_args()
     if args.impl == "reference":

@@ -28,10 +28,11 @@ INCLUDE = PKG.parent / "include"
 # Codebooks with generated search code: name, min shell, max shell.
 # 2..13 is the reference's 48-bit (2 bits/dim) codebook; 2..4 a small
 # codebook for fast parity tests of the generated path; single shells 2, 5,
-# 11 and 13 are the shape codebooks of the shape-gain quantizer (1, 1.5 and
-# 2 bits/dim; 13 is the largest shell that fits 48 bits).  Other codebooks
-# run the table-driven chains.
-SPECS = (("m2_4", 2, 4), ("m2_13", 2, 13), ("s2", 2, 2), ("s5", 5, 5), ("s11", 11, 11), ("s13", 13, 13))
+# 11, 23 and 32 are the shape codebooks of the shape-gain quantizer (1, 1.5,
+# 2, 2.5 and 3 bits/dim) and 13 is the largest shell that fits 48 bits.
+# Other codebooks run the table-driven chains.
+SPECS = (("m2_4", 2, 4), ("m2_13", 2, 13), ("s2", 2, 2), ("s5", 5, 5), ("s11", 11, 11), ("s13", 13, 13),
+         ("s23", 23, 23), ("s32", 32, 32))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",

@@ -168,23 +168,40 @@ class ShapeGainQuantizer:
     def bits(self) -> int:
         return self.shape.shape_bits + self.gain_bits
 
-    def quantize(self, x: torch.Tensor, row_sigma: torch.Tensor | None = None) -> torch.Tensor:
-        """x [..., 24] -> combined int64 indices.  row_sigma (broadcast to
-        x[..., 0]) rescales the gain code per block, e.g. per weight row."""
+    def quantize_parts(self, x: torch.Tensor,
+                       row_sigma: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """x [..., 24] -> (shape index, gain index), both int64.  row_sigma
+        (broadcast to x[..., 0]) rescales the gain code per block, e.g. per
+        weight row."""
         x = x.to(device=self.shape.device, dtype=torch.float32)
         sidx = self.shape.quantize(x)
         u = self.shape.dequantize(sidx) / self.norm
         g = (x * u).sum(-1)
         if row_sigma is not None:
             g = g / row_sigma
-        gidx = torch.bucketize(g.contiguous(), self.thresholds)
+        return sidx, torch.bucketize(g.contiguous(), self.thresholds)
+
+    def dequantize_parts(self, sidx: torch.Tensor, gidx: torch.Tensor,
+                         row_sigma: torch.Tensor | None = None) -> torch.Tensor:
+        g = self.levels[gidx.to(self.shape.device)]
+        if row_sigma is not None:
+            g = g * row_sigma
+        return self.shape.dequantize(sidx.to(self.shape.device)) * (g / self.norm).unsqueeze(-1)
+
+    def quantize(self, x: torch.Tensor, row_sigma: torch.Tensor | None = None) -> torch.Tensor:
+        """x [..., 24] -> combined int64 indices shape * 2^b + gain.  Rates
+        whose index exceeds 63 bits (3.0 bits/dim: 62 + 10) raise ValueError;
+        use quantize_parts for them."""
+        self._check_packable()
+        sidx, gidx = self.quantize_parts(x, row_sigma)
         return sidx * (1 << self.gain_bits) + gidx
 
     def dequantize(self, indices: torch.Tensor, row_sigma: torch.Tensor | None = None) -> torch.Tensor:
+        self._check_packable()
         indices = indices.to(self.shape.device)
-        gidx = indices & ((1 << self.gain_bits) - 1)
-        sidx = indices >> self.gain_bits
-        g = self.levels[gidx]
-        if row_sigma is not None:
-            g = g * row_sigma
-        return self.shape.dequantize(sidx) * (g / self.norm).unsqueeze(-1)
+        return self.dequantize_parts(indices >> self.gain_bits, indices & ((1 << self.gain_bits) - 1), row_sigma)
+
+    def _check_packable(self) -> None:
+        if self.bits > 63:
+            raise ValueError(f"a {self.bits}-bit shape-gain index does not fit int64; use quantize_parts / "
+                             "dequantize_parts")

@@ -85,3 +85,31 @@ def test_gpu_shape_gain_roundtrip():
     assert torch.equal(again >> sg.gain_bits, idx >> sg.gain_bits)
     mse = float((x - recon).pow(2).mean())
     assert mse < 0.2  # 2 bits/dim on a unit Gaussian
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rate", [1.0, 1.5, 2.0, 2.5, 3.0])
+def test_gpu_shape_gain_every_rate_matches_oracle(rate):
+    """Shape search of every rate's single shell against the oracle search
+    restricted to that shell, then the combined index round trip."""
+    from llvq_paper_reproduction_b200.shaping import ShapeGainQuantizer
+    from oracle.oracle import OracleBook
+
+    sg = ShapeGainQuantizer.for_rate(rate)
+    x = torch.randn((48, 24), generator=torch.Generator().manual_seed(int(rate * 10))).float()
+    sidx = sg.shape.quantize(x.cuda()).cpu().numpy()
+    book = OracleBook(sg.shell, min_shell=sg.shell)
+    ref, _, _, _ = book.quantize_batch(x.numpy(), threads=8)
+    np.testing.assert_array_equal(sidx, ref)
+    s2, g2 = sg.quantize_parts(x.cuda())
+    assert torch.equal(s2.cpu(), torch.from_numpy(ref))
+    assert int(g2.min()) >= 0 and int(g2.max()) < (1 << sg.gain_bits)
+    recon = sg.dequantize_parts(s2, g2)
+    assert recon.shape == x.shape and bool(torch.isfinite(recon).all())
+    if sg.bits <= 63:
+        idx = sg.quantize(x.cuda())
+        assert int(idx.min()) >= 0 and int(idx.max()) < (1 << sg.bits)
+        assert torch.equal(sg.dequantize(idx), recon)
+    else:
+        with pytest.raises(ValueError):
+            sg.quantize(x.cuda())
