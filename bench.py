@@ -12,7 +12,11 @@ bit-exact).  One step = one quantize pass over the whole batch.  Inputs
             device->host copy of the int64 indices inside the timed region.
 Secondary (rank 0, N=1): dequantizer GB/s on all Llama-3-8B linear shapes
 (291,307,520 random valid indices, seed 3, bf16 weights with fp16 per-row
-scales).
+scales); dequant-GEMM TFLOP/s on the Llama-3-8B MLP shapes at
+M = 1 ... 4096; shape-gain quantization at 1.0 ... 3.0 bits/dim and the
+spherical-shaping variant (blocks/s, SQNR).
+At every N: whole-model quantization of the Llama-2-7B-shaped linears,
+sharded by matrix over the ranks (blocks/s, plus the all-gather to rank 0).
 
 --impl reference times the reference algorithm on the host cores instead:
 the oracle's restatement of LeechLatticeVectorQuantizer.quantize (per-pair
@@ -282,6 +286,10 @@ def run_gpu_arm(args) -> None:
         raise RuntimeError("end-to-end indices differ from the device-resident run")
 
     extra = {}
+    if args.model_layers > 0:  # every rank takes part (sharded by matrix)
+        mq = model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks)
+        if rank == 0:
+            extra["model_quant"] = mq
     if rank == 0 and world == 1 and not args.skip_dequant:
         extra["dequant"] = dequant_bench(q, device, stream, args)
     if rank == 0 and world == 1 and not args.skip_gemm:
@@ -311,8 +319,8 @@ def run_gpu_arm(args) -> None:
         "config": {"workload": f"gaussian N(0,1) fp32 [{n}, 24] per GPU, seed 1+rank, shells 2..{args.max_shell} "
                                "(48-bit index), bit-exact reference quantize", "blocks_per_gpu": n,
                    "l2": "inputs (1.6 GB) larger than L2, no flush", "parallelism": f"weak x{world}"},
-        "e2e": {"value": world * n / (e2e_ms / 1000.0), "unit": "blocks/s", "h2d_bytes_per_step": n * 96,
-                "d2h_bytes_per_step": n * 8},
+        "e2e": {"value": world * n / (e2e_ms / 1000.0), "unit": "blocks/s", "h2d_bytes_per_step": world * n * 96,
+                "d2h_bytes_per_step": world * n * 8},
         "gpu_launches": 2 * args.steps,
         "roofline": {"bound": "alu", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
                      "frac": achieved / peak_tflops, "traffic": None,
@@ -325,6 +333,44 @@ def run_gpu_arm(args) -> None:
         line["cpu_baseline"] = cpu
     line.update(extra)
     print(json.dumps(line), flush=True)
+
+
+def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks) -> dict:
+    """Whole-model quantization of the Llama-2-7B-shaped linears (the first
+    --model-layers layers; seed 2): each rank quantizes its greedy share of
+    whole matrices (synthetic fp16 weights, Hadamard rotation, row scales,
+    shape-gain at 2 bits/dim) with no inter-GPU traffic, timed with CUDA
+    events on the launching stream (max over ranks); then one all-gather
+    brings every index tensor and row scale to rank 0, timed separately."""
+    import torch
+
+    from llvq_paper_reproduction_b200.model_quant import (MatrixQuantizer, MatrixSpec, gather_to_rank0,
+                                                          llama2_7b_matrices, plan_shards)
+
+    specs = llama2_7b_matrices(args.model_layers)
+    mine = plan_shards(specs, world)[rank]
+    mq = MatrixQuantizer(2.0, seed=2, device=device)
+    mq.quantize(MatrixSpec(0, "q_proj", 256, 4096))  # codebook upload and first launches
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    results = {specs[i].key: mq.quantize(specs[i]) for i in mine}
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    secs = max_over_ranks(e0.elapsed_time(e1) / 1000.0)
+    t0 = time.perf_counter()
+    local = {k: (r["indices"].cpu(), r["row_scale"].cpu()) for k, r in results.items()}
+    gathered = gather_to_rank0(specs, local, rank, world, device) if world > 1 else local
+    gather_s = max_over_ranks(time.perf_counter() - t0)
+    total = sum(s.blocks for s in specs)
+    if rank == 0 and len(gathered) != len(specs):
+        raise RuntimeError("gather lost matrices")
+    return {"workload": f"Llama-2-7B linears, {args.model_layers} layers ({len(specs)} matrices, {total} blocks), "
+                        "fp16 N(0, sigma_row^2) seed 2, Hadamard rotation, shape-gain 2 bits/dim, sharded by "
+                        "matrix", "n_gpus": world, "blocks": total, "seconds": secs, "blocks_per_s": total / secs,
+            "gather_seconds": gather_s, "scaling": "strong (fixed model, split over the GPUs)"}
 
 
 def rate_sweep_bench(q, x, device, stream, args) -> dict:
@@ -420,7 +466,7 @@ def dequant_bench(q, device, stream, args) -> dict:
 
 
 def gemm_bench(q, device, stream, args) -> dict:
-    """Fused dequant-GEMM on the Llama-3-8B MLP shapes: W 14336 x 4096 (171
+    """Dequant-GEMM on the Llama-3-8B MLP shapes: W 14336 x 4096 (171
     blocks per row) and 4096 x 14336 (598 blocks per row), random valid
     indices (seed 4) with fp16 row scales, bf16 activations N(0,1) [M, K]."""
     import torch
@@ -468,7 +514,16 @@ def gemm_bench(q, device, stream, args) -> dict:
         del acts, ys
     return {"workload": "Llama-3-8B MLP weights 14336x4096 + 4096x14336, random valid indices seed 4, fp16 row "
                         "scales, bf16 activations N(0,1), fp32 out", "by_m": out,
-            "gpu_launches": 2 * args.steps * len(args.gemm_m)}
+            "gpu_launches": args.steps * len(args.gemm_m) * sum(2 * gemm_chunks(n, bpr) for n, _, bpr, _, _ in mats)}
+
+
+def gemm_chunks(n_out: int, bpr: int, budget: int = 256 << 20) -> int:
+    """Staging chunks of one dequant-GEMM call (one decode and one GEMM
+    launch each): rows of 24 * bpr bf16 columns padded to 64, at most
+    `budget` bytes (the library's stream-ordered staging limit)."""
+    row_bytes = (24 * bpr + 63) // 64 * 64 * 2
+    rows = min(n_out, max(128, budget // row_bytes // 128 * 128))
+    return -(-n_out // rows)
 
 
 def main():
@@ -483,6 +538,8 @@ def main():
     ap.add_argument("--skip-dequant", action="store_true")
     ap.add_argument("--dequant-layers", type=int, default=32)
     ap.add_argument("--skip-gemm", action="store_true")
+    ap.add_argument("--model-layers", type=int, default=32,
+                    help="Llama-2-7B layers of the whole-model quantization section (0 skips it)")
     ap.add_argument("--sweep-rows", type=int, default=4_194_304,
                     help="blocks of the rate sweep sample (0 skips the sweep)")
     ap.add_argument("--gemm-m", type=int, nargs="+", default=[1, 8, 64, 512, 4096])

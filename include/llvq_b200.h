@@ -90,18 +90,18 @@ int llvq_dequantize(const llvq_codebook* cb, const int64_t* indices, int64_t n, 
 int llvq_dequantize_bf16(const llvq_codebook* cb, const int64_t* indices, int64_t n, const uint16_t* row_scale_f16,
                          int64_t blocks_per_row, uint16_t* out_bf16, int32_t* error_count, void* stream);
 
-/* Fused dequant-GEMM: y[m, n] = sum_k a[m, k] * W[n, k], where row n of W is
- * the dequantized indices[n * blocks_per_row + b] (b = 0 .. blocks_per_row-1,
+/* Dequant-GEMM: y[m, n] = sum_k a[m, k] * W[n, k], where row n of W is the
+ * dequantized indices[n * blocks_per_row + b] (b = 0 .. blocks_per_row-1,
  * 24 columns each) times row_scale[n] (fp16 bits; NULL means 1).  a: bf16
  * [m, k] row-major, 16-byte aligned, k % 8 == 0, k <= 24 * blocks_per_row
- * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  Up to 256
- * activation rows the weights are decoded straight into shared memory and
- * multiplied on the tcgen05 tensor cores with fp32 accumulation, never
- * written to global memory.  Above 256 rows they are decoded chunk by chunk
- * into a bf16 staging buffer (about 32 MiB, cudaMallocAsync/cudaFreeAsync on
- * `stream`) that a pipelined tcgen05 GEMM reads from L2.
- * *error_flag (device int, may be NULL) is set to 1 if a tensor-core wait
- * timed out.  No reference counterpart (the reference has no GEMM). */
+ * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  The weights
+ * are decoded into a bf16 staging buffer (at most 256 MiB, chunk by chunk
+ * beyond that; cudaMallocAsync/cudaFreeAsync on `stream`) that a pipelined
+ * tcgen05 GEMM reads, accumulating in fp32; when the matrix has fewer
+ * 128 x 256 output tiles than SMs the K range is split in two and y is
+ * zeroed first (cudaMemsetAsync).  *error_flag (device int, may be NULL) is
+ * set to 1 if a tensor-core wait timed out.  No reference counterpart (the
+ * reference has no GEMM). */
 int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
               const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
               int32_t* error_flag, void* stream);
@@ -109,11 +109,10 @@ int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, in
 /* llvq_gemm without device allocation.  No counterpart in the reference.
  * For callers that may not allocate device memory while they run (a serving
  * engine that reserved the GPU's memory for its own pool, a step that must not
- * fail on out-of-memory halfway): batches above 256 rows stage the decoded
- * weights in a fixed LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 MiB) array compiled
- * into the library, one per device, instead of a cudaMallocAsync buffer;
- * smaller batches take llvq_gemm's fused kernel, which uses no staging.
- * Same arguments, results and error flag as llvq_gemm, plus the limit
+ * fail on out-of-memory halfway): the decoded weights are staged in a fixed
+ * LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 MiB) array compiled into the library,
+ * one per device, instead of a cudaMallocAsync buffer, a chunk of rows at a
+ * time.  Same arguments, results and error flag as llvq_gemm, plus the limit
  * blocks_per_row <= LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW (2730: one 128-row
  * tile of rows up to 65536 columns fits the array); wider rows return
  * LLVQ_ERR_INVALID_ARGUMENT.  The array needs no initial contents.  The first

@@ -361,9 +361,10 @@ int upload(llvq::Codebook& cb, int device) {
   return LLVQ_OK;
 }
 
-// Decoded-weight staging of the large-batch GEMM: 32 MiB keeps a chunk of
-// bf16 weights resident in L2 while every activation tile streams over it.
-constexpr int64_t kGemmStagingBudget = 32ll << 20;
+// Decoded-weight staging of the large-batch GEMM: up to 256 MiB, so the
+// Llama-size matrices (up to 16k x 8k) are decoded in one chunk and every
+// tile of the matrix is available to the SMs at once.
+constexpr int64_t kGemmStagingBudget = 256ll << 20;
 
 // Runs `fn` with the codebook's device current, restoring the caller's device.
 template <class F>
@@ -475,10 +476,8 @@ int llvq_gemm(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm pointers: null, or activations not 16-byte aligned");
   if (m > (int64_t)INT32_MAX || n_out > (int64_t)INT32_MAX || blocks_per_row > (int64_t)INT32_MAX)
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
+  if (m == 0 || n_out == 0) return LLVQ_OK;
   return on_device(h, [&] {
-    if (m <= llvq::kGemmFusedMaxM)
-      return llvq::gemm_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
-                               (cudaStream_t)stream);
     // stream-ordered staging buffer, released on the same stream after the GEMM
     const int64_t bytes = llvq::gemm_staging_bytes(n_out, blocks_per_row, kGemmStagingBudget);
     void* staging = nullptr;
@@ -508,13 +507,10 @@ int llvq_gemm_noalloc(const llvq_codebook* h, const int64_t* indices, int64_t n_
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm pointers: null, or activations not 16-byte aligned");
   if (m > (int64_t)INT32_MAX || n_out > (int64_t)INT32_MAX)
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
-  return on_device(h, [&] {
+  return on_device(h, [&] {  // setup runs even for empty shapes, so a first empty call prepares the device
     void* staging = nullptr;
     cudaError_t e = llvq::noalloc_staging(&staging);  // first call on a device: symbol lookup
     if (e != cudaSuccess) return e;
-    if (m <= llvq::kGemmFusedMaxM)
-      return llvq::gemm_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
-                               (cudaStream_t)stream);
     return llvq::gemm_staged_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
                                     error_flag, staging, llvq::kNoAllocStagingBytes, (cudaStream_t)stream);
   });

@@ -53,15 +53,12 @@ cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t 
                               const uint16_t* row_scale, int64_t blocks_per_row, int* error_count,
                               cudaStream_t stream);
 
-cudaError_t gemm_launch(const Codebook& cb, const int64_t* idx, int64_t n_out, int64_t bpr, const uint16_t* rscale,
-                        const void* a, int64_t m, int64_t k, float* y, int* error_flag, cudaStream_t stream);
-
-// Large-batch GEMM: weights decoded chunk by chunk into a bf16 staging
-// buffer of staging_bytes (rows padded to gemm_staging_ldw(bpr) columns),
-// then a pipelined tcgen05 GEMM over it.  gemm_staging_bytes gives the buffer
-// size for a byte budget (at least one 128-row tile, at most the whole matrix).
+// Dequant-GEMM: weights decoded (a chunk of rows at a time) into a bf16
+// staging buffer of staging_bytes (rows padded to gemm_staging_ldw(bpr)
+// columns), then a pipelined tcgen05 GEMM over it.  gemm_staging_bytes gives
+// the buffer size for a byte budget (at least one 128-row tile, at most the
+// whole matrix).
 constexpr int kMaxDevices = 64;
-constexpr int kGemmFusedMaxM = 256;  // batches up to this size use the fused kernel
 int64_t gemm_staging_ldw(int64_t bpr);
 int64_t gemm_staging_bytes(int64_t n_out, int64_t bpr, int64_t budget);
 cudaError_t decode_rows_bf16_launch(const Codebook& cb, const int64_t* index, int rows, int bpr, int ldw, void* out,

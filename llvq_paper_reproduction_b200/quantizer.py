@@ -192,13 +192,12 @@ class LeechLatticeVectorQuantizerGpu:
         return out
 
     def gemm(self, a: torch.Tensor, indices: torch.Tensor, row_scale: torch.Tensor | None = None) -> torch.Tensor:
-        """Fused dequant-GEMM: ``a @ W.T`` in fp32 for bf16 activations ``a``
-        [m, k] and a weight given by its indices [n, blocks] (W[n] =
-        dequantize(indices[n]).flatten()[:k] * row_scale[n]).  Up to 256
-        activation rows the weight is decoded inside the GEMM kernel and never
-        materialised; larger batches decode it chunk by chunk into a bf16
-        staging buffer (stream-ordered, about 32 MiB) that a pipelined GEMM
-        streams from L2 (no reference counterpart)."""
+        """Dequant-GEMM: ``a @ W.T`` in fp32 for bf16 activations ``a`` [m, k]
+        and a weight given by its indices [n, blocks] (W[n] =
+        dequantize(indices[n]).flatten()[:k] * row_scale[n]).  The weight is
+        decoded into a bf16 staging buffer (stream-ordered, at most 256 MiB,
+        chunk by chunk beyond that) that a pipelined tcgen05 GEMM reads (no
+        reference counterpart)."""
         self._require_cuda("gemm")
         if a.dim() != 2 or indices.dim() != 2:
             raise ValueError("expected a [m, k] and indices [n, blocks]")

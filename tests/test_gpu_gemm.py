@@ -1,6 +1,6 @@
-"""Fused dequant-GEMM on the tcgen05 tensor cores against dequantize-then-
-matmul in fp32 (relative Frobenius error <= 1e-3; the kernel only rounds the
-bf16 activations, so the observed error is far smaller)."""
+"""Dequant-GEMM (decode to bf16 staging, tcgen05 GEMM) against dequantize-
+then-matmul in fp32 (relative Frobenius error <= 1e-3; the path only rounds
+the bf16 activations, so the observed error is far smaller)."""
 from __future__ import annotations
 
 import numpy as np
@@ -32,12 +32,13 @@ def rel_err(y, ref):
     return float(torch.linalg.norm(y - ref) / torch.linalg.norm(ref))
 
 
-# batches above 256 rows take the staged path (decode to bf16, then a
-# pipelined GEMM); (300, 2500, 598, 14336) stages the weights in 3 row chunks
+# the K range is split in two while the output has fewer 128 x 256 tiles
+# than SMs; (1024, 4736, 8, 192) has 148 tiles (no split); (300, 2500, 598,
+# 14336) is one staging chunk here and three in the no-allocation variant
 @pytest.mark.parametrize("m_act,n,bpr,k", [(1, 128, 8, 192), (8, 300, 20, 472), (64, 256, 171, 4096),
                                            (200, 130, 25, 600), (256, 200, 12, 288), (300, 257, 9, 216),
                                            (16, 1024, 598, 14336), (513, 384, 171, 4096), (300, 2500, 598, 14336),
-                                           (1100, 131, 3, 56)])
+                                           (1100, 131, 3, 56), (1024, 4736, 8, 192)])
 def test_gemm_matches_dequantize_matmul(m_act, n, bpr, k):
     q = api()
     g = torch.Generator(device="cuda").manual_seed(4)

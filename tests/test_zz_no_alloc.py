@@ -1,12 +1,11 @@
 """llvq_gemm_noalloc (static staging array, no device allocation) against
 llvq_gemm (stream-ordered staging allocation) on the same inputs.
 
-Above 256 activation rows both run the staged kernels with the same k order
-per output element, so the outputs are compared bit for bit.  Up to 256 rows
-both take the fused kernel, which adds split-K partial sums with atomics in
-no fixed order, so there the outputs agree to fp32 rounding (relative
-Frobenius distance <= 1e-6).  Two calls in a row with different weights check
-that nothing of the first call's staging survives into the second.
+Both run the same kernels with the same k order per output element (the K
+split, when there is one, is decided from the whole matrix, not from the
+staging chunk, and two halves added into zero commute), so the outputs are
+compared bit for bit.  Two calls in a row with different weights check that
+nothing of the first call's staging survives into the second.
 The file name sorts last so the suite also runs it after every other test
 has used the device.
 """
@@ -18,7 +17,6 @@ import torch
 pytestmark = pytest.mark.gpu
 
 MAX_BPR = 2730  # LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW
-FUSED_MAX_M = 256  # batches up to this size use the fused kernel (no staging)
 
 
 def _quantizer():
@@ -48,10 +46,11 @@ def _run(q, fn_name, idx, a, scale):
     return y
 
 
-# (m, n, bpr, k): staged batches (m > 256), one with weights wider than the
-# 16 MiB array holds at once (K = 14336: 512 rows per chunk, 3 chunks), and a
-# fused-kernel batch (m <= 256, no staging).
-CASES = [(300, 1300, 598, 14336), (513, 384, 171, 4096), (1100, 131, 3, 56), (64, 256, 171, 4096)]
+# (m, n, bpr, k): one with weights wider than the 16 MiB array holds at once
+# (K = 14336: 512 rows per chunk, 3 chunks), one with enough output tiles to
+# run without the K split, and small batches.
+CASES = [(300, 1300, 598, 14336), (513, 384, 171, 4096), (1100, 131, 3, 56), (1024, 4736, 8, 192),
+         (64, 256, 171, 4096), (1, 700, 40, 960)]
 
 
 @pytest.mark.parametrize("m,n,bpr,k", CASES)
@@ -63,11 +62,8 @@ def test_noalloc_matches_gemm_two_calls(m, n, bpr, k):
     ref2 = _run(q, "gemm", *second)
     out1 = _run(q, "gemm_noalloc", *first)
     out2 = _run(q, "gemm_noalloc", *second)
-    for out, ref in ((out1, ref1), (out2, ref2)):
-        if m > FUSED_MAX_M:
-            assert torch.equal(out, ref)
-        else:
-            assert float(torch.linalg.norm(out - ref) / torch.linalg.norm(ref)) <= 1e-6
+    assert torch.equal(out1, ref1)
+    assert torch.equal(out2, ref2)
     assert not torch.equal(out1, out2)
 
 
