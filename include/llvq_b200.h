@@ -96,7 +96,8 @@ int llvq_dequantize_bf16(const llvq_codebook* cb, const int64_t* indices, int64_
  * [m, k] row-major, 16-byte aligned, k % 8 == 0, k <= 24 * blocks_per_row
  * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  The weights
  * are decoded into a bf16 staging buffer (at most 256 MiB, chunk by chunk
- * beyond that; cudaMallocAsync/cudaFreeAsync on `stream`) that a pipelined
+ * beyond that; stream-ordered on `stream` from a library-owned memory pool
+ * that keeps its reservation between calls) that a pipelined
  * tcgen05 GEMM reads, accumulating in fp32; when the matrix has fewer
  * 128 x 256 output tiles than SMs the K range is split in two and y is
  * zeroed first (cudaMemsetAsync).  *error_flag (device int, may be NULL) is
@@ -111,7 +112,7 @@ int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, in
  * engine that reserved the GPU's memory for its own pool, a step that must not
  * fail on out-of-memory halfway): the decoded weights are staged in a fixed
  * LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 MiB) array compiled into the library,
- * one per device, instead of a cudaMallocAsync buffer, a chunk of rows at a
+ * one per device, instead of a stream-ordered pool buffer, a chunk of rows at a
  * time.  Same arguments, results and error flag as llvq_gemm, plus the limit
  * blocks_per_row <= LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW (2730: one 128-row
  * tile of rows up to 65536 columns fits the array); wider rows return

@@ -478,10 +478,14 @@ int llvq_gemm(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
   if (m == 0 || n_out == 0) return LLVQ_OK;
   return on_device(h, [&] {
-    // stream-ordered staging buffer, released on the same stream after the GEMM
+    // stream-ordered staging buffer from the library's pool, released on the
+    // same stream after the GEMM
     const int64_t bytes = llvq::gemm_staging_bytes(n_out, blocks_per_row, kGemmStagingBudget);
+    cudaMemPool_t pool;
+    cudaError_t e = llvq::gemm_staging_pool(&pool);
+    if (e != cudaSuccess) return e;
     void* staging = nullptr;
-    cudaError_t e = cudaMallocAsync(&staging, (size_t)bytes, (cudaStream_t)stream);
+    e = cudaMallocFromPoolAsync(&staging, (size_t)bytes, pool, (cudaStream_t)stream);
     if (e != cudaSuccess) return e;
     e = llvq::gemm_staged_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
                                  staging, bytes, (cudaStream_t)stream);

@@ -28,6 +28,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "llvq_device.cuh"
 #include "llvq_internal.h"
@@ -199,6 +200,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // (the launcher also does this lazily on its first launch).
 cudaError_t gemm_configure_device() {
   return cudaFuncSetAttribute(gemm_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmem);
+}
+
+// The library's staging pool on the current device: stream-ordered like the
+// default pool, but it keeps what it has reserved (release threshold = max),
+// so a GEMM after a synchronize does not map the staging memory again.  It
+// holds at most one staging buffer per concurrent call (256 MiB each).
+cudaError_t gemm_staging_pool(cudaMemPool_t* pool) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t p = nullptr;
+    e = cudaMemPoolCreate(&p, &props);
+    if (e != cudaSuccess) return e;
+    uint64_t keep = UINT64_MAX;
+    e = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+    if (e != cudaSuccess) {
+      cudaMemPoolDestroy(p);
+      return e;
+    }
+    pools[dev] = p;
+  }
+  *pool = pools[dev];
+  return cudaSuccess;
 }
 
 int64_t gemm_staging_ldw(int64_t bpr) { return (24 * bpr + 63) / 64 * 64; }

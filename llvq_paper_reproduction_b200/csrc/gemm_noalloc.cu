@@ -1,7 +1,7 @@
 // Fixed staging buffer for llvq_gemm_noalloc.
 //
 // The large-batch GEMM decodes weights into a bf16 staging buffer before the
-// tensor-core pass.  llvq_gemm takes that buffer from cudaMallocAsync on the
+// tensor-core pass.  llvq_gemm takes that buffer from a stream-ordered pool on the
 // caller's stream; llvq_gemm_noalloc takes it from the array below instead,
 // for callers that may not allocate device memory while they run: a serving
 // engine that reserved the GPU's memory for its own pool at start-up and must

@@ -1,24 +1,24 @@
-// Per-index Λ24 decoder shared by the dequantizer and the fused dequant-GEMM.
+// Per-index Λ24 decoder shared by the dequantizer and the dequant-GEMM's
+// weight staging.
 //
 // Index layout and unranking as in the reference's codeword() path
 // (impl/leech_lattice_vector_quantizer.py:196-245, :774-867): class by binary
 // search over the class starts, a 96-byte decode record (six 16-byte loads),
 // the per-class splits by reciprocal multiplication with an exact correction,
 // then one 24-step lexicographic unranking loop shared by both parities (an
-// even class unranks its |v| = 2 mod 4 part, then its |v| = 0 mod 4 part), so
-// warps holding both parities do not diverge there.  Lexicographic
-// unranking picks, at each step, the value whose branch [N*C_{j-1}/rem,
-// N*C_j/rem) holds the rank (C = cumulative counts, N the multinomial of
-// what remains, rem the positions left), i.e. the bucket of
-// t = floor(rank * rem / N) among the cumulative counts.  Once N fits 32
-// bits, t is estimated in fp32, the bucket found with a byte-wise compare of
-// the packed cumulative counts, and the choice verified exactly with two
-// 32x32->64 products (a miss, at an fp32 rounding boundary, is stepped to
-// the neighbouring bucket).  The new rank and N are exact divisions by rem:
-// a shift by its power of two and a multiply by the inverse of its odd part
-// (mod 2^32).  Larger N (the first steps of the largest classes) use the
-// 64-bit branch-by-branch scan.  Even-class signs use the closed form of
-// rank_even_signs (llvq_device.cuh) inside the scatter loop.
+// even class unranks its |v| = 2 mod 4 part on the word's positions, then its
+// |v| = 0 mod 4 part on the others), so warps holding both parities do not
+// diverge there.  Lexicographic unranking picks, at each step, the value
+// whose branch [N*C_{j-1}/rem, N*C_j/rem) holds the rank (C = cumulative
+// counts, N the multinomial of what remains, rem the positions left).
+// For parts of at most four distinct values (fast_step) the three boundaries
+// are computed exactly -- a product, a shift by the power of two in rem and a
+// multiply by the inverse of its odd part -- and compared with the rank; the
+// magnitude goes straight to its position in a per-thread shared-memory row.
+// Other classes use a general step (fp32 estimate of rank*rem/N, byte-wise
+// compare of the packed cumulative counts, exact verification; a 64-bit scan
+// while N >= 2^32) and a nibble sequence scattered afterwards.  Even-class
+// signs use the closed form of rank_even_signs (llvq_device.cuh).
 #pragma once
 
 #include <cstdint>
@@ -28,11 +28,14 @@
 namespace llvq {
 
 constexpr int kMaxSmemClasses = 1024;
+constexpr int kDecodeThreads = 256;  // blocks up to this size get per-thread rows
+constexpr int kRowWords = 7;         // 24 magnitude bytes per thread; a 28-byte stride reads without bank conflicts
 
 struct DecodeShared {
   int64_t starts[kMaxSmemClasses];
   uint64_t inv[kDim + 1];   // inverse of the odd part of d modulo 2^64
   uint32_t shift[kDim + 1]; // trailing zeros of d
+  uint32_t rows[kDecodeThreads * kRowWords];  // each thread's codeword magnitudes, by position
 };
 
 // Fill the shared tables (call with the whole block, then __syncthreads()).
@@ -113,9 +116,72 @@ __device__ __forceinline__ uint32_t unrank_step(uint64_t& rank, uint64_t& N, uin
   return j;
 }
 
+// One unranking step for a part of at most four distinct values: the
+// branch boundaries B_i = N * C_i / rem (C_i = c_0 + ... + c_i, exact
+// integers because N * c_j / rem is the multinomial of what remains after
+// value j) are computed exactly, the value taken is the number of boundaries
+// at or below `rank`, and the new rank and N are rank - B_{j-1} and
+// B_j - B_{j-1}.  C_i of absent values equals rem, so their boundary is N
+// and is never taken.  32-bit arithmetic once N < 2^32 (every step but the
+// first few of the largest classes).
+struct FastPart {
+  uint64_t rank, N;
+  uint32_t c0, c1, c2;      // cumulative counts of the first 1, 2, 3 values
+  uint32_t v0, v1, v2, v3;  // the values, descending
+};
+
+__device__ __forceinline__ uint32_t fast_step(FastPart& p, int rem, const DecodeShared& sh) {
+  const uint32_t s = sh.shift[rem];
+  bool p0, p1, p2;
+  if (p.N >> 32) {
+    const uint64_t inv = sh.inv[rem];
+    const uint64_t b0 = ((p.N * p.c0) >> s) * inv, b1 = ((p.N * p.c1) >> s) * inv, b2 = ((p.N * p.c2) >> s) * inv;
+    p0 = b0 <= p.rank;
+    p1 = b1 <= p.rank;
+    p2 = b2 <= p.rank;
+    const uint64_t lo = p2 ? b2 : p1 ? b1 : p0 ? b0 : 0ull;
+    const uint64_t hi = !p0 ? b0 : !p1 ? b1 : !p2 ? b2 : p.N;
+    p.rank -= lo;
+    p.N = hi - lo;
+  } else {
+    const uint32_t inv = (uint32_t)sh.inv[rem], n32 = (uint32_t)p.N, r32 = (uint32_t)p.rank;
+    const uint64_t q0 = (uint64_t)n32 * p.c0, q1 = (uint64_t)n32 * p.c1, q2 = (uint64_t)n32 * p.c2;
+    const uint32_t b0 = __funnelshift_r((uint32_t)q0, (uint32_t)(q0 >> 32), s) * inv;
+    const uint32_t b1 = __funnelshift_r((uint32_t)q1, (uint32_t)(q1 >> 32), s) * inv;
+    const uint32_t b2 = __funnelshift_r((uint32_t)q2, (uint32_t)(q2 >> 32), s) * inv;
+    p0 = b0 <= r32;
+    p1 = b1 <= r32;
+    p2 = b2 <= r32;
+    const uint32_t lo = p2 ? b2 : p1 ? b1 : p0 ? b0 : 0u;
+    const uint32_t hi = !p0 ? b0 : !p1 ? b1 : !p2 ? b2 : n32;
+    p.rank = r32 - lo;
+    p.N = hi - lo;
+  }
+  // the value taken loses one count: every cumulative count from it on
+  p.c0 -= !p0;
+  p.c1 -= !p1;
+  p.c2 -= !p2;
+  return p2 ? p.v3 : p1 ? p.v2 : p0 ? p.v1 : p.v0;
+}
+
+__device__ __forceinline__ void fast_part_load(FastPart& p, uint64_t rank, uint64_t N, uint64_t pv, uint64_t pm) {
+  p.rank = rank;
+  p.N = N;
+  p.v0 = byte_at(pv, 0);
+  p.v1 = byte_at(pv, 1);
+  p.v2 = byte_at(pv, 2);
+  p.v3 = byte_at(pv, 3);
+  p.c0 = byte_at(pm, 0);
+  p.c1 = p.c0 + byte_at(pm, 1);
+  p.c2 = p.c1 + byte_at(pm, 2);
+}
+
 // Integer codeword of index v (before the 1/sqrt(8) scale); false and zeros
-// when v is outside the codebook.
-__device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, const DecodeShared& sh, int (&y)[kDim]) {
+// when v is outside the codebook.  Classes whose parts have at most four
+// distinct values (all but a few classes) unrank with fast_step and write
+// each magnitude to its position in the thread's shared-memory row; the
+// others use the general step and a nibble sequence.
+__device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, DecodeShared& sh, int (&y)[kDim]) {
   bool ok = v >= 0 && v < book.total;
   if (ok) {
     const int k = find_class(book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start, book.n_classes, v);
@@ -158,30 +224,63 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, con
       cnt2 = pm0;
       nfirst = weight;
     }
-    uint64_t seq_lo = 0, seq_hi = 0;  // 4-bit value indices, step order
-#pragma unroll
-    for (int t = 0; t < kDim; ++t) {
-      if (t == nfirst) {
-        rank = rank2;
-        N = N2;
-        cnt = cnt2;
+    uint32_t mag[6];  // magnitudes by position, 4 per word
+    const int nv0 = (meta >> 11) & 15, nv1 = (meta >> 15) & 15;
+    if (nv0 <= 4 && nv1 <= 4 && threadIdx.x < kDecodeThreads) {
+      uint8_t* row = reinterpret_cast<uint8_t*>(sh.rows + threadIdx.x * kRowWords);
+      FastPart part;
+      fast_part_load(part, rank, N, odd ? pv0 : pv1, cnt);
+      uint32_t mask = odd ? kFull24 : word;  // positions still to fill, lowest first
+      int rem = nfirst;
+#pragma unroll 4
+      for (int t = 0; t < kDim; ++t) {
+        if (t == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
+          fast_part_load(part, rank2, N2, pv0, cnt2);
+          mask = ~word & kFull24;
+          rem = kDim - t;
+        }
+        const uint32_t val = fast_step(part, rem, sh);
+        --rem;
+        const int pos = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        row[pos] = (uint8_t)val;
       }
-      const int rem = t < nfirst ? nfirst - t : kDim - t;
-      const uint32_t j = unrank_step(rank, N, cnt, rem, sh);
-      if (t < 16) seq_lo |= (uint64_t)j << (4 * t);
-      else seq_hi |= (uint64_t)j << (4 * (t - 16));
+      const uint32_t* rw = sh.rows + threadIdx.x * kRowWords;
+#pragma unroll
+      for (int w = 0; w < 6; ++w) mag[w] = rw[w];
+    } else {
+      uint64_t seq_lo = 0, seq_hi = 0;  // 4-bit value indices, step order
+#pragma unroll 4
+      for (int t = 0; t < kDim; ++t) {
+        if (t == nfirst) {
+          rank = rank2;
+          N = N2;
+          cnt = cnt2;
+        }
+        const int rem = t < nfirst ? nfirst - t : kDim - t;
+        const uint32_t j = unrank_step(rank, N, cnt, rem, sh);
+        if (t < 16) seq_lo |= (uint64_t)j << (4 * t);
+        else seq_hi |= (uint64_t)j << (4 * (t - 16));
+      }
+      // scatter: odd -> step d at position d; even -> the word's positions
+      // take the first (f1) part in order, the others the second (f0) part
+#pragma unroll
+      for (int w = 0; w < 6; ++w) mag[w] = 0;
+#pragma unroll
+      for (int d = 0; d < kDim; ++d) {
+        const bool bit = (word >> d) & 1u;
+        const bool part1 = !odd && bit;
+        const int below1 = __popc(word & ((1u << d) - 1u));
+        const int t = odd ? d : (bit ? below1 : nfirst + d - below1);
+        const uint32_t nib = (uint32_t)((t < 16 ? seq_lo >> (4 * t) : seq_hi >> (4 * (t - 16))) & 15u);
+        mag[d >> 2] |= byte_at(part1 ? pv1 : pv0, (int)nib) << (8 * (d & 3));
+      }
     }
-    // scatter: odd -> step d at position d; even -> the word's positions take
-    // the first (f1) part in order, the others the second (f0) part
     uint32_t nzmask = 0;
 #pragma unroll
     for (int d = 0; d < kDim; ++d) {
+      const int m = (int)((mag[d >> 2] >> (8 * (d & 3))) & 0xFFu);
       const bool bit = (word >> d) & 1u;
-      const bool part1 = !odd && bit;
-      const int below1 = __popc(word & ((1u << d) - 1u));
-      const int t = odd ? d : (bit ? below1 : nfirst + d - below1);
-      const uint32_t nib = (uint32_t)((t < 16 ? seq_lo >> (4 * t) : seq_hi >> (4 * (t - 16))) & 15u);
-      const int m = (int)byte_at(part1 ? pv1 : pv0, (int)nib);
       nzmask |= (uint32_t)(m != 0) << d;
       y[d] = odd ? (((m & 3) == (bit ? 3 : 1)) ? m : -m) : m;
     }

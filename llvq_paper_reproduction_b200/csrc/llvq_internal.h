@@ -60,6 +60,7 @@ cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t 
 // whole matrix).
 constexpr int kMaxDevices = 64;
 int64_t gemm_staging_ldw(int64_t bpr);
+cudaError_t gemm_staging_pool(cudaMemPool_t* pool);
 int64_t gemm_staging_bytes(int64_t n_out, int64_t bpr, int64_t budget);
 cudaError_t decode_rows_bf16_launch(const Codebook& cb, const int64_t* index, int rows, int bpr, int ldw, void* out,
                                     cudaStream_t stream);

@@ -74,3 +74,30 @@ def test_out_of_range_raises():
     with pytest.raises(IndexError):
         q.dequantize_lattice(torch.tensor([-1], device="cuda"))
     assert q.dequantize(torch.empty(0, dtype=torch.long, device="cuda")).shape == (0, 24)
+
+
+@pytest.mark.parametrize("lo,hi", [(2, 13), (23, 23), (32, 32)])
+def test_every_class_vs_oracle(lo, hi):
+    """First, last and seeded interior indices of every class, including
+    classes with more than four distinct magnitudes and permutation counts
+    of 2^32 and more (the single shells 23 and 32), against the oracle."""
+    from llvq_paper_reproduction_b200 import LeechLatticeVectorQuantizerGpu
+    from oracle.oracle import OracleBook
+
+    q = LeechLatticeVectorQuantizerGpu(max_shell=hi, min_shell=lo, use_cache=False, device="cuda")
+    ob = OracleBook(hi, min_shell=lo)
+    rng = np.random.default_rng(lo * 100 + hi)
+    idx = []
+    for k in range(ob.n_classes):
+        info = ob.class_info(k)
+        start, count = info["start"], info["count"]
+        idx += [start, start + count - 1]
+        idx += [start + int(rng.integers(count)) for _ in range(4)]
+        # the first and last permutation of a random (golay, sign) choice
+        perm = info["permutation_count"]
+        base = start + int(rng.integers(count // perm)) * perm
+        idx += [base, base + perm - 1]
+    idx = np.array(idx, dtype=np.int64)
+    got = q.dequantize_lattice(torch.from_numpy(idx).cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got, ob.codeword_batch(idx))
+    assert q.total_count == ob.total_count
