@@ -283,6 +283,28 @@ int build(llvq::Codebook& cb, int32_t n, const int32_t* shell, const int32_t* pa
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
+// The decoder's fast path (fully unrolled, 32-bit after the first step) needs
+// every part to have at most four distinct values and N < 2^32 from the
+// second step of each part on: N only shrinks, so it suffices that N after
+// the first step (at most N * c_max / positions) and the N of a part that
+// starts after step 0 (the f0 part of a word of weight > 0) are below 2^32.
+bool fast_decode_ok(const llvq::DevClass& c) {
+  using u128 = unsigned __int128;
+  const u128 lim = (u128)1 << 32;
+  auto cmax = [](const int32_t* m, int nv) {
+    int32_t best = 0;
+    for (int j = 0; j < nv; ++j) best = std::max(best, m[j]);
+    return (u128)best;
+  };
+  if (c.nv0 > 4 || c.nv1 > 4) return false;
+  if (c.parity) return (u128)c.perm_count * cmax(c.m0, c.nv0) / llvq::kDim < lim;
+  const int w = c.even_weight;
+  const u128 f1 = c.f1_perm, f0 = c.perm_count / c.f1_perm;
+  if (w > 0 && f1 * cmax(c.m1, c.nv1) / (u128)w >= lim) return false;
+  if (w == 0) return f0 * cmax(c.m0, c.nv0) / llvq::kDim < lim;
+  return f0 < lim;
+}
+
 int upload(llvq::Codebook& cb, int device) {
   using namespace llvq;
   const size_t n = cb.cls.size();
@@ -308,7 +330,8 @@ int upload(llvq::Codebook& cb, int device) {
       d.f1_perm = (uint32_t)c.f1_perm;
       d.inv_f1 = 1.0 / (double)c.f1_perm;
       d.meta = (uint32_t)c.parity | ((uint32_t)c.even_weight << 1) | ((uint32_t)c.sign_shift << 6) |
-               ((uint32_t)c.nv0 << 11) | ((uint32_t)c.nv1 << 15) | ((uint32_t)c.required << 19);
+               ((uint32_t)c.nv0 << 11) | ((uint32_t)c.nv1 << 15) | ((uint32_t)c.required << 19) |
+               (fast_decode_ok(c) ? kMetaFast : 0u);
       d.golay_base = (uint32_t)cb.weight_start[c.even_weight];
       d.pad = 0;
       d.v0 = d.m0 = d.v1 = d.m1 = 0;

@@ -130,10 +130,11 @@ struct FastPart {
   uint32_t v0, v1, v2, v3;  // the values, descending
 };
 
+template <bool kMay64>
 __device__ __forceinline__ uint32_t fast_step(FastPart& p, int rem, const DecodeShared& sh) {
   const uint32_t s = sh.shift[rem];
   bool p0, p1, p2;
-  if (p.N >> 32) {
+  if (kMay64 && (p.N >> 32)) {
     const uint64_t inv = sh.inv[rem];
     const uint64_t b0 = ((p.N * p.c0) >> s) * inv, b1 = ((p.N * p.c1) >> s) * inv, b2 = ((p.N * p.c2) >> s) * inv;
     p0 = b0 <= p.rank;
@@ -225,22 +226,29 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
       nfirst = weight;
     }
     uint32_t mag[6];  // magnitudes by position, 4 per word
-    const int nv0 = (meta >> 11) & 15, nv1 = (meta >> 15) & 15;
-    if (nv0 <= 4 && nv1 <= 4 && threadIdx.x < kDecodeThreads) {
+    if ((meta & kMetaFast) && threadIdx.x < kDecodeThreads) {
+      // Straight-line steps: a part can only start at step 0 or at a word
+      // weight (8, 12, 16), and N can only reach 2^32 at step 0.
       uint8_t* row = reinterpret_cast<uint8_t*>(sh.rows + threadIdx.x * kRowWords);
       FastPart part;
-      fast_part_load(part, rank, N, odd ? pv0 : pv1, cnt);
-      uint32_t mask = odd ? kFull24 : word;  // positions still to fill, lowest first
-      int rem = nfirst;
-#pragma unroll 4
+      uint32_t mask;  // positions still to fill, lowest first
+      if (nfirst == 0) {  // weight 0: only the f0 part
+        fast_part_load(part, rank2, N2, pv0, cnt2);
+        mask = kFull24;
+      } else {
+        fast_part_load(part, rank, N, odd ? pv0 : pv1, cnt);
+        mask = odd ? kFull24 : word;
+      }
+#pragma unroll
       for (int t = 0; t < kDim; ++t) {
-        if (t == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
-          fast_part_load(part, rank2, N2, pv0, cnt2);
-          mask = ~word & kFull24;
-          rem = kDim - t;
+        if (t == 8 || t == 12 || t == 16) {
+          if (t == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
+            fast_part_load(part, rank2, N2, pv0, cnt2);
+            mask = ~word & kFull24;
+          }
         }
-        const uint32_t val = fast_step(part, rem, sh);
-        --rem;
+        const int rem = t < nfirst ? nfirst - t : kDim - t;
+        const uint32_t val = t == 0 ? fast_step<true>(part, rem, sh) : fast_step<false>(part, rem, sh);
         const int pos = __ffs(mask) - 1;
         mask &= mask - 1u;
         row[pos] = (uint8_t)val;
