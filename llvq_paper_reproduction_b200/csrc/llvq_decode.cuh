@@ -35,6 +35,7 @@ struct DecodeShared {
   int64_t starts[kMaxSmemClasses];
   uint64_t inv[kDim + 1];   // inverse of the odd part of d modulo 2^64
   uint32_t shift[kDim + 1]; // trailing zeros of d
+  uint2 div32[kDim + 1];    // {inverse of the odd part of d modulo 2^32, trailing zeros of d}
   uint32_t rows[kDecodeThreads * kRowWords];  // each thread's codeword magnitudes, by position
 };
 
@@ -46,6 +47,7 @@ __device__ __forceinline__ void decode_setup(const DevBook& book, DecodeShared& 
     const uint32_t d = threadIdx.x, s = __ffs(d) - 1;
     sh.shift[d] = s;
     sh.inv[d] = inv_odd64(d >> s);
+    sh.div32[d] = make_uint2((uint32_t)sh.inv[d], s);
   }
 }
 
@@ -125,39 +127,25 @@ __device__ __forceinline__ uint32_t unrank_step(uint64_t& rank, uint64_t& N, uin
 // and is never taken.  32-bit arithmetic once N < 2^32 (every step but the
 // first few of the largest classes).
 struct FastPart {
-  uint64_t rank, N;
+  uint32_t rank, N;         // N < 2^32 after the first step of a part
   uint32_t c0, c1, c2;      // cumulative counts of the first 1, 2, 3 values
   uint32_t v0, v1, v2, v3;  // the values, descending
 };
 
-template <bool kMay64>
-__device__ __forceinline__ uint32_t fast_step(FastPart& p, int rem, const DecodeShared& sh) {
-  const uint32_t s = sh.shift[rem];
-  bool p0, p1, p2;
-  if (kMay64 && (p.N >> 32)) {
-    const uint64_t inv = sh.inv[rem];
-    const uint64_t b0 = ((p.N * p.c0) >> s) * inv, b1 = ((p.N * p.c1) >> s) * inv, b2 = ((p.N * p.c2) >> s) * inv;
-    p0 = b0 <= p.rank;
-    p1 = b1 <= p.rank;
-    p2 = b2 <= p.rank;
-    const uint64_t lo = p2 ? b2 : p1 ? b1 : p0 ? b0 : 0ull;
-    const uint64_t hi = !p0 ? b0 : !p1 ? b1 : !p2 ? b2 : p.N;
-    p.rank -= lo;
-    p.N = hi - lo;
-  } else {
-    const uint32_t inv = (uint32_t)sh.inv[rem], n32 = (uint32_t)p.N, r32 = (uint32_t)p.rank;
-    const uint64_t q0 = (uint64_t)n32 * p.c0, q1 = (uint64_t)n32 * p.c1, q2 = (uint64_t)n32 * p.c2;
-    const uint32_t b0 = __funnelshift_r((uint32_t)q0, (uint32_t)(q0 >> 32), s) * inv;
-    const uint32_t b1 = __funnelshift_r((uint32_t)q1, (uint32_t)(q1 >> 32), s) * inv;
-    const uint32_t b2 = __funnelshift_r((uint32_t)q2, (uint32_t)(q2 >> 32), s) * inv;
-    p0 = b0 <= r32;
-    p1 = b1 <= r32;
-    p2 = b2 <= r32;
-    const uint32_t lo = p2 ? b2 : p1 ? b1 : p0 ? b0 : 0u;
-    const uint32_t hi = !p0 ? b0 : !p1 ? b1 : !p2 ? b2 : n32;
-    p.rank = r32 - lo;
-    p.N = hi - lo;
-  }
+// Exact N * c / d for d = rem, given d's {odd-part inverse mod 2^32, shift},
+// when the quotient is an integer below 2^32.
+__device__ __forceinline__ uint32_t exact_div32(uint32_t n, uint32_t c, uint2 d) {
+  const uint64_t q = (uint64_t)n * c;
+  return __funnelshift_r((uint32_t)q, (uint32_t)(q >> 32), d.y) * d.x;
+}
+
+__device__ __forceinline__ uint32_t fast_step(FastPart& p, uint2 d) {
+  const uint32_t b0 = exact_div32(p.N, p.c0, d), b1 = exact_div32(p.N, p.c1, d), b2 = exact_div32(p.N, p.c2, d);
+  const bool p0 = b0 <= p.rank, p1 = b1 <= p.rank, p2 = b2 <= p.rank;
+  const uint32_t lo = p2 ? b2 : p1 ? b1 : p0 ? b0 : 0u;
+  const uint32_t hi = !p0 ? b0 : !p1 ? b1 : !p2 ? b2 : p.N;
+  p.rank -= lo;
+  p.N = hi - lo;
   // the value taken loses one count: every cumulative count from it on
   p.c0 -= !p0;
   p.c1 -= !p1;
@@ -165,9 +153,30 @@ __device__ __forceinline__ uint32_t fast_step(FastPart& p, int rem, const Decode
   return p2 ? p.v3 : p1 ? p.v2 : p0 ? p.v1 : p.v0;
 }
 
-__device__ __forceinline__ void fast_part_load(FastPart& p, uint64_t rank, uint64_t N, uint64_t pv, uint64_t pm) {
-  p.rank = rank;
-  p.N = N;
+// The first step of a part whose N may reach 2^32 (64-bit boundaries, the
+// 64-bit inverse of rem's odd part); leaves N below 2^32.
+__device__ __forceinline__ uint32_t fast_first_step(FastPart& p, uint64_t rank, uint64_t N, int rem,
+                                                    const DecodeShared& sh) {
+  if (!(N >> 32)) {
+    p.rank = (uint32_t)rank;
+    p.N = (uint32_t)N;
+    return fast_step(p, sh.div32[rem]);
+  }
+  const uint32_t s = sh.shift[rem];
+  const uint64_t inv = sh.inv[rem];
+  const uint64_t b0 = ((N * p.c0) >> s) * inv, b1 = ((N * p.c1) >> s) * inv, b2 = ((N * p.c2) >> s) * inv;
+  const bool p0 = b0 <= rank, p1 = b1 <= rank, p2 = b2 <= rank;
+  const uint64_t lo = p2 ? b2 : p1 ? b1 : p0 ? b0 : 0ull;
+  const uint64_t hi = !p0 ? b0 : !p1 ? b1 : !p2 ? b2 : N;
+  p.rank = (uint32_t)(rank - lo);
+  p.N = (uint32_t)(hi - lo);
+  p.c0 -= !p0;
+  p.c1 -= !p1;
+  p.c2 -= !p2;
+  return p2 ? p.v3 : p1 ? p.v2 : p0 ? p.v1 : p.v0;
+}
+
+__device__ __forceinline__ void fast_part_load(FastPart& p, uint64_t pv, uint64_t pm) {
   p.v0 = byte_at(pv, 0);
   p.v1 = byte_at(pv, 1);
   p.v2 = byte_at(pv, 2);
@@ -231,27 +240,36 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
       // weight (8, 12, 16), and N can only reach 2^32 at step 0.
       uint8_t* row = reinterpret_cast<uint8_t*>(sh.rows + threadIdx.x * kRowWords);
       FastPart part;
-      uint32_t mask;  // positions still to fill, lowest first
+      uint32_t mask, val;  // mask: positions still to fill, lowest first
+      int base;            // rem = base - t
       if (nfirst == 0) {  // weight 0: only the f0 part
-        fast_part_load(part, rank2, N2, pv0, cnt2);
+        fast_part_load(part, pv0, cnt2);
         mask = kFull24;
+        base = kDim;
+        val = fast_first_step(part, rank2, N2, kDim, sh);
       } else {
-        fast_part_load(part, rank, N, odd ? pv0 : pv1, cnt);
+        fast_part_load(part, odd ? pv0 : pv1, cnt);
         mask = odd ? kFull24 : word;
+        base = nfirst;
+        val = fast_first_step(part, rank, N, nfirst, sh);
       }
+      row[__ffs(mask) - 1] = (uint8_t)val;
+      mask &= mask - 1u;
+      const uint2* div = sh.div32 + base;  // div[-t] = rem's constants at step t
 #pragma unroll
-      for (int t = 0; t < kDim; ++t) {
+      for (int t = 1; t < kDim; ++t) {
         if (t == 8 || t == 12 || t == 16) {
           if (t == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
-            fast_part_load(part, rank2, N2, pv0, cnt2);
+            fast_part_load(part, pv0, cnt2);
+            part.rank = (uint32_t)rank2;
+            part.N = (uint32_t)N2;
             mask = ~word & kFull24;
+            div = sh.div32 + kDim;
           }
         }
-        const int rem = t < nfirst ? nfirst - t : kDim - t;
-        const uint32_t val = t == 0 ? fast_step<true>(part, rem, sh) : fast_step<false>(part, rem, sh);
-        const int pos = __ffs(mask) - 1;
+        val = fast_step(part, div[-t]);
+        row[__ffs(mask) - 1] = (uint8_t)val;
         mask &= mask - 1u;
-        row[pos] = (uint8_t)val;
       }
       const uint32_t* rw = sh.rows + threadIdx.x * kRowWords;
 #pragma unroll
