@@ -44,6 +44,9 @@ __device__ __forceinline__ float llvq_max3(float a, float b, float c) {
 namespace llvq {
 
 constexpr int kSearchThreads = 128;
+// At least 6 CTAs per SM (<= 85 registers): the search is issue-bound and
+// the extra resident warps outweigh a few spilled bytes (+4% on shells 2..13).
+constexpr int kSearchMinBlocks = 6;
 constexpr int kWordsPerThread = kNumGolay / kSearchThreads;
 constexpr long long kTagWord = 1ll << 40;   // low 12 bits: the word
 constexpr long long kTagExact = 2ll << 40;  // bits 12..39: class, low 12 bits: word
@@ -489,7 +492,7 @@ __device__ void stage_row(const float* __restrict__ x, int64_t row, RowShared& s
 }
 
 template <class S>
-__global__ void __launch_bounds__(kSearchThreads) search_kernel(const float* __restrict__ x, int64_t n, DevBook book,
+__global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kernel(const float* __restrict__ x, int64_t n, DevBook book,
                                                                 long long* tag_out, float* m_out) {
   __shared__ RowShared sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
