@@ -44,6 +44,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "Λ₂₄ blocks/sec quantized, dequant GB/s, fused-GEMM TFLOP/s at 1/2/4/8 B200 vs host CPU"
 SMS = 148
 FP32_LANES = 128
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) measured with ncu
+# on smaller launches of the same kernels, per unit, for the roofline
+# `traffic` entry: the search kernel on 65,536 blocks (6,676,992 + 52,480 B)
+# and the bf16 dequant kernel on 9,797,632 indices (78,546,432 + 410,793,728 B).
+SEARCH_DRAM_BYTES_PER_BLOCK = (6_676_992 + 52_480) / 65_536
+DEQUANT_DRAM_BYTES_PER_INDEX = (78_546_432 + 410_793_728) / 9_797_632
 
 
 def log(*a):
@@ -323,7 +329,8 @@ def run_gpu_arm(args) -> None:
                 "d2h_bytes_per_step": world * n * 8},
         "gpu_launches": 2 * args.steps,
         "roofline": {"bound": "alu", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
-                     "frac": achieved / peak_tflops, "traffic": None,
+                     "frac": achieved / peak_tflops, "traffic": SEARCH_DRAM_BYTES_PER_BLOCK * n,
+                     "traffic_unit": "bytes per launch (ncu on 65,536 blocks, scaled by blocks)",
                      "note": f"{ops / 1e6:.3f} M algorithmic ops/block (2 per distinct nonzero leader value per "
                              "evaluated pair + 2x4096x24 prefix adds); peak = 148 SMs x 128 FP32 lanes x 2 x "
                              "max SM clock (FFMA)"},
@@ -460,8 +467,12 @@ def dequant_bench(q, device, stream, args) -> dict:
                         "bf16 out, fp16 row scales",
             "gpu_launches": 2 * args.steps,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / peaks["hbm_gbs"], "traffic": None,
-                         "note": "56 B per index (8 B int64 index + 48 B bf16) + 2 B per row; peak of "
+                         "frac": gbs / peaks["hbm_gbs"],
+                         "traffic": DEQUANT_DRAM_BYTES_PER_INDEX * n_idx,
+                         "traffic_unit": "bytes per step (ncu on 9,797,632 indices, scaled by indices)",
+                         "note": "56 B per index (8 B int64 index + 48 B bf16) + 2 B per row; the kernel is "
+                                 "instruction-bound (about 2.3 k thread instructions per index under ncu, ALU "
+                                 "pipe ~54%), not HBM-bound; peak of "
                                  + ("fallback" if peaks.get("fallback") else "measured") + " copy bandwidth"}}
 
 
