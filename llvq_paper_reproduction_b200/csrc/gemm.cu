@@ -1,4 +1,4 @@
-// Λ24 dequant-GEMM for sm_100a (tcgen05 tensor cores, TMEM accumulators).
+// Λ24 dequant-GEMM for sm_100a (TMA, tcgen05 tensor cores, TMEM accumulators).
 //
 //   Y[m, n] = sum_k A[m, k] * W[n, k],   W[n, :] = row_scale[n] * fp32(1/sqrt 8) * codeword(indices[n, :])
 //
@@ -6,25 +6,29 @@
 // weights as bf16 copies of the integer codeword entries (|k| <= 22 for the
 // 48-bit codebook, exact in bf16) into a staging buffer, rows padded with
 // zeros to a multiple of 64 columns, a whole matrix or a chunk of rows at a
-// time.  The GEMM kernel then streams both operands through kStages shared-
-// memory stages of 64 columns (weights 128 rows, activations 256 rows) in the
-// 128-byte-swizzled K-major layout the tensor core reads, filled with 16-byte
-// cp.async copies (zero outside the matrices).  One thread issues 4 MMAs
-// (M = 128 weight rows, N = 256 activation rows, K = 16 each, fp32 in TMEM)
-// per stage and commits them to that stage's mbarrier; the MMAs of chunk c
-// are queued behind those of chunk c - 1 before the stage chunk c - 1 used is
-// refilled, so the tensor pipe does not drain between chunks.  The epilogue
-// applies fp32(1/sqrt 8) * row_scale[n], so the only rounding beyond fp32
-// accumulation is that of the bf16 activations; it writes Y transposed from
-// TMEM (lane = weight row, column = activation row), coalesced along n.
-// When the matrix has fewer output tiles than SMs the K range is split in two
-// and the halves are added into Y (zeroed first) with fp32 atomics.
+// time.  The GEMM kernel is persistent (one 192-thread CTA per SM) and warp-
+// specialised: one thread loads each 64-column stage of both operands
+// (weights 128 rows, activations 256 rows) with 2-D TMA tile loads in the
+// 128-byte-swizzled K-major layout the tensor core reads (zero fill outside
+// the matrices, no multicast); one thread issues 4 tcgen05 MMAs per stage
+// (M = 128 weight rows, N = 256 activation rows, K = 16 each, fp32 in TMEM);
+// four warps read finished accumulators from TMEM, apply
+// fp32(1/sqrt 8) * row_scale[n] and store Y transposed (lane = weight row,
+// column = activation row), coalesced along n.  Stages and the two TMEM
+// accumulators are handed over with mbarriers (TMA transaction counts,
+// tcgen05.commit arrivals, epilogue arrivals); every wait is bounded and sets
+// the caller's error flag when it gives up.  The only rounding beyond fp32
+// accumulation is that of the bf16 activations.  When the matrix has fewer
+// output tiles than SMs the K range is split in two and the halves are added
+// into Y (zeroed first) with fp32 atomics.
 //
 // The reference has no GEMM (its dequantizer returns int64 codewords,
 // impl/llvq_cuda_dequantize.py:78-181); the decode is the same index layout.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cstdint>
@@ -36,170 +40,218 @@
 
 namespace llvq {
 
-constexpr int kGemmThreads = 256;
 constexpr int kTileW = 128;   // weight rows per tile (MMA M)
 constexpr int kMaxAct = 256;  // activation rows per tile (MMA N)
 constexpr uint32_t kWaitLimit = 1u << 22;
 
-// Byte offset of 16-byte column chunk `chunk` of row `row` in a 128-byte-
-// swizzled K-major tile (the SWIZZLE_128B layout the MMA descriptors name).
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
-// ------------------------------------------------------------ the GEMM
-
+// Shared memory: kStages stages of [weights 128 rows | activations 256 rows]
+// x 64 bf16 columns in the 128-byte swizzle (each stage 1024-byte aligned),
+// then the mbarriers: full[kStages], empty[kStages], accumulator full[2] and
+// empty[2], drain; then the TMEM address.
+//
+// Roles: warp 0 (one thread) loads both operand tiles of a stage with TMA
+// (the box bytes complete the stage's "full" mbarrier); warp 1 (one thread)
+// waits for a full stage, issues the 4 MMAs and commits them to the stage's
+// "empty" mbarrier (and, after the last chunk of a tile, to the
+// accumulator's "full" mbarrier); warps 2-5 read the finished accumulator
+// from TMEM, scale and store it, then release it.  Two 256-column
+// accumulators let the epilogue of one tile overlap the MMAs of the next.
 constexpr int kStages = 4;
 constexpr int kStageW = kTileW * 128;           // 16 KB
 constexpr int kStageA = kMaxAct * 128;          // 32 KB
 constexpr int kStageBytes = kStageW + kStageA;  // 48 KB
-constexpr size_t kStagedSmem = (size_t)kStages * kStageBytes + 64 + 1024;
+constexpr int kTmaThreads = 192;
+constexpr int kAccCols = kMaxAct;  // fp32 columns per accumulator
+constexpr size_t kTmaBarOff = (size_t)kStages * kStageBytes;
+constexpr size_t kTmaSmem = kTmaBarOff + 8 * (2 * kStages + 5) + 16 + 1024;
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_staged_kernel(const __nv_bfloat16* __restrict__ Wk, int ldw, int w_rows, int n_base, int n_out,
-                       const uint16_t* __restrict__ rscale, const __nv_bfloat16* __restrict__ A, int m_act, int k_in,
-                       float* __restrict__ Y, int splits, int* error_flag) {
+__global__ void __launch_bounds__(kTmaThreads, 1)
+    gemm_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ta, int kc_total,
+                    int w_rows, int n_base, int n_out, const uint16_t* __restrict__ rscale, int m_act,
+                    float* __restrict__ Y, int splits, int* error_flag) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* mbars = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
-  uint32_t* holder = reinterpret_cast<uint32_t*>(base + kStages * kStageBytes + 8 * kStages);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kTmaBarOff);
+  uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  const uint32_t sbase = tc::smem_addr(base);
+  auto full = [&](int st) { return tc::smem_addr(&bars[st]); };
+  auto empty = [&](int st) { return tc::smem_addr(&bars[kStages + st]); };
+  auto acc_full = [&](int a) { return tc::smem_addr(&bars[2 * kStages + a]); };
+  auto acc_empty = [&](int a) { return tc::smem_addr(&bars[2 * kStages + 2 + a]); };
+  const uint32_t drain = tc::smem_addr(&bars[2 * kStages + 4]);  // the MMA issuer's last commit
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int st = 0; st < kStages; ++st) tc::mbar_init(tc::smem_addr(&mbars[st]), 1);
+    for (int st = 0; st < kStages; ++st) {
+      tc::mbar_init(full(st), 1);
+      tc::mbar_init(empty(st), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(acc_full(a), 1);
+      tc::mbar_init(acc_empty(a), 4);  // one arrival per epilogue warp
+    }
+    tc::mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 0) tc::tmem_alloc(tc::smem_addr(holder), kMaxAct);
+  if (warp == 0) tc::tmem_alloc(tc::smem_addr(holder), 2 * kAccCols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *holder;
-  const uint32_t idesc = tc::idesc_bf16_f32(kTileW, kMaxAct);
-  const uint32_t sbase = tc::smem_addr(base);
-  const int kc_total = ldw / 64;
   const int tn = (w_rows + kTileW - 1) / kTileW, tm = (m_act + kMaxAct - 1) / kMaxAct;
-  uint32_t phase = 0;  // bit st = parity of stage st's next completion
+  const int units = tn * tm * splits;
   bool failed = false;
-
-
-  // work unit = (weight tile, activation tile, K split), splits fastest so
-  // the units of one weight tile run side by side and share it in L2
-  for (int item = blockIdx.x; item < tn * tm * splits && !failed; item += gridDim.x) {
+  // unit -> (weight tile, activation tile, K split), splits fastest
+  auto unit_of = [&](int item, int& row0, int& m0, int& c_begin, int& c_end) {
     const int split = item % splits, tile = item / splits;
-    const int row0 = (tile / tm) * kTileW, m0 = (tile % tm) * kMaxAct;
-    const int c_begin = kc_total * split / splits, c_end = kc_total * (split + 1) / splits;
-    auto issue = [&](int c) {
-      const int st = c % kStages;
-      const uint32_t sw = sbase + st * kStageBytes, sa = sw + kStageW;
-      const int kb = c * 64;
-      for (int u = tid; u < kTileW * 8; u += kGemmThreads) {
-        const int r = u >> 3, c8 = u & 7;
-        const bool ok = row0 + r < w_rows;
-        const __nv_bfloat16* src = Wk + (int64_t)(ok ? row0 + r : 0) * ldw + kb + c8 * 8;
-        cp_async16(sw + swz(r, c8), src, ok);
+    row0 = (tile / tm) * kTileW;
+    m0 = (tile % tm) * kMaxAct;
+    c_begin = kc_total * split / splits;
+    c_end = kc_total * (split + 1) / splits;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      uint32_t g = 0;
+      for (int item = blockIdx.x; item < units && !failed; item += gridDim.x) {
+        int row0, m0, c_begin, c_end;
+        unit_of(item, row0, m0, c_begin, c_end);
+        for (int c = c_begin; c < c_end; ++c, ++g) {
+          const int st = (int)(g % kStages);
+          const uint32_t use = g / kStages;
+          if (use > 0 && !tc::mbar_wait(empty(st), (use - 1) & 1u, kWaitLimit)) {
+            failed = true;
+            break;
+          }
+          const uint32_t sw = sbase + st * kStageBytes;
+          tc::mbar_arrive_expect_tx(full(st), kStageBytes);
+          tc::tma_load_2d(sw, &tw, c * 64, row0, full(st));
+          tc::tma_load_2d(sw + kStageW, &ta, c * 64, m0, full(st));
+        }
       }
-      for (int u = tid; u < kMaxAct * 8; u += kGemmThreads) {
-        const int r = u >> 3, c8 = u & 7;
-        const int kg = kb + c8 * 8;
-        const bool ok = m0 + r < m_act && kg < k_in;
-        const __nv_bfloat16* src = A + (ok ? (int64_t)(m0 + r) * k_in + kg : 0);
-        cp_async16(sa + swz(r, c8), src, ok);
-      }
-    };
-    // prologue: the first kStages-1 stages in flight
-    for (int c = c_begin; c < c_begin + kStages - 1; ++c) {
-      if (c < c_end) issue(c);
-      cp_async_commit();
+      // no copy may still be in flight when the block exits (after a timeout
+      // elsewhere): wait for the last use of every stage
+      for (uint32_t u = g > (uint32_t)kStages ? g - kStages : 0u; u < g; ++u)
+        tc::mbar_wait(full((int)(u % kStages)), (u / kStages) & 1u, kWaitLimit);
     }
-    uint32_t pending = 0;  // stages whose MMA commit has not been waited for
-    for (int c = c_begin; c < c_end; ++c) {
-      // chunk c has landed (groups committed so far: c - c_begin + kStages - 1)
-      cp_async_wait<kStages - 2>();
-      tc::fence_proxy_async();
-      if (__syncthreads_or(failed)) {
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      const uint32_t idesc = tc::idesc_bf16_f32(kTileW, kMaxAct);
+      uint32_t g = 0;
+      int it = 0;
+      for (int item = blockIdx.x; item < units && !failed; item += gridDim.x, ++it) {
+        int row0, m0, c_begin, c_end;
+        unit_of(item, row0, m0, c_begin, c_end);
+        const int a = it & 1;
+        const uint32_t use_acc = (uint32_t)it >> 1;
+        if (use_acc > 0 && !tc::mbar_wait(acc_empty(a), (use_acc - 1) & 1u, kWaitLimit)) {
+          failed = true;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t d = tmem + (uint32_t)(a * kAccCols);
+        for (int c = c_begin; c < c_end; ++c, ++g) {
+          const int st = (int)(g % kStages);
+          if (!tc::mbar_wait(full(st), (g / kStages) & 1u, kWaitLimit)) {
+            failed = true;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t sw = sbase + st * kStageBytes, sa = sw + kStageW;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            tc::mma_bf16(d, tc::desc_sw128(sw + ks * 32), tc::desc_sw128(sa + ks * 32), idesc,
+                         (c > c_begin || ks > 0) ? 1u : 0u);
+          tc::commit(empty(st));
+        }
+        if (failed) break;
+        tc::commit(acc_full(a));
+      }
+      // every MMA issued has finished before TMEM is freed
+      tc::commit(drain);
+      tc::mbar_wait(drain, 0, kWaitLimit);
+    }
+  } else {  // epilogue: warps 2..5 read TMEM lane quarters 2, 3, 0, 1
+    const int q = warp & 3;
+    int it = 0;
+    for (int item = blockIdx.x; item < units && !failed; item += gridDim.x, ++it) {
+      int row0, m0, c_begin, c_end;
+      unit_of(item, row0, m0, c_begin, c_end);
+      const int a = it & 1;
+      if (!tc::mbar_wait(acc_full(a), ((uint32_t)it >> 1) & 1u, kWaitLimit)) {
         failed = true;
         break;
       }
-      const int st = c % kStages;
-      if (tid == 0) {  // queued behind MMA(c - 1): the tensor pipe does not drain between chunks
-        tc::fence_after_sync();
-        const uint32_t sw = sbase + st * kStageBytes, sa = sw + kStageW;
+      tc::fence_after_sync();
+      const int r = q * 32 + lane, n = n_base + row0 + r;
+      const bool live = row0 + r < w_rows && n < n_out;
+      float scale = kLatticeScaleF;
+      if (rscale && live) scale = __fmul_rn(kLatticeScaleF, __half2float(__ushort_as_half(rscale[n])));
+      const uint32_t t0 = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kAccCols);
+      for (int col0 = 0; col0 < kAccCols; col0 += 16) {
+        float v[16];
+        tc::tmem_ld16(t0 + (uint32_t)col0, v);
+        if (live) {
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          tc::mma_bf16(tmem, tc::desc_sw128(sw + ks * 32), tc::desc_sw128(sa + ks * 32), idesc,
-                       (c > c_begin || ks > 0) ? 1u : 0u);
-        }
-        tc::commit(tc::smem_addr(&mbars[st]));
-      }
-      pending |= 1u << st;
-      // refill the stage MMA(c - 1) read with chunk c + kStages - 1
-      const int nxt = c + kStages - 1;
-      if (nxt < c_end) {
-        const int sn = nxt % kStages;
-        if ((pending >> sn) & 1u) {
-          const bool ok = tc::mbar_wait(tc::smem_addr(&mbars[sn]), (phase >> sn) & 1u, kWaitLimit);
-          phase ^= 1u << sn;
-          pending &= ~(1u << sn);
-          if (!ok) failed = true;
-        }
-        if (!failed) issue(nxt);
-      }
-      cp_async_commit();
-    }
-    cp_async_wait<0>();
-    // drain: wait for every outstanding stage commit (the last one covers all MMAs)
-    for (int st = 0; st < kStages; ++st) {
-      if ((pending >> st) & 1u) {
-        const bool ok = tc::mbar_wait(tc::smem_addr(&mbars[st]), (phase >> st) & 1u, kWaitLimit);
-        phase ^= 1u << st;
-        if (!ok) failed = true;
-      }
-    }
-    if (__syncthreads_or(failed)) {
-      failed = true;
-      break;
-    }
-    tc::fence_after_sync();
-    const int q = warp & 3, half = warp >> 2;
-    const int r = q * 32 + lane, n = n_base + row0 + r;
-    const bool live = row0 + r < w_rows && n < n_out;
-    float scale = kLatticeScaleF;
-    if (rscale && live) scale = __fmul_rn(kLatticeScaleF, __half2float(__ushort_as_half(rscale[n])));
-    for (int col0 = half * 128; col0 < half * 128 + 128; col0 += 16) {
-      float v[16];
-      tc::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col0, v);
-      if (live) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + col0 + j;
-          if (m < m_act) {
-            float* dst = Y + (int64_t)m * n_out + n;
-            if (splits > 1) atomicAdd(dst, v[j] * scale);  // two halves into zero: order-free
-            else *dst = v[j] * scale;
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + col0 + j;
+            if (m < m_act) {
+              float* dst = Y + (int64_t)m * n_out + n;
+              if (splits > 1) atomicAdd(dst, v[j] * scale);  // two halves into zero: order-free
+              else *dst = v[j] * scale;
+            }
           }
         }
       }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(acc_empty(a));
     }
-    tc::fence_before_sync();
-    __syncthreads();
   }
-  if (failed && tid == 0 && error_flag) atomicExch(error_flag, 1);
+  // every role has left its loop (each wait is bounded); reconverge, then free TMEM
+  __syncwarp();
+  if (failed && error_flag) atomicExch(error_flag, 1);
+  tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, kMaxAct);
+  tc::fence_after_sync();
+  if (warp == 0) tc::tmem_dealloc(tmem, 2 * kAccCols);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 row-major [rows, cols] (row stride `stride` elements), box 64 columns
+// x box_rows rows, 128-byte swizzle, zero fill outside the matrix.
+cudaError_t encode_bf16_map(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows, uint64_t stride,
+                            uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {stride * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
 // Sets the GEMM kernel's dynamic shared-memory limit on the current device
 // (the launcher also does this lazily on its first launch).
 cudaError_t gemm_configure_device() {
-  return cudaFuncSetAttribute(gemm_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmem);
+  return cudaFuncSetAttribute(gemm_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaSmem);
 }
 
 // The library's staging pool on the current device: stream-ordered like the
@@ -255,11 +307,14 @@ cudaError_t gemm_staged_launch(const Codebook& cb, const int64_t* idx, int64_t n
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(gemm_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmem);
+    e = gemm_configure_device();
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   const int ldw = (int)gemm_staging_ldw(bpr);
+  CUtensorMap ta;
+  e = encode_bf16_map(&ta, a, (uint64_t)k, (uint64_t)m, (uint64_t)k, kMaxAct);
+  if (e != cudaSuccess) return e;
   int64_t chunk = std::min<int64_t>(n_out, staging_bytes / ((int64_t)ldw * 2));
   if (chunk < n_out) chunk = chunk / kTileW * kTileW;
   if (chunk <= 0) return cudaErrorInvalidValue;
@@ -277,9 +332,11 @@ cudaError_t gemm_staged_launch(const Codebook& cb, const int64_t* idx, int64_t n
     e = decode_rows_bf16_launch(cb, idx + n0 * bpr, rows, (int)bpr, ldw, staging, stream);
     if (e != cudaSuccess) return e;
     const int items = ((rows + kTileW - 1) / kTileW) * (int)((m + kMaxAct - 1) / kMaxAct) * splits;
-    gemm_staged_kernel<<<std::min(items, sms), kGemmThreads, kStagedSmem, stream>>>(
-        static_cast<const __nv_bfloat16*>(staging), ldw, rows, (int)n0, (int)n_out, rscale,
-        static_cast<const __nv_bfloat16*>(a), (int)m, (int)k, y, splits, error_flag);
+    CUtensorMap tw;
+    e = encode_bf16_map(&tw, staging, (uint64_t)ldw, (uint64_t)rows, (uint64_t)ldw, kTileW);
+    if (e != cudaSuccess) return e;
+    gemm_tma_kernel<<<std::min(items, sms), kTmaThreads, kTmaSmem, stream>>>(
+        tw, ta, ldw / 64, rows, (int)n0, (int)n_out, rscale, (int)m, y, splits, error_flag);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

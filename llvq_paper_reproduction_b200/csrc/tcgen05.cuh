@@ -1,7 +1,7 @@
-// Thin inline-PTX wrappers for the sm_100a tensor-core path used by the fused
+// Thin inline-PTX wrappers for the sm_100a tensor-core path of the
 // dequant-GEMM: TMEM allocation, tcgen05.mma (kind::f16, operands in shared
-// memory), tcgen05.commit to an mbarrier, TMEM -> register loads, and bounded
-// mbarrier waits.
+// memory), tcgen05.commit to an mbarrier, TMEM -> register loads, TMA tile
+// loads (no multicast), mbarrier arrivals and bounded mbarrier waits.
 #pragma once
 
 #include <cstdint>
@@ -63,6 +63,25 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 
 __device__ __forceinline__ void mbar_init(uint32_t mbar_saddr, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(mbar_saddr), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t mbar_saddr) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(mbar_saddr) : "memory");
+}
+
+// Arrive and add `bytes` to the transaction count the phase waits for.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t mbar_saddr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar_saddr), "r"(bytes) : "memory");
+}
+
+// 2-D TMA tile load (no multicast) into this CTA's shared memory; the box's
+// bytes count toward the mbarrier's transaction.  x is the innermost
+// coordinate (its byte offset must be a multiple of 16).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst_saddr, const void* tmap, int x, int y, uint32_t mbar_saddr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst_saddr), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(mbar_saddr)
+      : "memory");
 }
 
 // Wait for phase `parity` of an mbarrier, giving up after `limit` polls.
