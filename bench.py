@@ -369,7 +369,8 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
     secs = max_over_ranks(e0.elapsed_time(e1) / 1000.0)
     t0 = time.perf_counter()
     local = {k: (r["indices"].cpu(), r["row_scale"].cpu()) for k, r in results.items()}
-    gathered = gather_to_rank0(specs, local, rank, world, device) if world > 1 else local
+    index_bytes = (mq.sg.bits + 7) // 8  # 48-bit shape-gain index -> 6 bytes per block on the wire
+    gathered = gather_to_rank0(specs, local, rank, world, device, index_bytes) if world > 1 else local
     gather_s = max_over_ranks(time.perf_counter() - t0)
     total = sum(s.blocks for s in specs)
     if rank == 0 and len(gathered) != len(specs):
@@ -377,7 +378,8 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
     return {"workload": f"Llama-2-7B linears, {args.model_layers} layers ({len(specs)} matrices, {total} blocks), "
                         "fp16 N(0, sigma_row^2) seed 2, Hadamard rotation, shape-gain 2 bits/dim, sharded by "
                         "matrix", "n_gpus": world, "blocks": total, "seconds": secs, "blocks_per_s": total / secs,
-            "gather_seconds": gather_s, "scaling": "strong (fixed model, split over the GPUs)"}
+            "gather_seconds": gather_s, "gather_bytes": total * index_bytes + sum(s.out_features for s in specs) * 4,
+            "scaling": "strong (fixed model, split over the GPUs)"}
 
 
 def rate_sweep_bench(q, x, device, stream, args) -> dict:

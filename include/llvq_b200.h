@@ -127,6 +127,28 @@ int llvq_gemm_noalloc(const llvq_codebook* cb, const int64_t* indices, int64_t n
                       const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
                       int32_t* error_flag, void* stream);
 
+/* Packed index storage (no reference counterpart: the reference keeps int64
+ * indices, _gpu.py:333).  An index takes index_bytes little-endian bytes
+ * (6 for the 48-bit codebook of shells 2..13 instead of 8); the all-ones
+ * value stands for the invalid index -1.
+ * llvq_pack_indices: int64 [n] -> packed [n * index_bytes]; entries that are
+ *   negative (other than -1) or do not fit below all-ones are counted into
+ *   *error_count (device int, may be NULL) and stored as all-ones.
+ * llvq_unpack_indices: packed -> int64 (all-ones -> -1).
+ * llvq_dequantize_packed: any LLVQ_OUT_* kind from packed indices (row_scale
+ *   and blocks_per_row for LLVQ_OUT_BF16_ROWSCALE only).
+ * llvq_gemm_packed: llvq_gemm reading packed indices.
+ * The codebook-bound calls need index_bytes with total_count <= all-ones. */
+int llvq_pack_indices(const int64_t* indices, int64_t n, int32_t index_bytes, uint8_t* packed, int32_t* error_count,
+                      void* stream);
+int llvq_unpack_indices(const uint8_t* packed, int64_t n, int32_t index_bytes, int64_t* indices, void* stream);
+int llvq_dequantize_packed(const llvq_codebook* cb, const uint8_t* packed, int32_t index_bytes, int64_t n, void* out,
+                           int32_t kind, const uint16_t* row_scale_f16, int64_t blocks_per_row,
+                           int32_t* error_count, void* stream);
+int llvq_gemm_packed(const llvq_codebook* cb, const uint8_t* packed, int32_t index_bytes, int64_t n_out,
+                     int64_t blocks_per_row, const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m,
+                     int64_t k, float* y, int32_t* error_flag, void* stream);
+
 /* Seeded random Hadamard rotation of each row of a [rows, cols] matrix, in
  * segments of `block` columns (a power of two, <= 4096, dividing cols):
  * forward out = H (signs * in) / sqrt(block), inverse out = signs * (H in) /

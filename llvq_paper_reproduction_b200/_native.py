@@ -35,7 +35,8 @@ EXPORTS = (
     "llvq_codebook_create", "llvq_codebook_destroy", "llvq_codebook_info", "llvq_quantize", "llvq_quantize_ex",
     "llvq_dequantize_lattice", "llvq_dequantize", "llvq_dequantize_bf16", "llvq_codeword_host",
     "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version", "llvq_gemm",
-    "llvq_hadamard", "llvq_gemm_noalloc",
+    "llvq_hadamard", "llvq_gemm_noalloc", "llvq_pack_indices", "llvq_unpack_indices", "llvq_dequantize_packed",
+    "llvq_gemm_packed",
 )
 
 _lib = None
@@ -66,6 +67,10 @@ def load() -> ctypes.CDLL:
             "llvq_gemm": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_gemm_noalloc": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_hadamard": (ctypes.c_int, [vp, i32, vp, i64, i64, i32, vp, i32, vp]),
+            "llvq_pack_indices": (ctypes.c_int, [vp, i64, i32, vp, vp, vp]),
+            "llvq_unpack_indices": (ctypes.c_int, [vp, i64, i32, vp, vp]),
+            "llvq_dequantize_packed": (ctypes.c_int, [vp, vp, i32, i64, vp, i32, vp, i64, vp, vp]),
+            "llvq_gemm_packed": (ctypes.c_int, [vp, vp, i32, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_codeword_host": (ctypes.c_int, [vp, i64, vp]),
             "llvq_encode_host": (ctypes.c_int, [vp, vp, P(i64)]),
             "llvq_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -168,10 +173,28 @@ class NativeCodebook:
         check(self._lib.llvq_gemm_noalloc(self.handle, idx_ptr, n_out, blocks_per_row, scale_ptr, a_ptr, m, k, y_ptr,
                                           err_ptr, stream), "llvq_gemm_noalloc")
 
+    def dequantize_packed(self, packed_ptr: int, index_bytes: int, n: int, out_ptr: int, kind: int,
+                          scale_ptr: int | None, blocks_per_row: int, err_ptr: int | None, stream: int) -> None:
+        check(self._lib.llvq_dequantize_packed(self.handle, packed_ptr, index_bytes, n, out_ptr, kind, scale_ptr,
+                                               blocks_per_row, err_ptr, stream), "llvq_dequantize_packed")
+
+    def gemm_packed(self, packed_ptr: int, index_bytes: int, n_out: int, blocks_per_row: int, scale_ptr: int | None,
+                    a_ptr: int, m: int, k: int, y_ptr: int, err_ptr: int | None, stream: int) -> None:
+        check(self._lib.llvq_gemm_packed(self.handle, packed_ptr, index_bytes, n_out, blocks_per_row, scale_ptr,
+                                         a_ptr, m, k, y_ptr, err_ptr, stream), "llvq_gemm_packed")
+
     def dequantize_bf16(self, idx_ptr: int, n: int, scale_ptr: int, blocks_per_row: int, out_ptr: int,
                         err_ptr: int | None, stream: int) -> None:
         check(self._lib.llvq_dequantize_bf16(self.handle, idx_ptr, n, scale_ptr, blocks_per_row, out_ptr, err_ptr,
                                              stream), "llvq_dequantize_bf16")
+
+
+def pack_indices(idx_ptr: int, n: int, index_bytes: int, out_ptr: int, err_ptr: int | None, stream: int) -> None:
+    check(load().llvq_pack_indices(idx_ptr, n, index_bytes, out_ptr, err_ptr, stream), "llvq_pack_indices")
+
+
+def unpack_indices(packed_ptr: int, n: int, index_bytes: int, out_ptr: int, stream: int) -> None:
+    check(load().llvq_unpack_indices(packed_ptr, n, index_bytes, out_ptr, stream), "llvq_unpack_indices")
 
 
 def hadamard(in_ptr: int, in_is_half: bool, out_ptr: int, rows: int, cols: int, block: int, signs_ptr: int,

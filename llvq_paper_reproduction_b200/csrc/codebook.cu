@@ -467,7 +467,7 @@ int llvq_dequantize_lattice(const llvq_codebook* h, const int64_t* indices, int6
                             int32_t* error_count, void* stream) {
   if (n < 0 || (n > 0 && (!indices || !out))) return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad dequantize arguments");
   return on_device(h, [&] {
-    return llvq::dequantize_launch(h->cb, indices, n, out, 0, nullptr, 1, error_count, (cudaStream_t)stream);
+    return llvq::dequantize_launch(h->cb, {indices, 8}, n, out, 0, nullptr, 1, error_count, (cudaStream_t)stream);
   });
 }
 
@@ -476,7 +476,7 @@ int llvq_dequantize(const llvq_codebook* h, const int64_t* indices, int64_t n, f
   if (n < 0 || (n > 0 && (!indices || !out))) return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad dequantize arguments");
   if (kind != LLVQ_OUT_F32 && kind != LLVQ_OUT_F32_DOUBLE) return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad output kind");
   return on_device(h, [&] {
-    return llvq::dequantize_launch(h->cb, indices, n, out, kind, nullptr, 1, error_count, (cudaStream_t)stream);
+    return llvq::dequantize_launch(h->cb, {indices, 8}, n, out, kind, nullptr, 1, error_count, (cudaStream_t)stream);
   });
 }
 
@@ -485,17 +485,22 @@ int llvq_dequantize_bf16(const llvq_codebook* h, const int64_t* indices, int64_t
   if (n < 0 || blocks_per_row <= 0 || (n > 0 && (!indices || !out_bf16 || !row_scale_f16)))
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad dequantize arguments");
   return on_device(h, [&] {
-    return llvq::dequantize_launch(h->cb, indices, n, out_bf16, 3, row_scale_f16, blocks_per_row, error_count,
+    return llvq::dequantize_launch(h->cb, {indices, 8}, n, out_bf16, 3, row_scale_f16, blocks_per_row, error_count,
                                    (cudaStream_t)stream);
   });
 }
 
-int llvq_gemm(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
+}  // extern "C"
+
+namespace {
+
+// Shared by llvq_gemm and llvq_gemm_packed.
+int gemm_impl(const llvq_codebook* h, llvq::IndexSource src, int64_t n_out, int64_t blocks_per_row,
               const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
               int32_t* error_flag, void* stream) {
   if (m < 0 || n_out < 0 || blocks_per_row <= 0 || k <= 0 || k % 8 || k > 24 * blocks_per_row)
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes: need k % 8 == 0 and 0 < k <= 24 * blocks_per_row");
-  if (m > 0 && n_out > 0 && (!indices || !a_bf16 || !y || (reinterpret_cast<uintptr_t>(a_bf16) & 15)))
+  if (m > 0 && n_out > 0 && (!src.ptr || !a_bf16 || !y || (reinterpret_cast<uintptr_t>(a_bf16) & 15)))
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm pointers: null, or activations not 16-byte aligned");
   if (m > (int64_t)INT32_MAX || n_out > (int64_t)INT32_MAX || blocks_per_row > (int64_t)INT32_MAX)
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
@@ -510,11 +515,71 @@ int llvq_gemm(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int
     void* staging = nullptr;
     e = cudaMallocFromPoolAsync(&staging, (size_t)bytes, pool, (cudaStream_t)stream);
     if (e != cudaSuccess) return e;
-    e = llvq::gemm_staged_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
+    e = llvq::gemm_staged_launch(h->cb, src, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
                                  staging, bytes, (cudaStream_t)stream);
     const cudaError_t ef = cudaFreeAsync(staging, (cudaStream_t)stream);
     return e != cudaSuccess ? e : ef;
   });
+}
+
+// Packed indices of `index_bytes` bytes must leave the all-ones value free
+// for the invalid index.
+int check_index_bytes(const llvq_codebook* h, int32_t index_bytes) {
+  if (!h) return fail(LLVQ_ERR_INVALID_ARGUMENT, "null codebook");
+  if (index_bytes < 1 || index_bytes > 8) return fail(LLVQ_ERR_INVALID_ARGUMENT, "index_bytes must be 1..8");
+  if (index_bytes < 8 && (uint64_t)h->cb.total > (~0ull >> (64 - 8 * index_bytes)))
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "index_bytes too small for this codebook's index range");
+  return LLVQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int llvq_gemm(const llvq_codebook* h, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
+              const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
+              int32_t* error_flag, void* stream) {
+  return gemm_impl(h, {indices, 8}, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag, stream);
+}
+
+int llvq_gemm_packed(const llvq_codebook* h, const uint8_t* packed, int32_t index_bytes, int64_t n_out,
+                     int64_t blocks_per_row, const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m,
+                     int64_t k, float* y, int32_t* error_flag, void* stream) {
+  const int st = check_index_bytes(h, index_bytes);
+  if (st != LLVQ_OK) return st;
+  return gemm_impl(h, {packed, index_bytes}, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag,
+                   stream);
+}
+
+int llvq_dequantize_packed(const llvq_codebook* h, const uint8_t* packed, int32_t index_bytes, int64_t n, void* out,
+                           int32_t kind, const uint16_t* row_scale_f16, int64_t blocks_per_row,
+                           int32_t* error_count, void* stream) {
+  const int st = check_index_bytes(h, index_bytes);
+  if (st != LLVQ_OK) return st;
+  if (n < 0 || (n > 0 && (!packed || !out))) return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad dequantize arguments");
+  if (kind < LLVQ_OUT_INT64 || kind > LLVQ_OUT_BF16_ROWSCALE) return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad output kind");
+  if (kind == LLVQ_OUT_BF16_ROWSCALE && (blocks_per_row <= 0 || (n > 0 && !row_scale_f16)))
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "bf16 output needs row scales and blocks_per_row > 0");
+  return on_device(h, [&] {
+    return llvq::dequantize_launch(h->cb, {packed, index_bytes}, n, out, kind, row_scale_f16,
+                                   kind == LLVQ_OUT_BF16_ROWSCALE ? blocks_per_row : 1, error_count,
+                                   (cudaStream_t)stream);
+  });
+}
+
+int llvq_pack_indices(const int64_t* indices, int64_t n, int32_t index_bytes, uint8_t* packed, int32_t* error_count,
+                      void* stream) {
+  if (index_bytes < 1 || index_bytes > 8) return fail(LLVQ_ERR_INVALID_ARGUMENT, "index_bytes must be 1..8");
+  if (n < 0 || (n > 0 && (!indices || !packed))) return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad pack arguments");
+  const cudaError_t e = llvq::pack_indices_launch(indices, n, index_bytes, packed, error_count, (cudaStream_t)stream);
+  return e == cudaSuccess ? LLVQ_OK : cuda_fail(e, "pack launch");
+}
+
+int llvq_unpack_indices(const uint8_t* packed, int64_t n, int32_t index_bytes, int64_t* indices, void* stream) {
+  if (index_bytes < 1 || index_bytes > 8) return fail(LLVQ_ERR_INVALID_ARGUMENT, "index_bytes must be 1..8");
+  if (n < 0 || (n > 0 && (!indices || !packed))) return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad unpack arguments");
+  const cudaError_t e = llvq::unpack_indices_launch(packed, n, index_bytes, indices, (cudaStream_t)stream);
+  return e == cudaSuccess ? LLVQ_OK : cuda_fail(e, "unpack launch");
 }
 
 static_assert(LLVQ_GEMM_NOALLOC_STAGING_BYTES == llvq::kNoAllocStagingBytes, "staging size mismatch");
@@ -538,7 +603,7 @@ int llvq_gemm_noalloc(const llvq_codebook* h, const int64_t* indices, int64_t n_
     void* staging = nullptr;
     cudaError_t e = llvq::noalloc_staging(&staging);  // first call on a device: symbol lookup
     if (e != cudaSuccess) return e;
-    return llvq::gemm_staged_launch(h->cb, indices, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
+    return llvq::gemm_staged_launch(h->cb, {indices, 8}, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
                                     error_flag, staging, llvq::kNoAllocStagingBytes, (cudaStream_t)stream);
   });
 }

@@ -21,8 +21,23 @@ constexpr int kDeqThreads = 256;
 // dequant workload; the decode is issue-bound and latency-bound in turn.
 constexpr int kDeqMinBlocks = 5;
 
+// Index i of a source: one 8-byte load, or the packed bytes (6-byte indices,
+// the 48-bit codebook's, as three 2-byte loads); all-ones packed -> -1.
+__device__ __forceinline__ int64_t load_index(IndexSource src, int64_t i) {
+  if (src.bytes == 8) return __ldg(static_cast<const int64_t*>(src.ptr) + i);
+  uint64_t v = 0;
+  if (src.bytes == 6) {
+    const uint16_t* h = static_cast<const uint16_t*>(src.ptr) + i * 3;
+    v = (uint64_t)__ldg(h) | ((uint64_t)__ldg(h + 1) << 16) | ((uint64_t)__ldg(h + 2) << 32);
+  } else {
+    const uint8_t* b = static_cast<const uint8_t*>(src.ptr) + i * src.bytes;
+    for (int k = 0; k < src.bytes; ++k) v |= (uint64_t)__ldg(b + k) << (8 * k);
+  }
+  return v == (~0ull >> (64 - 8 * src.bytes)) ? -1 : (int64_t)v;
+}
+
 template <int KIND>
-__global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(const int64_t* __restrict__ index, int64_t n,
+__global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(IndexSource index, int64_t n,
                                                               DevBook book, void* __restrict__ out,
                                                               const uint16_t* __restrict__ row_scale,
                                                               int64_t blocks_per_row, int* error_count) {
@@ -32,7 +47,7 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(con
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   int y[kDim];
-  const bool ok = decode_index(__ldg(index + i), book, sh, y);
+  const bool ok = decode_index(load_index(index, i), book, sh, y);
   if (!ok && error_count) atomicAdd(error_count, 1);
   if constexpr (KIND == 0) {
     longlong2* o = reinterpret_cast<longlong2*>(static_cast<long long*>(out) + i * kDim);
@@ -68,7 +83,7 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(con
 // Weight staging for the large-batch GEMM: indices [rows, bpr] -> bf16
 // integer codewords [rows, ldw] (columns >= 24 * bpr zero), one thread per
 // (row, block) plus the padding.
-__global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(const int64_t* __restrict__ index, int rows,
+__global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(IndexSource index, int rows,
                                                                        int bpr, int ldw, DevBook book,
                                                                        __nv_bfloat16* __restrict__ out) {
   __shared__ DecodeShared sh;
@@ -81,7 +96,7 @@ __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(const int
   __nv_bfloat16* o = out + (int64_t)r * ldw;
   if (b < bpr) {
     int y[kDim];
-    decode_index(__ldg(index + (int64_t)r * bpr + b), book, sh, y);
+    decode_index(load_index(index, (int64_t)r * bpr + b), book, sh, y);
     uint4* dst = reinterpret_cast<uint4*>(o + b * kDim);
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
@@ -98,7 +113,7 @@ __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(const int
   }
 }
 
-cudaError_t decode_rows_bf16_launch(const Codebook& cb, const int64_t* index, int rows, int bpr, int ldw, void* out,
+cudaError_t decode_rows_bf16_launch(const Codebook& cb, IndexSource index, int rows, int bpr, int ldw, void* out,
                                     cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const int64_t n = (int64_t)rows * (ldw / kDim + 1);
@@ -107,7 +122,7 @@ cudaError_t decode_rows_bf16_launch(const Codebook& cb, const int64_t* index, in
   return cudaGetLastError();
 }
 
-cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t n, void* out, int kind,
+cudaError_t dequantize_launch(const Codebook& cb, IndexSource index, int64_t n, void* out, int kind,
                               const uint16_t* row_scale, int64_t blocks_per_row, int* error_count,
                               cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
@@ -119,6 +134,42 @@ cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t 
     case 3: dequant_kernel<3><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, error_count); break;
     default: return cudaErrorInvalidValue;
   }
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------- packed indices
+
+__global__ void pack_kernel(const int64_t* __restrict__ in, int64_t n, int bytes, uint8_t* __restrict__ out,
+                            int* error_count) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t ones = ~0ull >> (64 - 8 * bytes);
+  const int64_t v = in[i];
+  uint64_t u = (uint64_t)v;
+  if (v < 0 || u >= ones) {  // -1 and anything that does not fit become all-ones
+    if (v != -1 && error_count) atomicAdd(error_count, 1);
+    u = ones;
+  }
+  uint8_t* o = out + i * bytes;
+  for (int k = 0; k < bytes; ++k) o[k] = (uint8_t)(u >> (8 * k));
+}
+
+__global__ void unpack_kernel(const uint8_t* __restrict__ in, int64_t n, int bytes, int64_t* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  out[i] = load_index(IndexSource{in, bytes}, i);
+}
+
+cudaError_t pack_indices_launch(const int64_t* in, int64_t n, int bytes, uint8_t* out, int* error_count,
+                                cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  pack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(in, n, bytes, out, error_count);
+  return cudaGetLastError();
+}
+
+cudaError_t unpack_indices_launch(const uint8_t* in, int64_t n, int bytes, int64_t* out, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  unpack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(in, n, bytes, out);
   return cudaGetLastError();
 }
 

@@ -295,7 +295,7 @@ int64_t gemm_staging_bytes(int64_t n_out, int64_t bpr, int64_t budget) {
   return std::min(rows, n_out) * row_bytes;
 }
 
-cudaError_t gemm_staged_launch(const Codebook& cb, const int64_t* idx, int64_t n_out, int64_t bpr,
+cudaError_t gemm_staged_launch(const Codebook& cb, IndexSource idx, int64_t n_out, int64_t bpr,
                                const uint16_t* rscale, const void* a, int64_t m, int64_t k, float* y,
                                int* error_flag, void* staging, int64_t staging_bytes, cudaStream_t stream) {
   if (m <= 0 || n_out <= 0) return cudaSuccess;
@@ -329,7 +329,8 @@ cudaError_t gemm_staged_launch(const Codebook& cb, const int64_t* idx, int64_t n
   }
   for (int64_t n0 = 0; n0 < n_out; n0 += chunk) {
     const int rows = (int)std::min<int64_t>(chunk, n_out - n0);
-    e = decode_rows_bf16_launch(cb, idx + n0 * bpr, rows, (int)bpr, ldw, staging, stream);
+    const IndexSource part{static_cast<const uint8_t*>(idx.ptr) + n0 * bpr * idx.bytes, idx.bytes};
+    e = decode_rows_bf16_launch(cb, part, rows, (int)bpr, ldw, staging, stream);
     if (e != cudaSuccess) return e;
     const int items = ((rows + kTileW - 1) / kTileW) * (int)((m + kMaxAct - 1) / kMaxAct) * splits;
     CUtensorMap tw;

@@ -47,11 +47,25 @@ const SpecEntry* spec_table(int* count);
 cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long long* index, long long* pair,
                             float* score, cudaStream_t stream, bool force_runtime);
 
+// Where a kernel reads its indices: int64 (bytes = 8) or packed little-endian
+// unsigned integers of 1..7 bytes, the all-ones value standing for an
+// invalid index (-1).
+struct IndexSource {
+  const void* ptr;
+  int bytes;
+};
+
 // kind: 0 int64 codewords, 1 fp32 (fp32(1/sqrt 8) * k, torch semantics),
 // 2 fp32 (fp32 of the double product), 3 bf16 with per-row fp16 scale.
-cudaError_t dequantize_launch(const Codebook& cb, const int64_t* index, int64_t n, void* out, int kind,
+cudaError_t dequantize_launch(const Codebook& cb, IndexSource index, int64_t n, void* out, int kind,
                               const uint16_t* row_scale, int64_t blocks_per_row, int* error_count,
                               cudaStream_t stream);
+
+// int64 <-> packed indices; pack counts (and writes all-ones for) entries
+// that are negative or do not fit.
+cudaError_t pack_indices_launch(const int64_t* in, int64_t n, int bytes, uint8_t* out, int* error_count,
+                                cudaStream_t stream);
+cudaError_t unpack_indices_launch(const uint8_t* in, int64_t n, int bytes, int64_t* out, cudaStream_t stream);
 
 // Dequant-GEMM: weights decoded (a chunk of rows at a time) into a bf16
 // staging buffer of staging_bytes (rows padded to gemm_staging_ldw(bpr)
@@ -62,9 +76,9 @@ constexpr int kMaxDevices = 64;
 int64_t gemm_staging_ldw(int64_t bpr);
 cudaError_t gemm_staging_pool(cudaMemPool_t* pool);
 int64_t gemm_staging_bytes(int64_t n_out, int64_t bpr, int64_t budget);
-cudaError_t decode_rows_bf16_launch(const Codebook& cb, const int64_t* index, int rows, int bpr, int ldw, void* out,
+cudaError_t decode_rows_bf16_launch(const Codebook& cb, IndexSource index, int rows, int bpr, int ldw, void* out,
                                     cudaStream_t stream);
-cudaError_t gemm_staged_launch(const Codebook& cb, const int64_t* idx, int64_t n_out, int64_t bpr,
+cudaError_t gemm_staged_launch(const Codebook& cb, IndexSource idx, int64_t n_out, int64_t bpr,
                                const uint16_t* rscale, const void* a, int64_t m, int64_t k, float* y,
                                int* error_flag, void* staging, int64_t staging_bytes, cudaStream_t stream);
 

@@ -17,8 +17,9 @@ Per matrix:
 Sharding: matrices are independent, so ranks own whole matrices (greedy
 balance of block counts), quantize them with no inter-GPU traffic,
 checkpoint each finished matrix (atomic write; a restart skips finished
-ones), and finally gather every index tensor and row scale to rank 0 with one
-all-gather over the process group (NCCL on GPUs, gloo in CPU tests).
+ones), and finally gather every index tensor (packed to 6 bytes per block)
+and row scale to rank 0 with one all-gather over the process group (NCCL on
+GPUs, gloo in CPU tests).
 """
 from __future__ import annotations
 
@@ -176,9 +177,25 @@ def run_shard(specs: Sequence[MatrixSpec], rank: int, world: int, out_dir: Path,
     return done
 
 
-def gather_to_rank0(specs: Sequence[MatrixSpec], local: dict, rank: int, world: int, device) -> dict | None:
-    """One all-gather of every rank's indices and scales (flattened, padded
-    to the largest shard); rank 0 unpacks them per matrix."""
+def pack_host(indices: torch.Tensor, index_bytes: int) -> torch.Tensor:
+    """Non-negative int64 indices (CPU) -> uint8 [n, index_bytes], little-endian."""
+    flat = indices.reshape(-1).contiguous()
+    return flat.view(torch.uint8).view(-1, 8)[:, :index_bytes].contiguous()
+
+
+def unpack_host(packed: torch.Tensor, index_bytes: int) -> torch.Tensor:
+    """uint8 [n, index_bytes] (CPU) -> int64 [n]."""
+    out = torch.zeros((packed.shape[0], 8), dtype=torch.uint8)
+    out[:, :index_bytes] = packed
+    return out.view(torch.int64).reshape(-1)
+
+
+def gather_to_rank0(specs: Sequence[MatrixSpec], local: dict, rank: int, world: int, device,
+                    index_bytes: int = 8) -> dict | None:
+    """One all-gather of every rank's indices (as index_bytes little-endian
+    bytes each: 6 for the 48-bit shape-gain index, a quarter less than int64)
+    and row scales, flattened and padded to the largest shard; rank 0 unpacks
+    them per matrix into int64."""
     import torch.distributed as dist
 
     plan = plan_shards(specs, world)
@@ -186,11 +203,13 @@ def gather_to_rank0(specs: Sequence[MatrixSpec], local: dict, rank: int, world: 
     rows = [sum(specs[i].out_features for i in p) for p in plan]
     mine_idx = [local[specs[i].key][0].reshape(-1) for i in plan[rank]]
     mine_sc = [local[specs[i].key][1].reshape(-1).view(torch.int16).to(torch.int32) for i in plan[rank]]
-    flat_idx = torch.zeros(max(sizes), dtype=torch.int64)
+    flat_idx = torch.zeros((max(sizes), index_bytes), dtype=torch.uint8)
     flat_sc = torch.zeros(max(rows), dtype=torch.int32)
     if mine_idx:
         cat = torch.cat(mine_idx)
-        flat_idx[: cat.numel()] = cat
+        if int(cat.min()) < 0 or (index_bytes < 8 and int(cat.max()) >> (8 * index_bytes)):
+            raise ValueError(f"indices do not fit {index_bytes} bytes")
+        flat_idx[: cat.numel()] = pack_host(cat, index_bytes)
         cs = torch.cat(mine_sc)
         flat_sc[: cs.numel()] = cs
     flat_idx, flat_sc = flat_idx.to(device), flat_sc.to(device)
@@ -203,7 +222,7 @@ def gather_to_rank0(specs: Sequence[MatrixSpec], local: dict, rank: int, world: 
     result = {}
     for r in range(world):
         oi, os_ = 0, 0
-        gi, gs = all_idx[r].cpu(), all_sc[r].cpu()
+        gi, gs = unpack_host(all_idx[r].cpu(), index_bytes), all_sc[r].cpu()
         for i in plan[r]:
             s = specs[i]
             result[s.key] = (gi[oi: oi + s.blocks].view(s.out_features, s.blocks_per_row),
@@ -239,7 +258,7 @@ def main():
     torch.cuda.synchronize()
     t_local = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=device)
     dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
-    result = gather_to_rank0(specs, local_res, rank, world, device)
+    result = gather_to_rank0(specs, local_res, rank, world, device, index_bytes=(mq.sg.bits + 7) // 8)
     if rank == 0:
         total = sum(s.blocks for s in specs)
         print(f"{len(result)} matrices, {total} blocks in {t_local.item():.2f} s "

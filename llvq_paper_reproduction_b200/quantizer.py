@@ -174,37 +174,84 @@ class LeechLatticeVectorQuantizerGpu:
         self._raise_if_bad(err)
         return out.reshape(*shape, DIM)
 
-    def dequantize_bf16(self, indices: torch.Tensor, row_scale: torch.Tensor) -> torch.Tensor:
-        """bf16 weights: bf16(dequantize(indices) * row_scale[row]) for indices
-        [rows, blocks_per_row] and fp16 row_scale [rows] (no reference
-        counterpart)."""
-        self._require_cuda("dequantize_bf16")
-        if indices.dim() != 2 or row_scale.shape != (indices.shape[0],) or row_scale.dtype != torch.float16:
-            raise ValueError("expected indices [rows, blocks] and fp16 row_scale [rows]")
+    # ---------------------------------------------------------- packed indices
+    @property
+    def index_bytes(self) -> int:
+        """Bytes per packed index: the smallest count whose all-ones value
+        (the invalid-index marker) lies above every index (6 at shells 2..13)."""
+        return max(1, (self.total_count.bit_length() + 7) // 8)
+
+    def pack_indices(self, indices: torch.Tensor) -> torch.Tensor:
+        """int64 indices [...] -> uint8 [..., index_bytes] little-endian; -1
+        (a NaN/Inf row) becomes all-ones.  No reference counterpart."""
+        self._require_cuda("pack_indices")
         idx = indices.to(device=self.device, dtype=torch.long).contiguous()
-        sc = row_scale.to(self.device).contiguous()
-        out = torch.empty((idx.shape[0], idx.shape[1] * DIM), dtype=torch.bfloat16, device=self.device)
+        b = self.index_bytes
+        out = torch.empty((*idx.shape, b), dtype=torch.uint8, device=self.device)
         err = self._error_counter()
         with torch.cuda.device(self.device):
-            self._book().dequantize_bf16(idx.data_ptr(), idx.numel(), sc.data_ptr(), idx.shape[1], out.data_ptr(),
-                                         err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            _native.pack_indices(idx.data_ptr(), idx.numel(), b, out.data_ptr(), err.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream)
+        if int(err.item()):
+            raise IndexError("index does not fit the packed width")
+        return out
+
+    def unpack_indices(self, packed: torch.Tensor) -> torch.Tensor:
+        """uint8 [..., index_bytes] -> int64 [...] (all-ones -> -1)."""
+        self._require_cuda("unpack_indices")
+        pk = self._packed(packed)
+        out = torch.empty(pk.shape[:-1], dtype=torch.long, device=self.device)
+        with torch.cuda.device(self.device):
+            _native.unpack_indices(pk.data_ptr(), out.numel(), self.index_bytes, out.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream)
+        return out
+
+    def _packed(self, packed: torch.Tensor) -> torch.Tensor:
+        if packed.dtype != torch.uint8 or packed.dim() < 1 or packed.shape[-1] != self.index_bytes:
+            raise ValueError(f"packed indices must be uint8 [..., {self.index_bytes}]")
+        return packed.to(self.device).contiguous()
+
+    def dequantize_bf16(self, indices: torch.Tensor, row_scale: torch.Tensor) -> torch.Tensor:
+        """bf16 weights: bf16(dequantize(indices) * row_scale[row]) for indices
+        [rows, blocks_per_row] (int64, or packed uint8 [rows, blocks_per_row,
+        index_bytes]) and fp16 row_scale [rows] (no reference counterpart)."""
+        self._require_cuda("dequantize_bf16")
+        packed = indices.dtype == torch.uint8
+        rows_blocks = indices.shape[:-1] if packed else indices.shape
+        if len(rows_blocks) != 2 or row_scale.shape != (rows_blocks[0],) or row_scale.dtype != torch.float16:
+            raise ValueError("expected indices [rows, blocks] and fp16 row_scale [rows]")
+        rows, bpr = rows_blocks
+        sc = row_scale.to(self.device).contiguous()
+        out = torch.empty((rows, bpr * DIM), dtype=torch.bfloat16, device=self.device)
+        err = self._error_counter()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        with torch.cuda.device(self.device):
+            if packed:
+                pk = self._packed(indices)
+                self._book().dequantize_packed(pk.data_ptr(), self.index_bytes, rows * bpr, out.data_ptr(),
+                                               _native.OUT_BF16_ROWSCALE, sc.data_ptr(), bpr, err.data_ptr(), stream)
+            else:
+                idx = indices.to(device=self.device, dtype=torch.long).contiguous()
+                self._book().dequantize_bf16(idx.data_ptr(), idx.numel(), sc.data_ptr(), bpr, out.data_ptr(),
+                                             err.data_ptr(), stream)
         self._raise_if_bad(err)
         return out
 
     def gemm(self, a: torch.Tensor, indices: torch.Tensor, row_scale: torch.Tensor | None = None) -> torch.Tensor:
         """Dequant-GEMM: ``a @ W.T`` in fp32 for bf16 activations ``a`` [m, k]
-        and a weight given by its indices [n, blocks] (W[n] =
-        dequantize(indices[n]).flatten()[:k] * row_scale[n]).  The weight is
-        decoded into a bf16 staging buffer (stream-ordered, at most 256 MiB,
-        chunk by chunk beyond that) that a pipelined tcgen05 GEMM reads (no
-        reference counterpart)."""
+        and a weight given by its indices [n, blocks] (int64, or packed uint8
+        [n, blocks, index_bytes]; W[n] = dequantize(indices[n]).flatten()[:k]
+        * row_scale[n]).  The weight is decoded into a bf16 staging buffer
+        (stream-ordered, at most 256 MiB, chunk by chunk beyond that) that a
+        pipelined tcgen05 GEMM reads (no reference counterpart)."""
         self._require_cuda("gemm")
-        if a.dim() != 2 or indices.dim() != 2:
-            raise ValueError("expected a [m, k] and indices [n, blocks]")
+        packed = indices.dtype == torch.uint8
+        if a.dim() != 2 or indices.dim() != (3 if packed else 2):
+            raise ValueError("expected a [m, k] and indices [n, blocks] (packed: [n, blocks, index_bytes])")
         m, k = a.shape
-        n, bpr = indices.shape
+        n, bpr = indices.shape[:2]
         a16 = a.to(device=self.device, dtype=torch.bfloat16).contiguous()
-        idx = indices.to(device=self.device, dtype=torch.long).contiguous()
+        idx = self._packed(indices) if packed else indices.to(device=self.device, dtype=torch.long).contiguous()
         sc = None
         if row_scale is not None:
             if row_scale.shape != (n,):
@@ -213,10 +260,16 @@ class LeechLatticeVectorQuantizerGpu:
         y = torch.empty((m, n), dtype=torch.float32, device=self.device)
         err = self._error_counter()
         with torch.cuda.device(self.device):
-            self._book().gemm(idx.data_ptr(), n, bpr, sc.data_ptr() if sc is not None else None, a16.data_ptr(), m, k,
-                              y.data_ptr(), err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            stream = torch.cuda.current_stream().cuda_stream
+            sp = sc.data_ptr() if sc is not None else None
+            if packed:
+                self._book().gemm_packed(idx.data_ptr(), self.index_bytes, n, bpr, sp, a16.data_ptr(), m, k,
+                                         y.data_ptr(), err.data_ptr(), stream)
+            else:
+                self._book().gemm(idx.data_ptr(), n, bpr, sp, a16.data_ptr(), m, k, y.data_ptr(), err.data_ptr(),
+                                  stream)
         if int(err.item()):
-            raise RuntimeError("tensor-core wait timed out in the fused dequant-GEMM")
+            raise RuntimeError("tensor-core wait timed out in the dequant-GEMM")
         return y
 
     def _dequantize_lattice_cuda(self, indices: torch.Tensor) -> torch.Tensor:

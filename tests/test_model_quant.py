@@ -45,6 +45,15 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def test_host_pack_roundtrip():
+    from llvq_paper_reproduction_b200.model_quant import pack_host, unpack_host
+
+    idx = torch.tensor([0, 1, (1 << 40) - 1, 123456789012], dtype=torch.int64)
+    pk = pack_host(idx, 5)
+    assert pk.shape == (4, 5) and pk.dtype == torch.uint8
+    assert torch.equal(unpack_host(pk, 5), idx)
+
+
 def _worker(rank, world, port, out_dir, fail_rank, result_path):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -55,7 +64,7 @@ def _worker(rank, world, port, out_dir, fail_rank, result_path):
     if rank == fail_rank:
         raise RuntimeError("injected failure on this rank")
     local = run_shard(specs, rank, world, Path(out_dir), fake_quantize)
-    res = gather_to_rank0(specs, local, rank, world, "cpu")
+    res = gather_to_rank0(specs, local, rank, world, "cpu", index_bytes=5)  # fake indices < 2^40
     if rank == 0:
         torch.save(res, result_path)
     dist.destroy_process_group()
