@@ -302,9 +302,15 @@ class LeechLatticeVectorQuantizerGpu:
         tensor out; a sequence input returns an int)."""
         return self.quantize_cuda(vector)
 
+    # rows per chunk when a large batch comes from host memory
+    HOST_CHUNK_ROWS = 1 << 20
+
     def quantize_cuda(self, vector, return_details: bool = False, table_driven: bool = False):
         self._require_cuda("quantize_cuda")
         tensor_input = torch.is_tensor(vector)
+        if (tensor_input and vector.device.type == "cpu" and not return_details and not table_driven
+                and vector.dim() >= 2 and vector.shape[-1] == DIM and vector.numel() // DIM > 2 * self.HOST_CHUNK_ROWS):
+            return self._quantize_from_host(vector)
         x = torch.as_tensor(vector, dtype=self.dtype, device=self.device)
         if x.shape[-1] != DIM:
             raise ValueError(f"expected last dimension {DIM}, got {x.shape[-1]}")
@@ -327,6 +333,44 @@ class LeechLatticeVectorQuantizerGpu:
         if not tensor_input:
             return int(indices.item())
         return indices
+
+    def _quantize_from_host(self, vector: torch.Tensor) -> torch.Tensor:
+        """Large host batches: copy chunk i+1 to the device on a side stream
+        while chunk i is quantized on the current stream (two device buffers,
+        events in both directions), so the host->device copy hides behind the
+        search.  Same indices as the single-copy path (rows are independent)."""
+        shape = vector.shape[:-1]
+        x = vector.reshape(-1, DIM)
+        if x.dtype != torch.float32:
+            x = x.to(torch.float32)
+        x = x.contiguous()
+        n, c = x.shape[0], self.HOST_CHUNK_ROWS
+        indices = torch.empty((n,), dtype=torch.long, device=self.device)
+        pair = torch.empty((c,), dtype=torch.long, device=self.device)
+        score = torch.empty((c,), dtype=torch.float32, device=self.device)
+        bufs = [torch.empty((c, DIM), dtype=torch.float32, device=self.device) for _ in range(2)]
+        compute = torch.cuda.current_stream(self.device)
+        copy = torch.cuda.Stream(device=self.device)
+        copied = [torch.cuda.Event() for _ in range(2)]
+        used = [None, None]
+        book = self._book()
+        # the buffers may be memory that earlier work on the current stream
+        # still reads (the caching allocator recycles it in stream order)
+        copy.wait_stream(compute)
+        with torch.cuda.device(self.device):
+            for i, r0 in enumerate(range(0, n, c)):
+                rows, b = min(c, n - r0), i & 1
+                with torch.cuda.stream(copy):
+                    if used[b] is not None:
+                        copy.wait_event(used[b])
+                    bufs[b][:rows].copy_(x[r0: r0 + rows], non_blocking=True)
+                    copied[b].record(copy)
+                compute.wait_event(copied[b])
+                book.quantize(bufs[b].data_ptr(), rows, indices[r0:].data_ptr(), pair.data_ptr(), score.data_ptr(),
+                              compute.cuda_stream, 0)
+                used[b] = torch.cuda.Event()
+                used[b].record(compute)
+        return indices.reshape(shape)
 
     # ------------------------------------------------------------ checks
     def _validate(self) -> None:

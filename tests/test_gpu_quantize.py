@@ -170,3 +170,23 @@ def test_reference_shims(m):
         quantize_lattice_cuda(x.double(), indices, best_pair, best_score, meta, rank_meta, comb)
     with pytest.raises(ValueError):
         quantize_lattice_cuda(x.cpu(), indices, best_pair, best_score, meta, rank_meta, comb)
+
+
+def test_host_input_pipeline_matches_device_path(monkeypatch):
+    """Host batches larger than two chunks take the chunked copy/compute
+    pipeline; its indices equal the device-resident call's."""
+    from llvq_paper_reproduction_b200 import LeechLatticeVectorQuantizerGpu
+
+    q = LeechLatticeVectorQuantizerGpu(max_shell=13, use_cache=False, device="cuda")
+    monkeypatch.setattr(LeechLatticeVectorQuantizerGpu, "HOST_CHUNK_ROWS", 3000)
+    x = torch.randn((20011, 24), generator=torch.Generator().manual_seed(7))
+    want = q.quantize(x.cuda())
+    for host in (x, x.pin_memory()):
+        got = q.quantize(host)
+        assert got.device.type == "cuda" and got.shape == (20011,)
+        assert torch.equal(got, want)
+    # back-to-back calls with no synchronisation: each call's buffers may be
+    # the previous call's, still being read by its kernels
+    pinned = x.pin_memory()
+    outs = [q.quantize(pinned) for _ in range(4)]
+    assert all(torch.equal(o, want) for o in outs)
