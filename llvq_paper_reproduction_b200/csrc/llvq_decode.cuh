@@ -302,17 +302,25 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
         mag[d >> 2] |= byte_at(part1 ? pv1 : pv0, (int)nib) << (8 * (d & 3));
       }
     }
-    uint32_t nzmask = 0;
+    // Per-position bits of the magnitudes, four bytes at a time (every
+    // magnitude is below 128, so byte + 0x7F carries into bit 7 exactly when
+    // it is nonzero; a multiply by 0x01020408 gathers bit 0 of the four bytes
+    // into the top nibble).
+    uint32_t nzmask = 0, b1mask = 0;
 #pragma unroll
-    for (int d = 0; d < kDim; ++d) {
-      const int m = (int)((mag[d >> 2] >> (8 * (d & 3))) & 0xFFu);
-      const bool bit = (word >> d) & 1u;
-      nzmask |= (uint32_t)(m != 0) << d;
-      y[d] = odd ? (((m & 3) == (bit ? 3 : 1)) ? m : -m) : m;
+    for (int w = 0; w < 6; ++w) {
+      const uint32_t t = mag[w];
+      nzmask |= (((((t + 0x7F7F7F7Fu) >> 7) & 0x01010101u) * 0x01020408u) >> 24) << (4 * w);
+      b1mask |= ((((t >> 1) & 0x01010101u) * 0x01020408u) >> 24) << (4 * w);
     }
-    if (!odd) {
+    uint32_t neg;  // coordinates to negate
+    if (odd) {
+      // y = m where m = 1 mod 4 off the word or m = 3 mod 4 on it, else -m
+      neg = b1mask ^ word;
+    } else {
       // signs: insert, at the first word coordinate, the bit that gives the
-      // class's parity of negative word coordinates (weight 0: rank = mask)
+      // class's parity of negative word coordinates (weight 0: rank = mask),
+      // then deposit the bits on the nonzero coordinates in position order
       const int nz = __popc(nzmask);
       uint32_t cmask;
       if (word) {
@@ -324,17 +332,19 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
         ok = nz >= 32 || (sign >> nz) == 0;
         cmask = (uint32_t)sign;
       }
-      uint32_t neg = 0;
-      int ci = 0;
+      neg = 0;
 #pragma unroll
       for (int d = 0; d < kDim; ++d) {
-        const bool nzd = (nzmask >> d) & 1u;
-        neg |= (nzd ? (cmask >> ci) & 1u : 0u) << d;
-        ci += nzd;
+        const uint32_t nzd = (nzmask >> d) & 1u;
+        neg |= (cmask & nzd) << d;
+        cmask >>= nzd;
       }
       if (word && (__popc(neg & word) & 1) != (int)((meta >> 19) & 1)) neg ^= word & (0u - word);
+    }
 #pragma unroll
-      for (int d = 0; d < kDim; ++d) y[d] = ((neg >> d) & 1u) ? -y[d] : y[d];
+    for (int d = 0; d < kDim; ++d) {
+      const int m = (int)((mag[d >> 2] >> (8 * (d & 3))) & 0xFFu);
+      y[d] = ((neg >> d) & 1u) ? -m : m;
     }
   }
   if (!ok) {
