@@ -131,9 +131,13 @@ void build_chain(llvq::DevClass& c, const int* leader) {
   }
 }
 
+// The class search's bucket table stores class numbers in 16 bits.
+constexpr int kMaxClasses = 65536;
+
 int build(llvq::Codebook& cb, int32_t n, const int32_t* shell, const int32_t* parity, const int32_t* leader) {
   using namespace llvq;
   if (n <= 0 || !shell || !parity || !leader) return fail(LLVQ_ERR_INVALID_ARGUMENT, "empty class list");
+  if (n > kMaxClasses) return fail(LLVQ_ERR_UNSUPPORTED, "more than 65536 classes");
   cb.golay = golay_lex();
   int nww[25] = {0};
   cb.golay_wrank.resize(kNumGolay);
@@ -317,6 +321,7 @@ int upload(llvq::Codebook& cb, int device) {
   const size_t o_wlex = off; off = align256(off + kNumGolay * sizeof(uint16_t));
   const size_t o_byw = off; off = align256(off + kNumGolay * sizeof(uint16_t));
   const size_t o_dcls = off; off = align256(off + n * sizeof(DecodeClass));
+  const size_t o_bucket = off; off = align256(off + (kBuckets + 1) * sizeof(uint16_t));
   std::vector<unsigned char> host(off, 0);
   {
     std::vector<DecodeClass> dc(n);
@@ -343,6 +348,14 @@ int upload(llvq::Codebook& cb, int device) {
       }
     }
     std::memcpy(host.data() + o_dcls, dc.data(), n * sizeof(DecodeClass));
+    // owner class of each bucket's lowest index (the last class past the end)
+    std::vector<uint16_t> bucket(kBuckets + 1);
+    for (int b = 0; b <= kBuckets; ++b) {
+      const uint64_t lo = bucket_low(b);
+      bucket[b] = (uint16_t)(lo >= (uint64_t)cb.total ? n - 1
+                                                      : find_class(cb.class_start.data(), (int)n, (int64_t)lo));
+    }
+    std::memcpy(host.data() + o_bucket, bucket.data(), bucket.size() * sizeof(uint16_t));
   }
   std::memcpy(host.data() + o_cls, cb.cls.data(), n * sizeof(DevClass));
   std::memcpy(host.data() + o_start, cb.class_start.data(), n * sizeof(int64_t));
@@ -376,6 +389,7 @@ int upload(llvq::Codebook& cb, int device) {
   d.wlist_lex = reinterpret_cast<const uint16_t*>(base + o_wlex);
   d.by_weight = reinterpret_cast<const uint16_t*>(base + o_byw);
   d.dcls = reinterpret_cast<const DecodeClass*>(base + o_dcls);
+  d.bucket = reinterpret_cast<const uint16_t*>(base + o_bucket);
   std::copy(cb.weight_start, cb.weight_start + 25, d.weight_start);
   d.n_classes = (int32_t)n;
   d.min_shell = cb.min_shell;

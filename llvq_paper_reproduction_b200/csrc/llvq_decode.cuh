@@ -186,6 +186,24 @@ __device__ __forceinline__ void fast_part_load(FastPart& p, uint64_t pv, uint64_
   p.c2 = p.c1 + byte_at(pm, 2);
 }
 
+// Class of a valid index: the bucket table narrows the search to the classes
+// between the owners of the bucket's lowest index and of the next bucket's
+// (1.5 to 2.3 binary-search steps on average at shells 2..13 instead of 9).
+__device__ __forceinline__ int find_class_bucketed(const DevBook& book, const int64_t* starts, int64_t v) {
+  const uint64_t u = (uint64_t)v;
+  int key = 0;
+  if (u) {
+    const int e = 63 - __clzll((long long)u);
+    key = 1 + e * 16 + (int)((e >= 4 ? u >> (e - 4) : u << (4 - e)) & 15u);
+  }
+  int lo = __ldg(book.bucket + key), hi = __ldg(book.bucket + key + 1) + 1;
+  while (lo + 1 < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (starts[mid] <= v) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
 // Integer codeword of index v (before the 1/sqrt(8) scale); false and zeros
 // when v is outside the codebook.  Classes whose parts have at most four
 // distinct values (all but a few classes) unrank with fast_step and write
@@ -194,7 +212,7 @@ __device__ __forceinline__ void fast_part_load(FastPart& p, uint64_t pv, uint64_
 __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, DecodeShared& sh, int (&y)[kDim]) {
   bool ok = v >= 0 && v < book.total;
   if (ok) {
-    const int k = find_class(book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start, book.n_classes, v);
+    const int k = find_class_bucketed(book, book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start, v);
     const uint4* rp = reinterpret_cast<const uint4*>(book.dcls + k);
     const uint4 w0 = __ldg(rp), w1 = __ldg(rp + 1), w2 = __ldg(rp + 2), w3 = __ldg(rp + 3), w4 = __ldg(rp + 4),
                 w5 = __ldg(rp + 5);

@@ -81,6 +81,7 @@ constexpr uint32_t kMetaFast = 1u << 20;
 struct DevBook {
   const DevClass* cls;
   const DecodeClass* dcls;        // [n_classes] compact decode records
+  const uint16_t* bucket;         // [kBuckets + 1] class holding the lowest index of each bucket
   const int64_t* class_start;     // [n_classes] (binary search)
   const uint32_t* golay;          // [4096] lexicographic order, bit d = coordinate d
   const uint16_t* golay_wrank;    // [4096] position among the words of equal weight
@@ -300,6 +301,22 @@ LLVQ_HD bool unrank_codeword(const DevClass& c, uint64_t local, WordOf word_of_c
 }
 
 // Class containing a global index: last class whose start is <= index.
+// Index buckets for the class search: a bucket is an index's leading bit
+// and the four bits after it (relative width 1/16, like a float with a 4-bit
+// mantissa), so the exponentially growing shells and classes spread over a
+// few buckets each.  Bucket 0 holds index 0; bucket 1 + 16 e + j the indices
+// with leading bit e and next four bits j.  bucket_low(b) is the smallest
+// index of bucket b (all-ones past the last bucket).
+constexpr int kBuckets = 1 + 64 * 16;
+
+LLVQ_HD uint64_t bucket_low(int b) {
+  if (b <= 0) return 0;
+  const int e = (b - 1) / 16;
+  const uint64_t j = (uint64_t)((b - 1) % 16);
+  if (e >= 64) return ~0ull;
+  return (1ull << e) + (e >= 4 ? j << (e - 4) : (j << e) >> 4);
+}
+
 LLVQ_HD int find_class(const int64_t* starts, int n, int64_t index) {
   int lo = 0, hi = n;
   while (lo + 1 < hi) {
