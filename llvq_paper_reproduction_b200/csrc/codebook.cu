@@ -164,6 +164,22 @@ int build(llvq::Codebook& cb, int32_t n, const int32_t* shell, const int32_t* pa
       cb.wlist_word[j] = cb.golay[i];
     }
   }
+  // Complementary pairs (the all-ones word is in the code, and complementing
+  // reverses the lexicographic order, so lex(~c) = 4095 - lex(c)): keep the
+  // lighter word of each pair (bit 0 clear when both weigh 12), ordered by
+  // weight (0, 8, 12) then lex, so warps of the search run one weight's code.
+  cb.plist_word.clear();
+  cb.plist_lex.clear();
+  for (int w : {0, 8, 12}) {
+    for (int i = 0; i < kNumGolay; ++i) {
+      const uint32_t c = cb.golay[i];
+      if (__builtin_popcount(c) != w || (w == 12 && (c & 1u))) continue;
+      if (cb.golay[kNumGolay - 1 - i] != (~c & kFull24)) return fail(LLVQ_ERR_UNSUPPORTED, "golay order broken");
+      cb.plist_word.push_back(c);
+      cb.plist_lex.push_back((uint16_t)i);
+    }
+  }
+  if ((int)cb.plist_word.size() != kNumGolay / 2) return fail(LLVQ_ERR_UNSUPPORTED, "golay pairs broken");
   cb.cls.assign(n, DevClass{});
   cb.class_start.assign(n, 0);
   u128 cursor = 0;
@@ -322,6 +338,8 @@ int upload(llvq::Codebook& cb, int device) {
   const size_t o_byw = off; off = align256(off + kNumGolay * sizeof(uint16_t));
   const size_t o_dcls = off; off = align256(off + n * sizeof(DecodeClass));
   const size_t o_bucket = off; off = align256(off + (kBuckets + 1) * sizeof(uint16_t));
+  const size_t o_pword = off; off = align256(off + (kNumGolay / 2) * sizeof(uint32_t));
+  const size_t o_plex = off; off = align256(off + (kNumGolay / 2) * sizeof(uint16_t));
   std::vector<unsigned char> host(off, 0);
   {
     std::vector<DecodeClass> dc(n);
@@ -364,6 +382,8 @@ int upload(llvq::Codebook& cb, int device) {
   std::memcpy(host.data() + o_wword, cb.wlist_word.data(), kNumGolay * sizeof(uint32_t));
   std::memcpy(host.data() + o_wlex, cb.wlist_lex.data(), kNumGolay * sizeof(uint16_t));
   std::memcpy(host.data() + o_byw, cb.by_weight.data(), kNumGolay * sizeof(uint16_t));
+  std::memcpy(host.data() + o_pword, cb.plist_word.data(), (kNumGolay / 2) * sizeof(uint32_t));
+  std::memcpy(host.data() + o_plex, cb.plist_lex.data(), (kNumGolay / 2) * sizeof(uint16_t));
   int prev = -1;
   cudaError_t e = cudaGetDevice(&prev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -390,6 +410,8 @@ int upload(llvq::Codebook& cb, int device) {
   d.by_weight = reinterpret_cast<const uint16_t*>(base + o_byw);
   d.dcls = reinterpret_cast<const DecodeClass*>(base + o_dcls);
   d.bucket = reinterpret_cast<const uint16_t*>(base + o_bucket);
+  d.plist_word = reinterpret_cast<const uint32_t*>(base + o_pword);
+  d.plist_lex = reinterpret_cast<const uint16_t*>(base + o_plex);
   std::copy(cb.weight_start, cb.weight_start + 25, d.weight_start);
   d.n_classes = (int32_t)n;
   d.min_shell = cb.min_shell;

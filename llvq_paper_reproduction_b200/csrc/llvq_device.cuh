@@ -88,6 +88,8 @@ struct DevBook {
   const uint32_t* wlist_word;     // [4096] words sorted by (weight, lex)
   const uint16_t* wlist_lex;      // [4096] their lexicographic indices
   const uint16_t* by_weight;      // [4096] lex indices grouped by weight (lex order inside)
+  const uint32_t* plist_word;     // [2048] the lighter word of each complementary pair, weights 0, 8, 12 in order
+  const uint16_t* plist_lex;      // [2048] its lexicographic index (the complement's is 4095 minus it)
   int32_t weight_start[25];       // start of each weight group in by_weight
   int32_t n_classes;
   int32_t min_shell, max_shell;

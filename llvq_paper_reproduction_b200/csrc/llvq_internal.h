@@ -34,6 +34,8 @@ struct Codebook {
   std::vector<uint32_t> wlist_word;
   std::vector<uint16_t> wlist_lex;
   std::vector<uint16_t> by_weight;
+  std::vector<uint32_t> plist_word;    // one word of each complementary pair (the lighter; bit 0 clear at weight 12)
+  std::vector<uint16_t> plist_lex;
   int32_t weight_start[25] = {};
   DevBook dev{};                       // device pointers (valid when device >= 0)
   void* dev_alloc = nullptr;

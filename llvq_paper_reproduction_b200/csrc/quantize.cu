@@ -48,6 +48,7 @@ constexpr int kSearchThreads = 128;
 // the extra resident warps outweigh a few spilled bytes (+4% on shells 2..13).
 constexpr int kSearchMinBlocks = 6;
 constexpr int kWordsPerThread = kNumGolay / kSearchThreads;
+constexpr int kPairsPerThread = kWordsPerThread / 2;
 constexpr long long kTagWord = 1ll << 40;   // low 12 bits: the word
 constexpr long long kTagExact = 2ll << 40;  // bits 12..39: class, low 12 bits: word
 
@@ -328,18 +329,6 @@ __device__ __forceinline__ void even_sums(const Row& sh, uint32_t c, uint32_t cA
   P1 = negpar ? 0.f : qmin1;  // ... and for those that need an odd count
 }
 
-template <class S, int W, class Row>
-__device__ __forceinline__ float even_max_word(const DevBook& b, const Row& sh, uint32_t c, uint32_t cA,
-                                               const float* nmk) {
-  if constexpr (!Ops<S>::template has_even<W>()) {
-    return -INFINITY;
-  } else {
-    float R0[25], R1[25], P0, P1;
-    even_sums<W, Ops<S>::template r0max<W>()>(sh, c, cA, R0, R1, P0, P1);
-    return Ops<S>::template even_max<W>(b, R0, R1, P0, P1, nmk);
-  }
-}
-
 template <class S, int W, class Row, class F>
 __device__ __forceinline__ void even_cands_word(const DevBook& b, const Row& sh, uint32_t c, uint32_t cA,
                                                 const float* nmk, float thr, F&& f) {
@@ -362,25 +351,6 @@ __device__ __forceinline__ uint32_t permute_word(const RowLocal& r, uint32_t c) 
   return u;
 }
 
-template <class S, class Row>
-__device__ __forceinline__ float word_max(const DevBook& b, const Row& sh, uint32_t c, const float* nmk) {
-  const uint32_t cA = permute_word(sh, c);
-  float best = -INFINITY;
-  if constexpr (Ops<S>::kHasOdd) {
-    float R[25];
-    odd_sums(sh, cA, R);
-    best = Ops<S>::odd_max(b, R, nmk);
-  }
-  switch (__popc(c)) {
-    case 8: best = fmaxf(best, even_max_word<S, 8>(b, sh, c, cA, nmk)); break;
-    case 12: best = fmaxf(best, even_max_word<S, 12>(b, sh, c, cA, nmk)); break;
-    case 16: best = fmaxf(best, even_max_word<S, 16>(b, sh, c, cA, nmk)); break;
-    case 0: best = fmaxf(best, even_max_word<S, 0>(b, sh, c, cA, nmk)); break;
-    default: best = fmaxf(best, even_max_word<S, 24>(b, sh, c, cA, nmk)); break;
-  }
-  return best;
-}
-
 template <class S, class Row, class F>
 __device__ __forceinline__ void word_cands(const DevBook& b, const Row& sh, uint32_t c, const float* nmk,
                                            float thr, F&& f) {
@@ -396,6 +366,85 @@ __device__ __forceinline__ void word_cands(const DevBook& b, const Row& sh, uint
     case 16: even_cands_word<S, 16>(b, sh, c, cA, nmk, thr, f); break;
     case 0: even_cands_word<S, 0>(b, sh, c, cA, nmk, thr, f); break;
     default: even_cands_word<S, 24>(b, sh, c, cA, nmk, thr, f); break;
+  }
+}
+
+// ------------------------------------------- complementary word pairs
+//
+// The all-ones word is a Golay word, so the words pair up as (c, ~c), and
+// one walk over the sorted coordinates serves both.  Odd classes: x' of ~c
+// is -x' of c, so R_~c[t] = R_c[24 - t] - R_c[24] (exact: integers below
+// 2^24 in fp32).  Even classes: the in-word and off-word suffix sums swap,
+// so walking both completely (24 steps) gives both words' sums.  Each
+// complement sum is bounded like the sum it replaces, so the window constants
+// of the scoring chains hold for both words.
+
+// Even sums of c (weight W) and of ~c (weight 24 - W): R1 over c's W
+// positions, R0 over the others, the sign-parity penalties of both words.
+template <int W, class Row>
+__device__ __forceinline__ void even_sums_pair(const Row& sh, uint32_t c, uint32_t cA, float (&R0)[25],
+                                               float (&R1)[25], float& P0, float& P1, float& Q0, float& Q1) {
+  uint32_t f1 = cA, f0 = ~cA & kFull24;
+  R1[0] = 0.f;
+#pragma unroll
+  for (int t = 1; t <= W; ++t) {
+    const int j = 31 - __clz(f1);
+    R1[t] = R1[t - 1] + sh.aval[j];
+    f1 ^= 1u << j;
+  }
+  R0[0] = 0.f;
+#pragma unroll
+  for (int t = 1; t <= kDim - W; ++t) {
+    const int j = 31 - __clz(f0);
+    R0[t] = R0[t - 1] + sh.aval[j];
+    f0 ^= 1u << j;
+  }
+  const float qc = W ? sh.aval[__ffs(cA) - 1] : 0.f;
+  const float qn = W < kDim ? sh.aval[__ffs(~cA & kFull24) - 1] : 0.f;
+  const int nc = __popc(c & sh.negmask) & 1, nn = __popc(~c & kFull24 & sh.negmask) & 1;
+  P0 = nc ? qc : 0.f;
+  P1 = nc ? 0.f : qc;
+  Q0 = nn ? qn : 0.f;
+  Q1 = nn ? 0.f : qn;
+}
+
+template <class S, int W, class Row>
+__device__ __forceinline__ void even_pair_max(const DevBook& b, const Row& sh, uint32_t c, uint32_t cA,
+                                              const float* nmk, float& bc, float& bn) {
+  constexpr int WC = kDim - W;
+  if constexpr (Ops<S>::template has_even<W>() || Ops<S>::template has_even<WC>()) {
+    float R0[25], R1[25], P0, P1, Q0, Q1;
+    even_sums_pair<W>(sh, c, cA, R0, R1, P0, P1, Q0, Q1);
+    if constexpr (Ops<S>::template has_even<W>()) bc = fmaxf(bc, Ops<S>::template even_max<W>(b, R0, R1, P0, P1, nmk));
+    if constexpr (Ops<S>::template has_even<WC>())
+      bn = fmaxf(bn, Ops<S>::template even_max<WC>(b, R1, R0, Q0, Q1, nmk));
+  }
+}
+
+// Best approximate scores of c and of ~c (c: weight 0, 8 or 12).
+template <class S, class Row>
+__device__ __forceinline__ void pair_max(const DevBook& b, const Row& sh, uint32_t c, const float* nmk, float& bc,
+                                         float& bn) {
+  const uint32_t cA = permute_word(sh, c);
+  bc = -INFINITY;
+  bn = -INFINITY;
+  if constexpr (Ops<S>::kHasOdd) {
+    float R[25];
+    odd_sums(sh, cA, R);
+    bc = Ops<S>::odd_max(b, R, nmk);
+    const float r24 = R[kDim];
+#pragma unroll
+    for (int t = 0; t <= kDim / 2; ++t) {  // in place: R[t] <- R[24 - t] - R[24]
+      const float lo = R[t], hi = R[kDim - t];
+      R[t] = hi - r24;
+      R[kDim - t] = lo - r24;
+    }
+    bn = Ops<S>::odd_max(b, R, nmk);
+  }
+  switch (__popc(c)) {
+    case 8: even_pair_max<S, 8>(b, sh, c, cA, nmk, bc, bn); break;
+    case 0: even_pair_max<S, 0>(b, sh, c, cA, nmk, bc, bn); break;
+    default: even_pair_max<S, 12>(b, sh, c, cA, nmk, bc, bn); break;
   }
 }
 
@@ -512,19 +561,27 @@ __global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kerne
 #pragma unroll
     for (int s = 0; s < NS; ++s) nmk[s] = -(float)(min_shell + s) * sh.K;
 
+    // best score (b1) and word (lex w1) of this thread's words, and the best
+    // score of its other words (b2)
     float b1 = -INFINITY, b2 = -INFINITY;
     int w1 = -1;
-    for (int i = 0; i < kWordsPerThread; ++i) {
-      const int j = i * kSearchThreads + tid;
-      const uint32_t c = __ldg(book.wlist_word + j);
-      const float bw = word_max<S>(book, sh, c, nmk);
+    auto take = [&](float bw, int lex) {
       if (bw > b1) {
         b2 = b1;
         b1 = bw;
-        w1 = j;
+        w1 = lex;
       } else {
         b2 = fmaxf(b2, bw);
       }
+    };
+    for (int i = 0; i < kPairsPerThread; ++i) {
+      const int j = i * kSearchThreads + tid;
+      const uint32_t c = __ldg(book.plist_word + j);
+      const int lex = __ldg(book.plist_lex + j);
+      float bc, bn;
+      pair_max<S>(book, sh, c, nmk, bc, bn);
+      take(bc, lex);
+      take(bn, kNumGolay - 1 - lex);
     }
     const float wm = warp_max(b1);
     if (lane == 0) sh.red[warp] = wm;
@@ -537,7 +594,7 @@ __global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kerne
     const int second = __syncthreads_or(b2 >= thr);
     if (contenders == 1 && !second) {
       if (b1 >= thr) {
-        tag_out[row] = kTagWord | (long long)__ldg(book.wlist_lex + w1);
+        tag_out[row] = kTagWord | (long long)w1;
         m_out[row] = M;
       }
     } else {
