@@ -412,7 +412,32 @@ template <class S, int W, class Row>
 __device__ __forceinline__ void even_pair_max(const DevBook& b, const Row& sh, uint32_t c, uint32_t cA,
                                               const float* nmk, float& bc, float& bn) {
   constexpr int WC = kDim - W;
-  if constexpr (Ops<S>::template has_even<W>() || Ops<S>::template has_even<WC>()) {
+  if constexpr (W == WC) {
+    if constexpr (Ops<S>::template has_even<W>()) {
+      // both words weigh 12: one copy of the scoring code, run twice with
+      // the in-word and off-word sums swapped in between (the generated code
+      // is large; two inlined copies would not stay in the instruction cache)
+      float R0[25], R1[25], P0, P1, Q0, Q1;
+      even_sums_pair<W>(sh, c, cA, R0, R1, P0, P1, Q0, Q1);
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        const float v = Ops<S>::template even_max<W>(b, R0, R1, P0, P1, nmk);
+        if (h == 0) {
+          bc = fmaxf(bc, v);
+#pragma unroll
+          for (int t = 0; t <= W; ++t) {
+            const float x = R0[t];
+            R0[t] = R1[t];
+            R1[t] = x;
+          }
+          P0 = Q0;
+          P1 = Q1;
+        } else {
+          bn = fmaxf(bn, v);
+        }
+      }
+    }
+  } else if constexpr (Ops<S>::template has_even<W>() || Ops<S>::template has_even<WC>()) {
     float R0[25], R1[25], P0, P1, Q0, Q1;
     even_sums_pair<W>(sh, c, cA, R0, R1, P0, P1, Q0, Q1);
     if constexpr (Ops<S>::template has_even<W>()) bc = fmaxf(bc, Ops<S>::template even_max<W>(b, R0, R1, P0, P1, nmk));
@@ -431,15 +456,22 @@ __device__ __forceinline__ void pair_max(const DevBook& b, const Row& sh, uint32
   if constexpr (Ops<S>::kHasOdd) {
     float R[25];
     odd_sums(sh, cA, R);
-    bc = Ops<S>::odd_max(b, R, nmk);
     const float r24 = R[kDim];
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {  // one copy of the odd scoring code for both words
+      const float v = Ops<S>::odd_max(b, R, nmk);
+      if (h == 0) {
+        bc = v;
 #pragma unroll
-    for (int t = 0; t <= kDim / 2; ++t) {  // in place: R[t] <- R[24 - t] - R[24]
-      const float lo = R[t], hi = R[kDim - t];
-      R[t] = hi - r24;
-      R[kDim - t] = lo - r24;
+        for (int t = 0; t <= kDim / 2; ++t) {  // in place: R[t] <- R[24 - t] - R[24]
+          const float lo = R[t], hi = R[kDim - t];
+          R[t] = hi - r24;
+          R[kDim - t] = lo - r24;
+        }
+      } else {
+        bn = v;
+      }
     }
-    bn = Ops<S>::odd_max(b, R, nmk);
   }
   switch (__popc(c)) {
     case 8: even_pair_max<S, 8>(b, sh, c, cA, nmk, bc, bn); break;
