@@ -728,8 +728,17 @@ __global__ void __launch_bounds__(128) finalize_kernel(const float* __restrict__
     const uint32_t c = __ldg(book.golay + lex);
     double best = -INFINITY;
     order = LLONG_MAX;
-    word_cands<S>(book, r, c, nmk, thr,
-                  [&](int k, float) { consider_exact(r.x, r.apos, book, c, lex, k, &best, &order); });
+    // Collect the window's classes first and score them afterwards in one
+    // loop, so the lanes of a warp run the fp64 scoring together instead of
+    // one by one at each generated class site.
+    constexpr int kMaxCands = 8;
+    int cand[kMaxCands];
+    int nc = 0;
+    word_cands<S>(book, r, c, nmk, thr, [&](int k, float) {
+      if (nc < kMaxCands) cand[nc++] = k;
+      else consider_exact(r.x, r.apos, book, c, lex, k, &best, &order);
+    });
+    for (int i = 0; i < nc; ++i) consider_exact(r.x, r.apos, book, c, lex, cand[i], &best, &order);
     if (order == LLONG_MAX) {  // cannot happen for a finite row
       index_out[row] = -1;
       pair_out[row] = -1;
