@@ -186,6 +186,42 @@ __device__ __forceinline__ void fast_part_load(FastPart& p, uint64_t pv, uint64_
   p.c2 = p.c1 + byte_at(pm, 2);
 }
 
+// Magnitudes by position for the classes the fast path does not take (a part
+// with more than four values, or N >= 2^32 after a part's first step): the
+// general step, a nibble sequence of value indices, then the scatter.  Kept
+// out of line: rarely run, and the decoder's hot code must stay small.
+__device__ __noinline__ void decode_general(uint32_t word, bool odd, int nfirst, uint64_t rank, uint64_t N, uint64_t cnt,
+                                            uint64_t rank2, uint64_t N2, uint64_t cnt2, uint64_t pv0, uint64_t pv1,
+                                            const DecodeShared& sh, uint32_t* mag) {
+  uint64_t seq_lo = 0, seq_hi = 0;  // 4-bit value indices, step order
+#pragma unroll 4
+  for (int t = 0; t < kDim; ++t) {
+    if (t == nfirst) {
+      rank = rank2;
+      N = N2;
+      cnt = cnt2;
+    }
+    const int rem = t < nfirst ? nfirst - t : kDim - t;
+    const uint32_t j = unrank_step(rank, N, cnt, rem, sh);
+    if (t < 16) seq_lo |= (uint64_t)j << (4 * t);
+    else seq_hi |= (uint64_t)j << (4 * (t - 16));
+  }
+  // scatter: odd -> step d at position d; even -> the word's positions take
+  // the first (f1) part in order, the others the second (f0) part
+  uint32_t m[6] = {0, 0, 0, 0, 0, 0};
+#pragma unroll
+  for (int d = 0; d < kDim; ++d) {
+    const bool bit = (word >> d) & 1u;
+    const bool part1 = !odd && bit;
+    const int below1 = __popc(word & ((1u << d) - 1u));
+    const int t = odd ? d : (bit ? below1 : nfirst + d - below1);
+    const uint32_t nib = (uint32_t)((t < 16 ? seq_lo >> (4 * t) : seq_hi >> (4 * (t - 16))) & 15u);
+    m[d >> 2] |= byte_at(part1 ? pv1 : pv0, (int)nib) << (8 * (d & 3));
+  }
+#pragma unroll
+  for (int w = 0; w < 6; ++w) mag[w] = m[w];
+}
+
 // Class of a valid index: the bucket table narrows the search to the classes
 // between the owners of the bucket's lowest index and of the next bucket's
 // (1.5 to 2.3 binary-search steps on average at shells 2..13 instead of 9).
@@ -254,8 +290,8 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
     }
     uint32_t mag[6];  // magnitudes by position, 4 per word
     if ((meta & kMetaFast) && threadIdx.x < kDecodeThreads) {
-      // Straight-line steps: a part can only start at step 0 or at a word
-      // weight (8, 12, 16), and N can only reach 2^32 at step 0.
+      // A part can only start at step 0 or at a word weight (8, 12, 16), and
+      // N can only reach 2^32 at step 0.
       uint8_t* row = reinterpret_cast<uint8_t*>(sh.rows + threadIdx.x * kRowWords);
       FastPart part;
       uint32_t mask, val;  // mask: positions still to fill, lowest first
@@ -275,50 +311,36 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
       mask &= mask - 1u;
       const uint2* div = sh.div32 + base;  // div[-t] = rem's constants at step t
 #pragma unroll
-      for (int t = 1; t < kDim; ++t) {
-        if (t == 8 || t == 12 || t == 16) {
-          if (t == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
-            fast_part_load(part, pv0, cnt2);
-            part.rank = (uint32_t)rank2;
-            part.N = (uint32_t)N2;
-            mask = ~word & kFull24;
-            div = sh.div32 + kDim;
-          }
-        }
+      for (int t = 1; t < 4; ++t) {
         val = fast_step(part, div[-t]);
         row[__ffs(mask) - 1] = (uint8_t)val;
         mask &= mask - 1u;
+      }
+      // steps 4..23 in blocks of four, not unrolled (a part can only switch
+      // at a block start: 8, 12 or 16), so the code stays small enough for
+      // the instruction cache
+#pragma unroll 1
+      for (int tb = 4; tb < kDim; tb += 4) {
+        if (tb == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
+          fast_part_load(part, pv0, cnt2);
+          part.rank = (uint32_t)rank2;
+          part.N = (uint32_t)N2;
+          mask = ~word & kFull24;
+          div = sh.div32 + kDim;
+        }
+        const uint2* d = div - tb;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          val = fast_step(part, d[-i]);
+          row[__ffs(mask) - 1] = (uint8_t)val;
+          mask &= mask - 1u;
+        }
       }
       const uint32_t* rw = sh.rows + threadIdx.x * kRowWords;
 #pragma unroll
       for (int w = 0; w < 6; ++w) mag[w] = rw[w];
     } else {
-      uint64_t seq_lo = 0, seq_hi = 0;  // 4-bit value indices, step order
-#pragma unroll 4
-      for (int t = 0; t < kDim; ++t) {
-        if (t == nfirst) {
-          rank = rank2;
-          N = N2;
-          cnt = cnt2;
-        }
-        const int rem = t < nfirst ? nfirst - t : kDim - t;
-        const uint32_t j = unrank_step(rank, N, cnt, rem, sh);
-        if (t < 16) seq_lo |= (uint64_t)j << (4 * t);
-        else seq_hi |= (uint64_t)j << (4 * (t - 16));
-      }
-      // scatter: odd -> step d at position d; even -> the word's positions
-      // take the first (f1) part in order, the others the second (f0) part
-#pragma unroll
-      for (int w = 0; w < 6; ++w) mag[w] = 0;
-#pragma unroll
-      for (int d = 0; d < kDim; ++d) {
-        const bool bit = (word >> d) & 1u;
-        const bool part1 = !odd && bit;
-        const int below1 = __popc(word & ((1u << d) - 1u));
-        const int t = odd ? d : (bit ? below1 : nfirst + d - below1);
-        const uint32_t nib = (uint32_t)((t < 16 ? seq_lo >> (4 * t) : seq_hi >> (4 * (t - 16))) & 15u);
-        mag[d >> 2] |= byte_at(part1 ? pv1 : pv0, (int)nib) << (8 * (d & 3));
-      }
+      decode_general(word, odd, nfirst, rank, N, cnt, rank2, N2, cnt2, pv0, pv1, sh, mag);
     }
     // Per-position bits of the magnitudes, four bytes at a time (every
     // magnitude is below 128, so byte + 0x7F carries into bit 7 exactly when
