@@ -3,14 +3,16 @@
 // (impl/leech_lattice_vector_quantizer.py:282-314), fused with the index
 // encoding (encode_codeword, :247-280).
 //
-// One CTA per 24-D block at a time (persistent grid), 128 threads x 32 Golay
-// words each.  Per block it stages |x| in sorted order, the 3 byte tables that
-// permute a Golay word into that order, and the integer image
-// q = rint(|x| * 2^e) with |q| <= 2^19.  Per word it builds the suffix sums of
-// the sorted (sign-flipped) coordinates in registers and scores every class
-// with the generated FFMA chains (one FFMA per distinct leader value).  All
-// suffix sums are exact integers in fp32; only the FFMA chain rounds, so every
-// approximate score is within a proven bound E of the exact real score.
+// One CTA per 24-D block at a time (persistent grid), 128 threads x 16
+// complementary Golay word pairs (c, ~c) each.  Per block it stages |x| in
+// sorted order, the 3 byte tables that permute a Golay word into that order,
+// and the integer image q = rint(|x| * 2^e) with |q| <= 2^19.  Per pair it
+// builds the suffix sums of the sorted (sign-flipped) coordinates in
+// registers once (the complement's follow from them) and scores every class
+// of both words with the generated FFMA chains (one FFMA per distinct leader
+// value).  All suffix sums are exact integers in fp32; only the FFMA chain
+// rounds, so every approximate score is within a proven bound E of the exact
+// real score.
 //
 // The argmax is then decided exactly.  If a single word holds every pair
 // within W = 2E + 4 (q units) of the best approximate score, the search kernel
