@@ -462,9 +462,21 @@ def dequant_bench(q, device, stream, args) -> dict:
     algo_bytes = n_idx * (8 + 48) + n_rows * 2
     gbs = algo_bytes / (ms / 1000.0) / 1e9
     peaks = measured_peaks()
+    # host reference: the oracle's restatement of the reference codeword()
+    # per index (one thread) on a sample of the same indices
+    from oracle.oracle import OracleBook
+
+    sample = next(iter(work.values()))[0].reshape(-1)[: args.cpu_dequant_sample].cpu().numpy()
+    ob = OracleBook(args.max_shell)
+    t0 = time.perf_counter()
+    ob.codeword_batch(sample)
+    cpu_rate = sample.shape[0] / (time.perf_counter() - t0)
     del outs, work
     torch.cuda.empty_cache()
     return {"value": gbs, "unit": "GB/s", "ms_per_step": ms, "indices": n_idx, "rows": n_rows,
+            "cpu_baseline": {"value": cpu_rate * 56 / 1e9, "unit": "GB/s", "indices_per_s": cpu_rate, "cores": 1,
+                             "kind": "port", "sample": f"first {sample.shape[0]} indices of the workload; oracle "
+                                                       "restatement of the reference codeword() (int32 codewords)"},
             "workload": f"Llama-3-8B linears ({args.dequant_layers} layers), random valid int64 indices seed 3, "
                         "bf16 out, fp16 row scales",
             "gpu_launches": 2 * args.steps,
@@ -550,6 +562,7 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=96)
     ap.add_argument("--skip-dequant", action="store_true")
     ap.add_argument("--dequant-layers", type=int, default=32)
+    ap.add_argument("--cpu-dequant-sample", type=int, default=200_000)
     ap.add_argument("--skip-gemm", action="store_true")
     ap.add_argument("--model-layers", type=int, default=32,
                     help="Llama-2-7B layers of the whole-model quantization section (0 skips it)")

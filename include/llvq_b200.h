@@ -157,6 +157,14 @@ int llvq_gemm_packed(const llvq_codebook* cb, const uint8_t* packed, int32_t ind
  * No reference counterpart (the reference README lists the rotation only). */
 int llvq_hadamard(const void* in, int32_t in_is_half, float* out, int64_t rows, int64_t cols, int32_t block,
                   const int8_t* signs, int32_t inverse, void* stream);
+/* The same rotation with element types LLVQ_DT_F32 / LLVQ_DT_F16 /
+ * LLVQ_DT_BF16 in and LLVQ_DT_F32 / LLVQ_DT_BF16 out (butterflies in fp32,
+ * one rounding at the store; out must not alias in for bf16).  The bf16 ->
+ * bf16 form rotates a GEMM's activations for weights quantized after the
+ * same rotation: x W^T = (x R)(W R)^T.  No reference counterpart. */
+enum { LLVQ_DT_F32 = 0, LLVQ_DT_F16 = 1, LLVQ_DT_BF16 = 2 };
+int llvq_hadamard_ex(const void* in, int32_t in_type, void* out, int32_t out_type, int64_t rows, int64_t cols,
+                     int32_t block, const int8_t* signs, int32_t inverse, void* stream);
 
 /* Host-side scalar paths (no GPU needed).
  * llvq_codeword_host:  LeechLatticeVectorQuantizerGpu.codeword (_gpu.py:262-265)

@@ -36,7 +36,7 @@ EXPORTS = (
     "llvq_dequantize_lattice", "llvq_dequantize", "llvq_dequantize_bf16", "llvq_codeword_host",
     "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version", "llvq_gemm",
     "llvq_hadamard", "llvq_gemm_noalloc", "llvq_pack_indices", "llvq_unpack_indices", "llvq_dequantize_packed",
-    "llvq_gemm_packed",
+    "llvq_gemm_packed", "llvq_hadamard_ex",
 )
 
 _lib = None
@@ -67,6 +67,7 @@ def load() -> ctypes.CDLL:
             "llvq_gemm": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_gemm_noalloc": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_hadamard": (ctypes.c_int, [vp, i32, vp, i64, i64, i32, vp, i32, vp]),
+            "llvq_hadamard_ex": (ctypes.c_int, [vp, i32, vp, i32, i64, i64, i32, vp, i32, vp]),
             "llvq_pack_indices": (ctypes.c_int, [vp, i64, i32, vp, vp, vp]),
             "llvq_unpack_indices": (ctypes.c_int, [vp, i64, i32, vp, vp]),
             "llvq_dequantize_packed": (ctypes.c_int, [vp, vp, i32, i64, vp, i32, vp, i64, vp, vp]),
@@ -195,6 +196,15 @@ def pack_indices(idx_ptr: int, n: int, index_bytes: int, out_ptr: int, err_ptr: 
 
 def unpack_indices(packed_ptr: int, n: int, index_bytes: int, out_ptr: int, stream: int) -> None:
     check(load().llvq_unpack_indices(packed_ptr, n, index_bytes, out_ptr, stream), "llvq_unpack_indices")
+
+
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+
+
+def hadamard_ex(in_ptr: int, in_type: int, out_ptr: int, out_type: int, rows: int, cols: int, block: int,
+                signs_ptr: int, inverse: bool, stream: int) -> None:
+    check(load().llvq_hadamard_ex(in_ptr, in_type, out_ptr, out_type, rows, cols, block, signs_ptr, int(inverse),
+                                  stream), "llvq_hadamard_ex")
 
 
 def hadamard(in_ptr: int, in_is_half: bool, out_ptr: int, rows: int, cols: int, block: int, signs_ptr: int,

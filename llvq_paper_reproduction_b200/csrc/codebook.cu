@@ -644,14 +644,22 @@ int llvq_gemm_noalloc(const llvq_codebook* h, const int64_t* indices, int64_t n_
   });
 }
 
-int llvq_hadamard(const void* in, int32_t in_is_half, float* out, int64_t rows, int64_t cols, int32_t block,
-                  const int8_t* signs, int32_t inverse, void* stream) {
+int llvq_hadamard_ex(const void* in, int32_t in_type, void* out, int32_t out_type, int64_t rows, int64_t cols,
+                     int32_t block, const int8_t* signs, int32_t inverse, void* stream) {
   if (rows < 0 || cols <= 0 || block < 1 || block > 4096 || (block & (block - 1)) || cols % block)
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "hadamard: block must be a power of two <= 4096 dividing cols");
+  if (in_type < LLVQ_DT_F32 || in_type > LLVQ_DT_BF16 || (out_type != LLVQ_DT_F32 && out_type != LLVQ_DT_BF16))
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "hadamard: bad element type");
   if (rows > 0 && (!in || !out || !signs)) return fail(LLVQ_ERR_INVALID_ARGUMENT, "hadamard: null pointer");
-  const cudaError_t e = llvq::hadamard_launch(in, in_is_half, out, rows, cols, block, signs, inverse,
+  const cudaError_t e = llvq::hadamard_launch(in, in_type, out, out_type, rows, cols, block, signs, inverse,
                                               (cudaStream_t)stream);
   return e == cudaSuccess ? LLVQ_OK : cuda_fail(e, "hadamard launch");
+}
+
+int llvq_hadamard(const void* in, int32_t in_is_half, float* out, int64_t rows, int64_t cols, int32_t block,
+                  const int8_t* signs, int32_t inverse, void* stream) {
+  return llvq_hadamard_ex(in, in_is_half ? LLVQ_DT_F16 : LLVQ_DT_F32, out, LLVQ_DT_F32, rows, cols, block, signs,
+                          inverse, stream);
 }
 
 int llvq_codeword_host(const llvq_codebook* h, int64_t index, int32_t* out24) {

@@ -10,8 +10,12 @@
 // listed in its README only); this is the pre-quantization step of the
 // whole-model workload.
 //
-// One CTA per (row, segment): load to shared memory (fp16 or fp32 input),
-// log2(block) butterfly stages separated by barriers, scale, store fp32.
+// One CTA per (row, segment): load to shared memory (fp32, fp16 or bf16
+// input), log2(block) butterfly stages in fp32 separated by barriers, scale,
+// store fp32 or bf16 (rounded once).  The bf16 form rotates a GEMM's
+// activations for weights that were quantized after the same rotation:
+// x W^T = (x R)(W R)^T for orthogonal R.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -24,8 +28,22 @@ namespace llvq {
 constexpr int kHadThreads = 256;
 constexpr int kMaxHadBlock = 4096;
 
-template <bool kHalfIn>
-__global__ void __launch_bounds__(kHadThreads) hadamard_kernel(const void* __restrict__ in, float* __restrict__ out,
+// Element types: 0 fp32, 1 fp16, 2 bf16 (inputs); 0 fp32, 2 bf16 (outputs).
+template <int kIn>
+__device__ __forceinline__ float load_elem(const void* p, int64_t i) {
+  if constexpr (kIn == 1) return __half2float(static_cast<const __half*>(p)[i]);
+  else if constexpr (kIn == 2) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  else return static_cast<const float*>(p)[i];
+}
+
+template <int kOut>
+__device__ __forceinline__ void store_elem(void* p, int64_t i, float v) {
+  if constexpr (kOut == 2) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else static_cast<float*>(p)[i] = v;
+}
+
+template <int kIn, int kOut>
+__global__ void __launch_bounds__(kHadThreads) hadamard_kernel(const void* __restrict__ in, void* __restrict__ out,
                                                                int64_t cols, int block, int log2b,
                                                                const int8_t* __restrict__ signs, int inverse) {
   __shared__ float buf[kMaxHadBlock];
@@ -35,7 +53,7 @@ __global__ void __launch_bounds__(kHadThreads) hadamard_kernel(const void* __res
   const int64_t base = row * cols + seg * block;
   const int8_t* sg = signs + seg * block;
   for (int i = threadIdx.x; i < block; i += kHadThreads) {
-    float v = kHalfIn ? __half2float(static_cast<const __half*>(in)[base + i]) : static_cast<const float*>(in)[base + i];
+    float v = load_elem<kIn>(in, base + i);
     if (!inverse) v = sg[i] < 0 ? -v : v;
     buf[i] = v;
   }
@@ -54,21 +72,29 @@ __global__ void __launch_bounds__(kHadThreads) hadamard_kernel(const void* __res
   for (int i = threadIdx.x; i < block; i += kHadThreads) {
     float v = buf[i] * scale;
     if (inverse) v = sg[i] < 0 ? -v : v;
-    out[base + i] = v;
+    store_elem<kOut>(out, base + i, v);
   }
 }
 
-cudaError_t hadamard_launch(const void* in, int in_is_half, float* out, int64_t rows, int64_t cols, int block,
-                            const int8_t* signs, int inverse, cudaStream_t stream) {
+cudaError_t hadamard_launch(const void* in, int in_type, void* out, int out_type, int64_t rows, int64_t cols,
+                            int block, const int8_t* signs, int inverse, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   int log2b = 0;
   while ((1 << log2b) < block) ++log2b;
   const int64_t grid = rows * (cols / block);
   if (grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
-  if (in_is_half)
-    hadamard_kernel<true><<<(unsigned)grid, kHadThreads, 0, stream>>>(in, out, cols, block, log2b, signs, inverse);
-  else
-    hadamard_kernel<false><<<(unsigned)grid, kHadThreads, 0, stream>>>(in, out, cols, block, log2b, signs, inverse);
+  const unsigned g = (unsigned)grid;
+#define LLVQ_HAD(I, O) hadamard_kernel<I, O><<<g, kHadThreads, 0, stream>>>(in, out, cols, block, log2b, signs, inverse)
+  if (out_type == 0) {
+    if (in_type == 0) LLVQ_HAD(0, 0);
+    else if (in_type == 1) LLVQ_HAD(1, 0);
+    else LLVQ_HAD(2, 0);
+  } else {
+    if (in_type == 0) LLVQ_HAD(0, 2);
+    else if (in_type == 1) LLVQ_HAD(1, 2);
+    else LLVQ_HAD(2, 2);
+  }
+#undef LLVQ_HAD
   return cudaGetLastError();
 }
 

@@ -90,7 +90,8 @@ constexpr int64_t kNoAllocStagingBytes = 16ll << 20;
 cudaError_t noalloc_staging(void** ptr);
 cudaError_t gemm_configure_device();
 
-cudaError_t hadamard_launch(const void* in, int in_is_half, float* out, int64_t rows, int64_t cols, int block,
-                            const int8_t* signs, int inverse, cudaStream_t stream);
+// Element types 0 fp32, 1 fp16, 2 bf16 (out: 0 or 2).
+cudaError_t hadamard_launch(const void* in, int in_type, void* out, int out_type, int64_t rows, int64_t cols,
+                            int block, const int8_t* signs, int inverse, cudaStream_t stream);
 
 }  // namespace llvq

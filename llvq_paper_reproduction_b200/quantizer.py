@@ -237,13 +237,18 @@ class LeechLatticeVectorQuantizerGpu:
         self._raise_if_bad(err)
         return out
 
-    def gemm(self, a: torch.Tensor, indices: torch.Tensor, row_scale: torch.Tensor | None = None) -> torch.Tensor:
+    def gemm(self, a: torch.Tensor, indices: torch.Tensor, row_scale: torch.Tensor | None = None,
+             rotation: tuple[int, torch.Tensor] | None = None) -> torch.Tensor:
         """Dequant-GEMM: ``a @ W.T`` in fp32 for bf16 activations ``a`` [m, k]
         and a weight given by its indices [n, blocks] (int64, or packed uint8
         [n, blocks, index_bytes]; W[n] = dequantize(indices[n]).flatten()[:k]
         * row_scale[n]).  The weight is decoded into a bf16 staging buffer
         (stream-ordered, at most 256 MiB, chunk by chunk beyond that) that a
-        pipelined tcgen05 GEMM reads (no reference counterpart)."""
+        pipelined tcgen05 GEMM reads.  ``rotation=(block, signs)`` first
+        rotates the activations with the seeded Hadamard transform the weight
+        was quantized under (int8 +-1 signs [k], block a power of two dividing
+        k), rounding them to bf16 once: x W^T = (x R)(W R)^T.  No reference
+        counterpart."""
         self._require_cuda("gemm")
         packed = indices.dtype == torch.uint8
         if a.dim() != 2 or indices.dim() != (3 if packed else 2):
@@ -251,6 +256,16 @@ class LeechLatticeVectorQuantizerGpu:
         m, k = a.shape
         n, bpr = indices.shape[:2]
         a16 = a.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        if rotation is not None:
+            block, signs = rotation
+            signs = signs.to(device=self.device, dtype=torch.int8).contiguous()
+            if signs.shape != (k,):
+                raise ValueError("rotation signs must have one entry per activation column")
+            rot = torch.empty_like(a16)
+            with torch.cuda.device(self.device):
+                _native.hadamard_ex(a16.data_ptr(), _native.DT_BF16, rot.data_ptr(), _native.DT_BF16, m, k, int(block),
+                                    signs.data_ptr(), False, torch.cuda.current_stream().cuda_stream)
+            a16 = rot
         idx = self._packed(indices) if packed else indices.to(device=self.device, dtype=torch.long).contiguous()
         sc = None
         if row_scale is not None:

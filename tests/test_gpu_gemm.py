@@ -61,3 +61,41 @@ def test_gemm_argument_checks():
     with pytest.raises(ValueError):
         q.gemm(torch.zeros((2, 20), device="cuda"), idx)  # k % 8 != 0
     assert q.gemm(torch.zeros((0, 48), device="cuda"), idx).shape == (0, 4)
+
+
+def test_bf16_hadamard_matches_fp32_rotation():
+    from llvq_paper_reproduction_b200 import _native
+    from llvq_paper_reproduction_b200.model_quant import hadamard_signs, rotate
+
+    a = torch.randn((37, 1024), generator=torch.Generator(device="cuda").manual_seed(8), device="cuda")
+    a16 = a.to(torch.bfloat16)
+    signs = hadamard_signs(1024, 5, "cuda")
+    out = torch.empty_like(a16)
+    _native.hadamard_ex(a16.data_ptr(), _native.DT_BF16, out.data_ptr(), _native.DT_BF16, 37, 1024, 256,
+                        signs.data_ptr(), False, torch.cuda.current_stream().cuda_stream)
+    # same fp32 butterflies as the fp32 kernel on the widened input, one bf16 rounding
+    assert torch.equal(out, rotate(a16.float(), signs, 256).to(torch.bfloat16))
+
+
+def test_gemm_with_activation_rotation():
+    """A weight quantized after a Hadamard rotation, multiplied with the
+    rotation applied to the activations, approximates x W^T up to the
+    quantization error; without the rotation the result is unrelated."""
+    from llvq_paper_reproduction_b200.model_quant import hadamard_signs, rotate
+
+    q = api()
+    g = torch.Generator(device="cuda").manual_seed(9)
+    n, k, block = 192, 1536, 512
+    w = torch.randn((n, k), generator=g, device="cuda") * 0.02
+    signs = hadamard_signs(k, 3, "cuda")
+    wr = rotate(w, signs, block)
+    scale = wr.pow(2).mean(1).sqrt().to(torch.float16)
+    idx = q.quantize((wr / scale.float()[:, None]).reshape(-1, 24)).reshape(n, k // 24)
+    x = torch.randn((64, k), generator=g, device="cuda").to(torch.bfloat16)
+    want = x.float() @ w.T
+    y = q.gemm(x, idx, scale, rotation=(block, signs))
+    assert rel_err(y, want) < 0.4
+    assert rel_err(q.gemm(x, idx, scale), want) > 0.9
+    # the rotation is exactly a bf16 Hadamard of the activations, then the plain GEMM
+    xr = rotate(x.float(), signs, block).to(torch.bfloat16)
+    assert torch.equal(y, q.gemm(xr, idx, scale))
