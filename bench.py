@@ -368,9 +368,10 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
     barrier()
     secs = max_over_ranks(e0.elapsed_time(e1) / 1000.0)
     t0 = time.perf_counter()
-    local = {k: (r["indices"].cpu(), r["row_scale"].cpu()) for k, r in results.items()}
+    local = {k: (r["indices"], r["row_scale"]) for k, r in results.items()}  # stay on the device
     index_bytes = (mq.sg.bits + 7) // 8  # 48-bit shape-gain index -> 6 bytes per block on the wire
     gathered = gather_to_rank0(specs, local, rank, world, device, index_bytes) if world > 1 else local
+    torch.cuda.synchronize()
     gather_s = max_over_ranks(time.perf_counter() - t0)
     total = sum(s.blocks for s in specs)
     if rank == 0 and len(gathered) != len(specs):

@@ -177,15 +177,16 @@ def run_shard(specs: Sequence[MatrixSpec], rank: int, world: int, out_dir: Path,
     return done
 
 
-def pack_host(indices: torch.Tensor, index_bytes: int) -> torch.Tensor:
-    """Non-negative int64 indices (CPU) -> uint8 [n, index_bytes], little-endian."""
+def pack_le_bytes(indices: torch.Tensor, index_bytes: int) -> torch.Tensor:
+    """Non-negative int64 indices (any device) -> uint8 [n, index_bytes],
+    little-endian (the low bytes of each index)."""
     flat = indices.reshape(-1).contiguous()
     return flat.view(torch.uint8).view(-1, 8)[:, :index_bytes].contiguous()
 
 
-def unpack_host(packed: torch.Tensor, index_bytes: int) -> torch.Tensor:
-    """uint8 [n, index_bytes] (CPU) -> int64 [n]."""
-    out = torch.zeros((packed.shape[0], 8), dtype=torch.uint8)
+def unpack_le_bytes(packed: torch.Tensor, index_bytes: int) -> torch.Tensor:
+    """uint8 [n, index_bytes] -> int64 [n] on the same device."""
+    out = torch.zeros((packed.shape[0], 8), dtype=torch.uint8, device=packed.device)
     out[:, :index_bytes] = packed
     return out.view(torch.int64).reshape(-1)
 
@@ -194,25 +195,25 @@ def gather_to_rank0(specs: Sequence[MatrixSpec], local: dict, rank: int, world: 
                     index_bytes: int = 8) -> dict | None:
     """One all-gather of every rank's indices (as index_bytes little-endian
     bytes each: 6 for the 48-bit shape-gain index, a quarter less than int64)
-    and row scales, flattened and padded to the largest shard; rank 0 unpacks
-    them per matrix into int64."""
+    and row scales, flattened and padded to the largest shard, entirely on
+    `device` (indices that are already there never visit the host); rank 0
+    unpacks them per matrix into int64 tensors on `device`."""
     import torch.distributed as dist
 
     plan = plan_shards(specs, world)
     sizes = [sum(specs[i].blocks for i in p) for p in plan]
     rows = [sum(specs[i].out_features for i in p) for p in plan]
-    mine_idx = [local[specs[i].key][0].reshape(-1) for i in plan[rank]]
-    mine_sc = [local[specs[i].key][1].reshape(-1).view(torch.int16).to(torch.int32) for i in plan[rank]]
-    flat_idx = torch.zeros((max(sizes), index_bytes), dtype=torch.uint8)
-    flat_sc = torch.zeros(max(rows), dtype=torch.int32)
+    mine_idx = [local[specs[i].key][0].to(device).reshape(-1) for i in plan[rank]]
+    mine_sc = [local[specs[i].key][1].to(device).reshape(-1).view(torch.int16).to(torch.int32) for i in plan[rank]]
+    flat_idx = torch.zeros((max(sizes), index_bytes), dtype=torch.uint8, device=device)
+    flat_sc = torch.zeros(max(rows), dtype=torch.int32, device=device)
     if mine_idx:
         cat = torch.cat(mine_idx)
         if int(cat.min()) < 0 or (index_bytes < 8 and int(cat.max()) >> (8 * index_bytes)):
             raise ValueError(f"indices do not fit {index_bytes} bytes")
-        flat_idx[: cat.numel()] = pack_host(cat, index_bytes)
+        flat_idx[: cat.numel()] = pack_le_bytes(cat, index_bytes)
         cs = torch.cat(mine_sc)
         flat_sc[: cs.numel()] = cs
-    flat_idx, flat_sc = flat_idx.to(device), flat_sc.to(device)
     all_idx = [torch.empty_like(flat_idx) for _ in range(world)]
     all_sc = [torch.empty_like(flat_sc) for _ in range(world)]
     dist.all_gather(all_idx, flat_idx)
@@ -222,7 +223,7 @@ def gather_to_rank0(specs: Sequence[MatrixSpec], local: dict, rank: int, world: 
     result = {}
     for r in range(world):
         oi, os_ = 0, 0
-        gi, gs = unpack_host(all_idx[r].cpu(), index_bytes), all_sc[r].cpu()
+        gi, gs = unpack_le_bytes(all_idx[r], index_bytes), all_sc[r]
         for i in plan[r]:
             s = specs[i]
             result[s.key] = (gi[oi: oi + s.blocks].view(s.out_features, s.blocks_per_row),

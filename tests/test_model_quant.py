@@ -46,12 +46,12 @@ def _free_port() -> int:
 
 
 def test_host_pack_roundtrip():
-    from llvq_paper_reproduction_b200.model_quant import pack_host, unpack_host
+    from llvq_paper_reproduction_b200.model_quant import pack_le_bytes, unpack_le_bytes
 
     idx = torch.tensor([0, 1, (1 << 40) - 1, 123456789012], dtype=torch.int64)
-    pk = pack_host(idx, 5)
+    pk = pack_le_bytes(idx, 5)
     assert pk.shape == (4, 5) and pk.dtype == torch.uint8
-    assert torch.equal(unpack_host(pk, 5), idx)
+    assert torch.equal(unpack_le_bytes(pk, 5), idx)
 
 
 def _worker(rank, world, port, out_dir, fail_rank, result_path):
