@@ -486,8 +486,8 @@ def dequant_bench(q, device, stream, args) -> dict:
                          "traffic": DEQUANT_DRAM_BYTES_PER_INDEX * n_idx,
                          "traffic_unit": "bytes per step (ncu on 9,797,632 indices, scaled by indices)",
                          "note": "56 B per index (8 B int64 index + 48 B bf16) + 2 B per row; the kernel is "
-                                 "instruction-bound (about 2.3 k thread instructions per index under ncu, ALU "
-                                 "pipe ~54%), not HBM-bound; peak of "
+                                 "instruction-bound (about 2 k thread instructions per index under ncu, ALU "
+                                 "pipe above 60%), not HBM-bound; peak of "
                                  + ("fallback" if peaks.get("fallback") else "measured") + " copy bandwidth"}}
 
 

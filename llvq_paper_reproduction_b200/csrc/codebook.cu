@@ -325,6 +325,18 @@ bool fast_decode_ok(const llvq::DevClass& c) {
   return f0 < lim;
 }
 
+// The decoder's eight-value variant: every part has at most kMaxVals distinct
+// values and a multinomial below 2^59, so N * C for any cumulative count C
+// (at most 24) stays below 2^64 in its 64-bit steps.
+bool wide_decode_ok(const llvq::DevClass& c) {
+  using u128 = unsigned __int128;
+  const u128 lim = (u128)1 << 59;
+  if (c.nv0 > llvq::kMaxVals || c.nv1 > llvq::kMaxVals) return false;
+  if (c.parity) return (u128)c.perm_count < lim;
+  const u128 f1 = c.f1_perm, f0 = c.perm_count / c.f1_perm;
+  return f1 < lim && f0 < lim;
+}
+
 int upload(llvq::Codebook& cb, int device) {
   using namespace llvq;
   const size_t n = cb.cls.size();
@@ -354,7 +366,7 @@ int upload(llvq::Codebook& cb, int device) {
       d.inv_f1 = 1.0 / (double)c.f1_perm;
       d.meta = (uint32_t)c.parity | ((uint32_t)c.even_weight << 1) | ((uint32_t)c.sign_shift << 6) |
                ((uint32_t)c.nv0 << 11) | ((uint32_t)c.nv1 << 15) | ((uint32_t)c.required << 19) |
-               (fast_decode_ok(c) ? kMetaFast : 0u);
+               (fast_decode_ok(c) ? kMetaFast | kMetaWide : 0u) | (wide_decode_ok(c) ? kMetaWide : 0u);
       d.golay_base = (uint32_t)cb.weight_start[c.even_weight];
       d.pad = 0;
       d.v0 = d.m0 = d.v1 = d.m1 = 0;

@@ -15,6 +15,9 @@
 // are computed exactly -- a product, a shift by the power of two in rem and a
 // multiply by the inverse of its odd part -- and compared with the rank; the
 // magnitude goes straight to its position in a per-thread shared-memory row.
+// Parts of up to eight values, or whose N stays at or above 2^32 past their
+// first step, use the same step with seven boundaries (wide_step, 64-bit while
+// N >= 2^32), taken by a whole warp at once.
 // Other classes use a general step (fp32 estimate of rank*rem/N, byte-wise
 // compare of the packed cumulative counts, exact verification; a 64-bit scan
 // while N >= 2^32) and a nibble sequence scattered afterwards.  Even-class
@@ -186,6 +189,83 @@ __device__ __forceinline__ void fast_part_load(FastPart& p, uint64_t pv, uint64_
   p.c2 = p.c1 + byte_at(pm, 2);
 }
 
+// The fast step for parts of up to eight values (kMaxVals) and any N below
+// 2^59: the value taken is the number of the seven boundaries B_i = N * C_i /
+// rem at or below `rank` (they do not decrease; C_i of absent values equals
+// rem, so their boundary is N and is never at or below it), then rank and N
+// become rank - B_{j-1} and B_j - B_{j-1}, recomputed from the packed
+// cumulative counts.  Exact divisions as in fast_step: in 32 bits once N <
+// 2^32, before that with the 64-bit inverse of rem's odd part (N * C < 2^64).
+struct WidePart {
+  uint64_t rank, N;
+  uint64_t cum;  // byte i = C_i = c_0 + ... + c_i (byte 7: all that remain)
+  uint64_t pv;   // byte j = value j, descending
+};
+
+__device__ __forceinline__ void wide_part_load(WidePart& p, uint64_t pv, uint64_t pm, uint64_t rank, uint64_t N) {
+  p.pv = pv;
+  p.rank = rank;
+  p.N = N;
+  p.cum = pm * 0x0101010101010101ull;  // prefix sums of the count bytes (at most 24: no carries)
+}
+
+// The value index taken; rank, N and the counts updated.  WIDE: N may be at
+// or above 2^32 (64-bit boundaries).  nb: boundaries to test, at least the
+// part's distinct values - 1 (the boundaries past it are N).
+template <bool WIDE>
+__device__ __forceinline__ uint32_t wide_step(WidePart& p, int rem, int nb, const DecodeShared& sh) {
+  uint32_t j = 0;
+  uint64_t lo, hi;
+  if constexpr (WIDE) {
+    const uint32_t s = sh.shift[rem];
+    const uint64_t inv = sh.inv[rem];
+#pragma unroll
+    for (int i = 0; i < kMaxVals - 1; ++i)
+      if (i < nb) j += ((p.N * byte_at(p.cum, i)) >> s) * inv <= p.rank;
+    lo = ((p.N * byte_at(p.cum << 8, j)) >> s) * inv;
+    hi = ((p.N * byte_at(p.cum, j)) >> s) * inv;
+  } else {
+    const uint2 d = sh.div32[rem];
+    const uint32_t n = (uint32_t)p.N, r = (uint32_t)p.rank;
+#pragma unroll
+    for (int i = 0; i < kMaxVals - 1; ++i)
+      if (i < nb) j += exact_div32(n, byte_at(p.cum, i), d) <= r;
+    lo = exact_div32(n, byte_at(p.cum << 8, j), d);
+    hi = exact_div32(n, byte_at(p.cum, j), d);
+  }
+  p.rank -= lo;
+  p.N = hi - lo;
+  p.cum -= 0x0101010101010101ull << (8 * j);  // the value taken loses one count
+  return j;
+}
+
+// Magnitudes by position with wide_step, into the thread's shared-memory row.
+// Out of line: a warp runs it only when one of its indices needs it.  Each
+// step takes the 64-bit form while any index of the warp has N >= 2^32, and
+// tests as many boundaries as the warp's largest part needs (nvals: this
+// index's largest count of distinct values in a part).
+__device__ __noinline__ void decode_wide(uint32_t word, bool odd, int nfirst, uint64_t rank, uint64_t N, uint64_t cnt,
+                                         uint64_t rank2, uint64_t N2, uint64_t cnt2, uint64_t pv0, uint64_t pv1,
+                                         int nvals, const DecodeShared& sh, uint8_t* row) {
+  const unsigned lanes = __activemask();  // every lane here runs the 24 steps
+  const int nb = (int)__reduce_max_sync(lanes, (unsigned)nvals) - 1;
+  WidePart p;
+  wide_part_load(p, odd ? pv0 : pv1, cnt, rank, N);
+  uint32_t mask = odd ? kFull24 : word;  // positions still to fill, lowest first
+#pragma unroll 1
+  for (int t = 0; t < kDim; ++t) {
+    if (t == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
+      wide_part_load(p, pv0, cnt2, rank2, N2);
+      mask = ~word & kFull24;
+    }
+    const int rem = t < nfirst ? nfirst - t : kDim - t;
+    const uint32_t j =
+        __any_sync(lanes, (p.N >> 32) != 0) ? wide_step<true>(p, rem, nb, sh) : wide_step<false>(p, rem, nb, sh);
+    row[__ffs(mask) - 1] = (uint8_t)byte_at(p.pv, (int)j);
+    mask &= mask - 1u;
+  }
+}
+
 // Magnitudes by position for the classes the fast path does not take (a part
 // with more than four values, or N >= 2^32 after a part's first step): the
 // general step, a nibble sequence of value indices, then the scatter.  Kept
@@ -242,9 +322,10 @@ __device__ __forceinline__ int find_class_bucketed(const DevBook& book, const in
 
 // Integer codeword of index v (before the 1/sqrt(8) scale); false and zeros
 // when v is outside the codebook.  Classes whose parts have at most four
-// distinct values (all but a few classes) unrank with fast_step and write
-// each magnitude to its position in the thread's shared-memory row; the
-// others use the general step and a nibble sequence.
+// distinct values (all but a few classes) unrank with fast_step, the others
+// with a part multinomial below 2^59 with wide_step; both write each magnitude
+// to its position in the thread's shared-memory row.  The rest (none up to
+// shell 32) use the general step and a nibble sequence.
 __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, DecodeShared& sh, int (&y)[kDim]) {
   bool ok = v >= 0 && v < book.total;
   if (ok) {
@@ -289,51 +370,59 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
       nfirst = weight;
     }
     uint32_t mag[6];  // magnitudes by position, 4 per word
-    if ((meta & kMetaFast) && threadIdx.x < kDecodeThreads) {
-      // A part can only start at step 0 or at a word weight (8, 12, 16), and
-      // N can only reach 2^32 at step 0.
+    if ((meta & kMetaWide) && threadIdx.x < kDecodeThreads) {
       uint8_t* row = reinterpret_cast<uint8_t*>(sh.rows + threadIdx.x * kRowWords);
-      FastPart part;
-      uint32_t mask, val;  // mask: positions still to fill, lowest first
-      int base;            // rem = base - t
-      if (nfirst == 0) {  // weight 0: only the f0 part
-        fast_part_load(part, pv0, cnt2);
-        mask = kFull24;
-        base = kDim;
-        val = fast_first_step(part, rank2, N2, kDim, sh);
+      // The whole warp takes the eight-value variant when one of its indices
+      // needs it (any index may: it decodes every fast class), so a warp runs
+      // one of the two step loops, never both.
+      if (__any_sync(__activemask(), !(meta & kMetaFast))) {
+        decode_wide(word, odd, nfirst, rank, N, cnt, rank2, N2, cnt2, pv0, pv1,
+                    (int)max((meta >> 11) & 15u, (meta >> 15) & 15u), sh, row);
       } else {
-        fast_part_load(part, odd ? pv0 : pv1, cnt);
-        mask = odd ? kFull24 : word;
-        base = nfirst;
-        val = fast_first_step(part, rank, N, nfirst, sh);
-      }
-      row[__ffs(mask) - 1] = (uint8_t)val;
-      mask &= mask - 1u;
-      const uint2* div = sh.div32 + base;  // div[-t] = rem's constants at step t
-#pragma unroll
-      for (int t = 1; t < 4; ++t) {
-        val = fast_step(part, div[-t]);
+        // A part can only start at step 0 or at a word weight (8, 12, 16), and
+        // N can only reach 2^32 at step 0.
+        FastPart part;
+        uint32_t mask, val;  // mask: positions still to fill, lowest first
+        int base;            // rem = base - t
+        if (nfirst == 0) {  // weight 0: only the f0 part
+          fast_part_load(part, pv0, cnt2);
+          mask = kFull24;
+          base = kDim;
+          val = fast_first_step(part, rank2, N2, kDim, sh);
+        } else {
+          fast_part_load(part, odd ? pv0 : pv1, cnt);
+          mask = odd ? kFull24 : word;
+          base = nfirst;
+          val = fast_first_step(part, rank, N, nfirst, sh);
+        }
         row[__ffs(mask) - 1] = (uint8_t)val;
         mask &= mask - 1u;
-      }
-      // steps 4..23 in blocks of four, not unrolled (a part can only switch
-      // at a block start: 8, 12 or 16), so the code stays small enough for
-      // the instruction cache
-#pragma unroll 1
-      for (int tb = 4; tb < kDim; tb += 4) {
-        if (tb == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
-          fast_part_load(part, pv0, cnt2);
-          part.rank = (uint32_t)rank2;
-          part.N = (uint32_t)N2;
-          mask = ~word & kFull24;
-          div = sh.div32 + kDim;
-        }
-        const uint2* d = div - tb;
+        const uint2* div = sh.div32 + base;  // div[-t] = rem's constants at step t
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          val = fast_step(part, d[-i]);
+        for (int t = 1; t < 4; ++t) {
+          val = fast_step(part, div[-t]);
           row[__ffs(mask) - 1] = (uint8_t)val;
           mask &= mask - 1u;
+        }
+        // steps 4..23 in blocks of four, not unrolled (a part can only switch
+        // at a block start: 8, 12 or 16), so the code stays small enough for
+        // the instruction cache
+#pragma unroll 1
+        for (int tb = 4; tb < kDim; tb += 4) {
+          if (tb == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
+            fast_part_load(part, pv0, cnt2);
+            part.rank = (uint32_t)rank2;
+            part.N = (uint32_t)N2;
+            mask = ~word & kFull24;
+            div = sh.div32 + kDim;
+          }
+          const uint2* d = div - tb;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            val = fast_step(part, d[-i]);
+            row[__ffs(mask) - 1] = (uint8_t)val;
+            mask &= mask - 1u;
+          }
         }
       }
       const uint32_t* rw = sh.rows + threadIdx.x * kRowWords;

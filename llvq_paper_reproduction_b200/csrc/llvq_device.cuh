@@ -68,7 +68,8 @@ struct alignas(16) DecodeClass {
   uint64_t f0_perm;     // perm_count / f1_perm
   uint32_t f1_perm;     // 1 for odd classes
   uint32_t meta;        // parity | even_weight << 1 | sign_shift << 6 | nv0 << 11 | nv1 << 15 | required << 19
-                        // | kMetaFast (the decoder's fast path applies)
+                        // | kMetaFast (the decoder's four-value fast path applies)
+                        // | kMetaWide (its eight-value, 64-bit variant applies)
   uint32_t golay_base;  // even: start of its weight group in by_weight
   uint32_t pad;
   double inv_f1;        // 1.0 / f1_perm
@@ -76,6 +77,7 @@ struct alignas(16) DecodeClass {
 };
 static_assert(sizeof(DecodeClass) == 96, "decode record is six 16-byte loads");
 constexpr uint32_t kMetaFast = 1u << 20;
+constexpr uint32_t kMetaWide = 1u << 21;
 
 // Everything a kernel needs about one codebook (plain pointers, passed by value).
 struct DevBook {
