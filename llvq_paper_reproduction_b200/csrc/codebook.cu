@@ -360,10 +360,10 @@ int upload(llvq::Codebook& cb, int device) {
       DecodeClass& d = dc[k];
       d.start = c.start;
       d.perm_count = c.perm_count;
-      d.inv_perm = 1.0 / (double)c.perm_count;
+      d.magic_perm = ~0ull / c.perm_count;
       d.f0_perm = c.perm_count / c.f1_perm;
       d.f1_perm = (uint32_t)c.f1_perm;
-      d.inv_f1 = 1.0 / (double)c.f1_perm;
+      d.magic_f1 = ~0ull / c.f1_perm;
       d.meta = (uint32_t)c.parity | ((uint32_t)c.even_weight << 1) | ((uint32_t)c.sign_shift << 6) |
                ((uint32_t)c.nv0 << 11) | ((uint32_t)c.nv1 << 15) | ((uint32_t)c.required << 19) |
                (fast_decode_ok(c) ? kMetaFast | kMetaWide : 0u) | (wide_decode_ok(c) ? kMetaWide : 0u);

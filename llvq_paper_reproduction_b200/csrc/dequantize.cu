@@ -40,7 +40,7 @@ template <int KIND>
 __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(IndexSource index, int64_t n,
                                                               DevBook book, void* __restrict__ out,
                                                               const uint16_t* __restrict__ row_scale,
-                                                              int64_t blocks_per_row, double inv_bpr,
+                                                              int64_t blocks_per_row, uint64_t magic_bpr,
                                                               int* error_count) {
   __shared__ DecodeShared sh;
   decode_setup(book, sh);
@@ -66,8 +66,8 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(Ind
 #pragma unroll
     for (int d = 0; d < kDim; d += 4) o[d / 4] = make_float4(f[d], f[d + 1], f[d + 2], f[d + 3]);
   } else {
-    uint64_t col;  // row = i / blocks_per_row by reciprocal multiplication with an exact correction
-    const uint64_t row = div_recip((uint64_t)i, (uint64_t)blocks_per_row, inv_bpr, col);
+    uint64_t col;  // row = i / blocks_per_row by multiply-high with an exact correction
+    const uint64_t row = div_magic((uint64_t)i, (uint64_t)blocks_per_row, magic_bpr, col);
     const float s = __half2float(__ushort_as_half(row_scale[row]));
     uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + i * kDim);
     uint32_t w[kDim / 2];
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(Ind
 // (row, block) plus the padding.
 __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(IndexSource index, int rows,
                                                                        int bpr, int ldw, DevBook book,
-                                                                       __nv_bfloat16* __restrict__ out, double inv_per_row) {
+                                                                       __nv_bfloat16* __restrict__ out, uint64_t magic_per_row) {
   __shared__ DecodeShared sh;
   decode_setup(book, sh);
   __syncthreads();
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(IndexSour
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)rows * per_row) return;
   uint64_t bq;
-  const int r = (int)div_recip((uint64_t)i, (uint64_t)per_row, inv_per_row, bq), b = (int)bq;
+  const int r = (int)div_magic((uint64_t)i, (uint64_t)per_row, magic_per_row, bq), b = (int)bq;
   __nv_bfloat16* o = out + (int64_t)r * ldw;
   if (b < bpr) {
     int y[kDim];
@@ -122,7 +122,7 @@ cudaError_t decode_rows_bf16_launch(const Codebook& cb, IndexSource index, int r
   if (rows <= 0) return cudaSuccess;
   const int64_t n = (int64_t)rows * (ldw / kDim + 1);
   decode_rows_bf16_kernel<<<(unsigned)((n + kDeqThreads - 1) / kDeqThreads), kDeqThreads, 0, stream>>>(
-      index, rows, bpr, ldw, cb.dev, static_cast<__nv_bfloat16*>(out), 1.0 / (double)(ldw / kDim + 1));
+      index, rows, bpr, ldw, cb.dev, static_cast<__nv_bfloat16*>(out), ~0ull / (uint64_t)(ldw / kDim + 1));
   return cudaGetLastError();
 }
 
@@ -131,12 +131,12 @@ cudaError_t dequantize_launch(const Codebook& cb, IndexSource index, int64_t n, 
                               cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   const unsigned blocks = (unsigned)((n + kDeqThreads - 1) / kDeqThreads);
-  const double inv_bpr = 1.0 / (double)blocks_per_row;
+  const uint64_t magic_bpr = ~0ull / (uint64_t)(blocks_per_row > 0 ? blocks_per_row : 1);
   switch (kind) {
-    case 0: dequant_kernel<0><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, inv_bpr, error_count); break;
-    case 1: dequant_kernel<1><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, inv_bpr, error_count); break;
-    case 2: dequant_kernel<2><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, inv_bpr, error_count); break;
-    case 3: dequant_kernel<3><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, inv_bpr, error_count); break;
+    case 0: dequant_kernel<0><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, magic_bpr, error_count); break;
+    case 1: dequant_kernel<1><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, magic_bpr, error_count); break;
+    case 2: dequant_kernel<2><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, magic_bpr, error_count); break;
+    case 3: dequant_kernel<3><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, magic_bpr, error_count); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

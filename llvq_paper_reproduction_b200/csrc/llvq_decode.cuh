@@ -4,7 +4,7 @@
 // Index layout and unranking as in the reference's codeword() path
 // (impl/leech_lattice_vector_quantizer.py:196-245, :774-867): class by binary
 // search over the class starts, a 96-byte decode record (six 16-byte loads),
-// the per-class splits by reciprocal multiplication with an exact correction,
+// the per-class splits by multiply-high with an exact correction,
 // then one 24-step lexicographic unranking loop shared by both parities (an
 // even class unranks its |v| = 2 mod 4 part on the word's positions, then its
 // |v| = 0 mod 4 part on the others), so warps holding both parities do not
@@ -56,19 +56,18 @@ __device__ __forceinline__ void decode_setup(const DevBook& book, DecodeShared& 
 
 __device__ __forceinline__ uint32_t byte_at(uint64_t packed, int j) { return (uint32_t)(packed >> (8 * j)) & 0xFFu; }
 
-// a / b for a < 2^63, b >= 1, with inv_b ~ 1/b: a reciprocal estimate fixed
-// up by one exact step; hardware division for a >= 2^52 (huge codebooks only).
-__device__ __forceinline__ uint64_t div_recip(uint64_t a, uint64_t b, double inv_b, uint64_t& rem) {
-  uint64_t q;
-  if (a >> 52) {
-    q = a / b;
-  } else {
-    q = (uint64_t)__dmul_rz((double)a, inv_b);
-    int64_t r = (int64_t)(a - q * b);
-    if (r < 0) { --q; r += (int64_t)b; }
-    else if ((uint64_t)r >= b) { ++q; r -= (int64_t)b; }
+// a / b for any a and b >= 1, given magic = floor((2^64 - 1) / b): the high
+// half of a * magic is floor(a / b) or one less (division by an invariant
+// integer by multiplication, Granlund and Montgomery 1994), fixed up by one
+// comparison of the remainder.  Integer pipes only.
+__device__ __forceinline__ uint64_t div_magic(uint64_t a, uint64_t b, uint64_t magic, uint64_t& rem) {
+  uint64_t q = __umul64hi(a, magic);
+  uint64_t r = a - q * b;
+  if (r >= b) {
+    ++q;
+    r -= b;
   }
-  rem = a - q * b;
+  rem = r;
   return q;
 }
 
@@ -335,15 +334,15 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
                 w5 = __ldg(rp + 5);
     auto u64 = [](uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; };
     const uint64_t start = u64(w0.x, w0.y), perm = u64(w0.z, w0.w);
-    const double inv_perm = __longlong_as_double((long long)u64(w1.x, w1.y));
+    const uint64_t magic_perm = u64(w1.x, w1.y);
     const uint64_t f0p = u64(w1.z, w1.w);
     const uint32_t f1p = w2.x, meta = w2.y, gbase = w2.z;
-    const double inv_f1 = __longlong_as_double((long long)u64(w3.x, w3.y));
+    const uint64_t magic_f1 = u64(w3.x, w3.y);
     const uint64_t pv0 = u64(w3.z, w3.w), pm0 = u64(w4.x, w4.y), pv1 = u64(w4.z, w4.w), pm1 = u64(w5.x, w5.y);
     const bool odd = meta & 1;
     const int weight = (meta >> 1) & 31, sshift = (meta >> 6) & 31;
     uint64_t prank;
-    const uint64_t cur = div_recip((uint64_t)v - start, perm, inv_perm, prank);
+    const uint64_t cur = div_magic((uint64_t)v - start, perm, magic_perm, prank);
     uint32_t word;
     uint64_t sign = 0;
     // first part: odd -> all 24 coordinates; even -> the word's f1 part, then f0
@@ -360,7 +359,7 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
       const uint64_t g = cur >> sshift;
       word = __ldg(book.golay + __ldg(book.by_weight + gbase + (int)g));
       uint64_t r1;
-      const uint64_t r0 = div_recip(prank, f1p, inv_f1, r1);
+      const uint64_t r0 = div_magic(prank, f1p, magic_f1, r1);
       rank = r1;
       N = f1p;
       cnt = pm1;

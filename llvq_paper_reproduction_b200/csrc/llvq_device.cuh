@@ -64,7 +64,7 @@ struct DevClass {
 struct alignas(16) DecodeClass {
   int64_t start;
   uint64_t perm_count;
-  double inv_perm;      // 1.0 / perm_count
+  uint64_t magic_perm;  // floor((2^64 - 1) / perm_count), for div_magic
   uint64_t f0_perm;     // perm_count / f1_perm
   uint32_t f1_perm;     // 1 for odd classes
   uint32_t meta;        // parity | even_weight << 1 | sign_shift << 6 | nv0 << 11 | nv1 << 15 | required << 19
@@ -72,7 +72,7 @@ struct alignas(16) DecodeClass {
                         // | kMetaWide (its eight-value, 64-bit variant applies)
   uint32_t golay_base;  // even: start of its weight group in by_weight
   uint32_t pad;
-  double inv_f1;        // 1.0 / f1_perm
+  uint64_t magic_f1;    // floor((2^64 - 1) / f1_perm)
   uint64_t v0, m0, v1, m1;  // byte j = j-th value / multiplicity (descending values)
 };
 static_assert(sizeof(DecodeClass) == 96, "decode record is six 16-byte loads");
