@@ -337,6 +337,41 @@ bool wide_decode_ok(const llvq::DevClass& c) {
   return f1 < lim && f0 < lim;
 }
 
+// The decoder's tail table (llvq_device.cuh, kTailLen): for every count
+// vector over four values summing to 8, its sequences in lexicographic order.
+void build_tail_tables(std::vector<uint32_t>& off, std::vector<uint16_t>& seq) {
+  using namespace llvq;
+  off.assign(kTailKeys, 0);
+  seq.clear();
+  int cnt[4];
+  uint32_t cur = 0;
+  auto emit = [&](auto&& self, int pos) -> void {
+    if (pos == kTailLen) {
+      seq.push_back((uint16_t)cur);
+      return;
+    }
+    for (int v = 0; v < 4; ++v) {
+      if (!cnt[v]) continue;
+      --cnt[v];
+      cur = (cur & ~(3u << (2 * pos))) | ((uint32_t)v << (2 * pos));
+      self(self, pos + 1);
+      ++cnt[v];
+    }
+  };
+  for (int n0 = 0; n0 <= kTailLen; ++n0)
+    for (int n1 = 0; n0 + n1 <= kTailLen; ++n1)
+      for (int n2 = 0; n0 + n1 + n2 <= kTailLen; ++n2) {
+        const int n3 = kTailLen - n0 - n1 - n2;
+        off[n0 * 81 + (n0 + n1) * 9 + (n0 + n1 + n2)] = (uint32_t)seq.size();
+        cnt[0] = n0;
+        cnt[1] = n1;
+        cnt[2] = n2;
+        cnt[3] = n3;
+        cur = 0;
+        emit(emit, 0);
+      }
+}
+
 int upload(llvq::Codebook& cb, int device) {
   using namespace llvq;
   const size_t n = cb.cls.size();
@@ -352,6 +387,8 @@ int upload(llvq::Codebook& cb, int device) {
   const size_t o_bucket = off; off = align256(off + (kBuckets + 1) * sizeof(uint16_t));
   const size_t o_pword = off; off = align256(off + (kNumGolay / 2) * sizeof(uint32_t));
   const size_t o_plex = off; off = align256(off + (kNumGolay / 2) * sizeof(uint16_t));
+  const size_t o_toff = off; off = align256(off + kTailKeys * sizeof(uint32_t));
+  const size_t o_tseq = off; off = align256(off + kTailSeqs * sizeof(uint16_t));
   std::vector<unsigned char> host(off, 0);
   {
     std::vector<DecodeClass> dc(n);
@@ -396,6 +433,14 @@ int upload(llvq::Codebook& cb, int device) {
   std::memcpy(host.data() + o_byw, cb.by_weight.data(), kNumGolay * sizeof(uint16_t));
   std::memcpy(host.data() + o_pword, cb.plist_word.data(), (kNumGolay / 2) * sizeof(uint32_t));
   std::memcpy(host.data() + o_plex, cb.plist_lex.data(), (kNumGolay / 2) * sizeof(uint16_t));
+  {
+    std::vector<uint32_t> toff;
+    std::vector<uint16_t> tseq;
+    build_tail_tables(toff, tseq);
+    if ((int)tseq.size() != kTailSeqs) return fail(LLVQ_ERR_UNSUPPORTED, "tail table broken");
+    std::memcpy(host.data() + o_toff, toff.data(), kTailKeys * sizeof(uint32_t));
+    std::memcpy(host.data() + o_tseq, tseq.data(), kTailSeqs * sizeof(uint16_t));
+  }
   int prev = -1;
   cudaError_t e = cudaGetDevice(&prev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -424,6 +469,8 @@ int upload(llvq::Codebook& cb, int device) {
   d.bucket = reinterpret_cast<const uint16_t*>(base + o_bucket);
   d.plist_word = reinterpret_cast<const uint32_t*>(base + o_pword);
   d.plist_lex = reinterpret_cast<const uint16_t*>(base + o_plex);
+  d.tail_off = reinterpret_cast<const uint32_t*>(base + o_toff);
+  d.tail_seq = reinterpret_cast<const uint16_t*>(base + o_tseq);
   std::copy(cb.weight_start, cb.weight_start + 25, d.weight_start);
   d.n_classes = (int32_t)n;
   d.min_shell = cb.min_shell;

@@ -383,6 +383,7 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
         FastPart part;
         uint32_t mask, val;  // mask: positions still to fill, lowest first
         int base;            // rem = base - t
+        uint32_t pvals = (uint32_t)(nfirst == 0 || odd ? pv0 : pv1);  // the part's values, bytes 0..3
         if (nfirst == 0) {  // weight 0: only the f0 part
           fast_part_load(part, pv0, cnt2);
           mask = kFull24;
@@ -403,17 +404,18 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
           row[__ffs(mask) - 1] = (uint8_t)val;
           mask &= mask - 1u;
         }
-        // steps 4..23 in blocks of four, not unrolled (a part can only switch
+        // steps 4..15 in blocks of four, not unrolled (a part can only switch
         // at a block start: 8, 12 or 16), so the code stays small enough for
         // the instruction cache
 #pragma unroll 1
-        for (int tb = 4; tb < kDim; tb += 4) {
+        for (int tb = 4; tb < kDim - kTailLen; tb += 4) {
           if (tb == nfirst) {  // even: the word's positions are done, the f0 part fills the rest
             fast_part_load(part, pv0, cnt2);
             part.rank = (uint32_t)rank2;
             part.N = (uint32_t)N2;
             mask = ~word & kFull24;
             div = sh.div32 + kDim;
+            pvals = (uint32_t)pv0;
           }
           const uint2* d = div - tb;
 #pragma unroll
@@ -422,6 +424,23 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
             row[__ffs(mask) - 1] = (uint8_t)val;
             mask &= mask - 1u;
           }
+        }
+        if (nfirst == kDim - kTailLen) {  // weight 16: the f0 part is exactly the last eight steps
+          fast_part_load(part, pv0, cnt2);
+          part.rank = (uint32_t)rank2;
+          mask = ~word & kFull24;
+          pvals = (uint32_t)pv0;
+        }
+        // Steps 16..23 end the last part of every class (odd, weight 0 or 24:
+        // the only part; weight 8, 12 or 16: the f0 part): one lookup in the
+        // tail table by the remaining counts and rank (bounded by the table
+        // sizes, which valid counts and ranks never reach).
+        const uint32_t key = min(part.c0 * 81u + part.c1 * 9u + part.c2, (uint32_t)kTailKeys - 1u);
+        const uint32_t seq = __ldg(book.tail_seq + min(__ldg(book.tail_off + key) + part.rank, (uint32_t)kTailSeqs - 1u));
+#pragma unroll
+        for (int i = 0; i < kTailLen; ++i) {
+          row[__ffs(mask) - 1] = (uint8_t)__byte_perm(pvals, 0u, (seq >> (2 * i)) & 3u);
+          mask &= mask - 1u;
         }
       }
       const uint32_t* rw = sh.rows + threadIdx.x * kRowWords;

@@ -79,6 +79,15 @@ static_assert(sizeof(DecodeClass) == 96, "decode record is six 16-byte loads");
 constexpr uint32_t kMetaFast = 1u << 20;
 constexpr uint32_t kMetaWide = 1u << 21;
 
+// Tail table of the decoder: the last kTailLen steps of a part of at most
+// four values are one lookup.  Block of the count vector (n0..n3), n0 + ... +
+// n3 = 8, at tail_off[c0 * 81 + c1 * 9 + c2] (cumulative c0 = n0, c1 = n0 +
+// n1, c2 = n0 + n1 + n2); inside it, the multinomial(n) sequences in
+// lexicographic order (value 0 first), value index of step i in bits 2i..2i+1.
+constexpr int kTailLen = 8;
+constexpr int kTailKeys = 9 * 9 * 9;
+constexpr int kTailSeqs = 1 << (2 * kTailLen);
+
 // Everything a kernel needs about one codebook (plain pointers, passed by value).
 struct DevBook {
   const DevClass* cls;
@@ -92,6 +101,8 @@ struct DevBook {
   const uint16_t* by_weight;      // [4096] lex indices grouped by weight (lex order inside)
   const uint32_t* plist_word;     // [2048] the lighter word of each complementary pair, weights 0, 8, 12 in order
   const uint16_t* plist_lex;      // [2048] its lexicographic index (the complement's is 4095 minus it)
+  const uint32_t* tail_off;       // [kTailKeys] start of each count vector's block in tail_seq
+  const uint16_t* tail_seq;       // [kTailSeqs] every 8-step sequence over 4 values, by count vector then rank
   int32_t weight_start[25];       // start of each weight group in by_weight
   int32_t n_classes;
   int32_t min_shell, max_shell;
