@@ -15,6 +15,8 @@
 // are computed exactly -- a product, a shift by the power of two in rem and a
 // multiply by the inverse of its odd part -- and compared with the rank; the
 // magnitude goes straight to its position in a per-thread shared-memory row.
+// The last eight steps, which always end a part, are one lookup in a table of
+// all eight-step sequences over four values (DevBook::tail_seq).
 // Parts of up to eight values, or whose N stays at or above 2^32 past their
 // first step, use the same step with seven boundaries (wide_step, 64-bit while
 // N >= 2^32), taken by a whole warp at once.
