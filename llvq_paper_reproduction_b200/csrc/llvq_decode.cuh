@@ -42,12 +42,23 @@ struct DecodeShared {
   uint32_t shift[kDim + 1]; // trailing zeros of d
   uint2 div32[kDim + 1];    // {inverse of the odd part of d modulo 2^32, trailing zeros of d}
   uint32_t rows[kDecodeThreads * kRowWords];  // each thread's codeword magnitudes, by position
+  uint8_t deposit4[256];  // [m * 16 + s]: the low popc(m) bits of s placed on the set bits of m, in order
 };
 
 // Fill the shared tables (call with the whole block, then __syncthreads()).
 __device__ __forceinline__ void decode_setup(const DevBook& book, DecodeShared& sh) {
   if (book.n_classes <= kMaxSmemClasses)
     for (int k = threadIdx.x; k < book.n_classes; k += blockDim.x) sh.starts[k] = book.class_start[k];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    const uint32_t m = i >> 4;
+    uint32_t src = i & 15, dep = 0;
+    for (int b = 0; b < 4; ++b)
+      if ((m >> b) & 1u) {
+        dep |= (src & 1u) << b;
+        src >>= 1;
+      }
+    sh.deposit4[i] = (uint8_t)dep;
+  }
   if (threadIdx.x <= kDim && threadIdx.x > 0) {
     const uint32_t d = threadIdx.x, s = __ffs(d) - 1;
     sh.shift[d] = s;
@@ -483,10 +494,10 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
       }
       neg = 0;
 #pragma unroll
-      for (int d = 0; d < kDim; ++d) {
-        const uint32_t nzd = (nzmask >> d) & 1u;
-        neg |= (cmask & nzd) << d;
-        cmask >>= nzd;
+      for (int k = 0; k < kDim / 4; ++k) {  // four positions at a time
+        const uint32_t m = (nzmask >> (4 * k)) & 15u;
+        neg |= (uint32_t)sh.deposit4[m * 16 + (cmask & 15u)] << (4 * k);
+        cmask >>= __popc(m);
       }
       if (word && (__popc(neg & word) & 1) != (int)((meta >> 19) & 1)) neg ^= word & (0u - word);
     }
