@@ -3,7 +3,7 @@
 // (impl/leech_lattice_vector_quantizer.py:282-314), fused with the index
 // encoding (encode_codeword, :247-280).
 //
-// One CTA per 24-D block at a time (persistent grid), 128 threads x 16
+// One CTA per 24-D block at a time (persistent grid), 256 threads x 8
 // complementary Golay word pairs (c, ~c) each.  Per block it stages |x| in
 // sorted order, the 3 byte tables that permute a Golay word into that order,
 // and the integer image q = rint(|x| * 2^e) with |q| <= 2^19.  Per pair it
@@ -45,10 +45,15 @@ __device__ __forceinline__ float llvq_max3(float a, float b, float c) {
 
 namespace llvq {
 
-constexpr int kSearchThreads = 128;
-// At least 6 CTAs per SM (<= 85 registers): the search is issue-bound and
-// the extra resident warps outweigh a few spilled bytes (+4% on shells 2..13).
-constexpr int kSearchMinBlocks = 6;
+// 256 threads (8 pairs each), at least 3 CTAs per SM (<= 85 registers: 24
+// resident warps; the search is issue-bound and the extra warps outweigh a
+// few spilled bytes).  The CTA's warps realign at every pair (a barrier), so
+// the 8 warps of a CTA run the same stretch of the generated scoring code and
+// share the instruction cache: 128 threads without the barrier ran 3.6%
+// slower on shells 2..13, 26% slower on shell 23 and 37% slower on shell 32,
+// whose scoring code is the largest.
+constexpr int kSearchThreads = 256;
+constexpr int kSearchMinBlocks = 3;
 constexpr int kWordsPerThread = kNumGolay / kSearchThreads;
 constexpr int kPairsPerThread = kWordsPerThread / 2;
 constexpr long long kTagWord = 1ll << 40;   // low 12 bits: the word
@@ -609,6 +614,7 @@ __global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kerne
       }
     };
     for (int i = 0; i < kPairsPerThread; ++i) {
+      __syncthreads();  // realign the CTA's warps (instruction cache)
       const int j = i * kSearchThreads + tid;
       const uint32_t c = __ldg(book.plist_word + j);
       const int lex = __ldg(book.plist_lex + j);
