@@ -391,7 +391,7 @@ def rate_sweep_bench(q, x, device, stream, args) -> dict:
     packing) on a sample of the batch, and SQNR in dB of the reconstruction.
     The sample is the first --sweep-rows blocks, cut so that one rate takes
     about 10 s when its search is slow (the 2.5 and 3.0 bits/dim shells 23
-    and 32 run the table-driven search)."""
+    and 32 have the largest scoring codes)."""
     import math
 
     import torch

@@ -173,10 +173,44 @@ class _Emitter:
         return self.lines
 
 
+# Golay words per weight; the scoring code a word runs is the odd classes'
+# plus the even classes' of its weight.
+WORDS_BY_WEIGHT = {0: 1, 8: 759, 12: 2576, 16: 759, 24: 1}
+# Codebooks whose scoring code issues more FFMAs per word than this (shell 32:
+# 2112; shells 2..13: 495; shell 23: 667) run 512-thread CTAs, one per SM:
+# 16 warps realigned at every pair share the instruction cache (+44% at
+# shell 32), where the smaller codes run best with 3 CTAs of 256 threads.
+LARGE_CODE_FFMA_PER_WORD = 1000
+
+
+def trie_size(items):
+    """FFMAs of the per-shell prefix tries of (shell, chain) items."""
+    roots, n = {}, 0
+    for shell, chain in items:
+        node = roots.setdefault(shell, {})
+        for t in chain:
+            if t not in node:
+                node[t] = {}
+                n += 1
+            node = node[t]
+    return n
+
+
+def ffma_per_word(classes, chains):
+    odd = trie_size([(c.shell, ch) for c, ch in zip(classes, chains) if c.parity == 1])
+    total = 0
+    for w, count in WORDS_BY_WEIGHT.items():
+        even = trie_size([(c.shell, ch) for c, ch in zip(classes, chains)
+                          if c.parity == 0 and even_terms(c.leader)[3] == w])
+        total += count * (odd + even)
+    return total / sum(WORDS_BY_WEIGHT.values())
+
+
 def emit_spec(name, classes):
     min_shell = min(c.shell for c in classes)
     max_shell = max(c.shell for c in classes)
     chains = ordered_chains(classes)
+    large = ffma_per_word(classes, chains) > LARGE_CODE_FFMA_PER_WORD
     lines = []
     L = lines.append
     l1max, mg, am = window_constants(classes, chains)
@@ -196,6 +230,8 @@ def emit_spec(name, classes):
     L(f"  static constexpr int kWinMG = {mg};")
     L(f"  static constexpr int kWinAM = {am};")
     L(f"  static constexpr bool kHasOdd = {'true' if has_odd else 'false'};")
+    L(f"  static constexpr int kCtaThreads = {512 if large else 256};")
+    L(f"  static constexpr int kCtaMinBlocks = {1 if large else 3};")
     for w in WEIGHTS:
         L(f"  static constexpr int kR0Max_w{w} = {r0max[w]};")
         L(f"  static constexpr bool kHasEven_w{w} = {'true' if has_w[w] else 'false'};")

@@ -4,7 +4,8 @@
 // encoding (encode_codeword, :247-280).
 //
 // One CTA per 24-D block at a time (persistent grid), 256 threads x 8
-// complementary Golay word pairs (c, ~c) each.  Per block it stages |x| in
+// complementary Golay word pairs (c, ~c) each (512 x 4 for the largest
+// codebooks).  Per block it stages |x| in
 // sorted order, the 3 byte tables that permute a Golay word into that order,
 // and the integer image q = rint(|x| * 2^e) with |q| <= 2^19.  Per pair it
 // builds the suffix sums of the sorted (sign-flipped) coordinates in
@@ -45,17 +46,19 @@ __device__ __forceinline__ float llvq_max3(float a, float b, float c) {
 
 namespace llvq {
 
-// 256 threads (8 pairs each), at least 3 CTAs per SM (<= 85 registers: 24
-// resident warps; the search is issue-bound and the extra warps outweigh a
-// few spilled bytes).  The CTA's warps realign at every pair (a barrier), so
-// the 8 warps of a CTA run the same stretch of the generated scoring code and
-// share the instruction cache: 128 threads without the barrier ran 3.6%
-// slower on shells 2..13, 26% slower on shell 23 and 37% slower on shell 32,
-// whose scoring code is the largest.
+// CTA shape of the search, per codebook (the generated Spec's kCtaThreads /
+// kCtaMinBlocks; table-driven codebooks use the first): 256 threads (8 pairs
+// each), at least 3 CTAs per SM (<= 85 registers: 24 resident warps; the
+// search is issue-bound and the extra warps outweigh a few spilled bytes), or
+// for the largest scoring codes 512 threads (4 pairs each), one CTA per SM.
+// The CTA's warps realign at every pair (a barrier), so they run the same
+// stretch of the generated scoring code and share the instruction cache: 128
+// threads without the barrier ran 3.6% slower on shells 2..13, 26% slower on
+// shell 23 and 37% slower on shell 32; on shell 32, 512 threads gain another
+// 44% over 256.
+constexpr int kMaxSearchThreads = 512;
 constexpr int kSearchThreads = 256;
 constexpr int kSearchMinBlocks = 3;
-constexpr int kWordsPerThread = kNumGolay / kSearchThreads;
-constexpr int kPairsPerThread = kWordsPerThread / 2;
 constexpr long long kTagWord = 1ll << 40;   // low 12 bits: the word
 constexpr long long kTagExact = 2ll << 40;  // bits 12..39: class, low 12 bits: word
 
@@ -71,9 +74,9 @@ struct RowShared {
   int invalid;
   float scale;          // 2^e
   float K;              // sqrt(8) * 2^e in fp32
-  float red[kSearchThreads / 32];
-  double xs_best[kSearchThreads];
-  long long xs_order[kSearchThreads];
+  float red[kMaxSearchThreads / 32];
+  double xs_best[kMaxSearchThreads];
+  long long xs_order[kMaxSearchThreads];
 };
 
 // The same block data for one thread (finalize kernel), without the byte tables.
@@ -187,6 +190,8 @@ __device__ void build_candidate(const float* x, const int8_t* apos, const DevCla
 // Generated specialisations: everything is a compile-time constant.
 template <class S>
 struct Ops {
+  static constexpr int kThreads = S::kCtaThreads;
+  static constexpr int kMinBlocks = S::kCtaMinBlocks;
   static constexpr int kNumShells = S::kNumShells;
   static constexpr int kMinShellC = S::kMinShell;
   static constexpr bool kHasOdd = S::kHasOdd;
@@ -243,6 +248,8 @@ __device__ __forceinline__ float runtime_chain(const DevClass& c, const float* R
 
 template <>
 struct Ops<RuntimeSpec> {
+  static constexpr int kThreads = kSearchThreads;
+  static constexpr int kMinBlocks = kSearchMinBlocks;
   static constexpr int kNumShells = kRuntimeShells;
   static constexpr int kMinShellC = -1;
   static constexpr bool kHasOdd = true;
@@ -580,9 +587,13 @@ __device__ void stage_row(const float* __restrict__ x, int64_t row, RowShared& s
 }
 
 template <class S>
-__global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kernel(const float* __restrict__ x, int64_t n, DevBook book,
+__global__ void __launch_bounds__(Ops<S>::kThreads, Ops<S>::kMinBlocks) search_kernel(const float* __restrict__ x, int64_t n, DevBook book,
                                                                 long long* tag_out, float* m_out) {
   __shared__ RowShared sh;
+  constexpr int T = Ops<S>::kThreads;
+  constexpr int kWordsPerThread = kNumGolay / T;
+  constexpr int kPairsPerThread = kWordsPerThread / 2;
+  static_assert(T <= kMaxSearchThreads && kNumGolay % (2 * T) == 0, "CTA shape");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NS = Ops<S>::kNumShells;
   const int min_shell = Ops<S>::kMinShellC >= 0 ? Ops<S>::kMinShellC : book.min_shell;
@@ -615,7 +626,7 @@ __global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kerne
     };
     for (int i = 0; i < kPairsPerThread; ++i) {
       __syncthreads();  // realign the CTA's warps (instruction cache)
-      const int j = i * kSearchThreads + tid;
+      const int j = i * T + tid;
       const uint32_t c = __ldg(book.plist_word + j);
       const int lex = __ldg(book.plist_lex + j);
       float bc, bn;
@@ -628,7 +639,7 @@ __global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kerne
     __syncthreads();
     float M = sh.red[0];
 #pragma unroll
-    for (int w = 1; w < kSearchThreads / 32; ++w) M = fmaxf(M, sh.red[w]);
+    for (int w = 1; w < T / 32; ++w) M = fmaxf(M, sh.red[w]);
     const float thr = __double2float_rd((double)M - window_width(sh.K, book));
     const int contenders = __syncthreads_count(b1 >= thr);
     const int second = __syncthreads_or(b2 >= thr);
@@ -643,7 +654,7 @@ __global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kerne
       double best = -INFINITY;
       long long order = LLONG_MAX;
       for (int i = 0; i < kWordsPerThread; ++i) {
-        const int j = i * kSearchThreads + tid;
+        const int j = i * T + tid;
         const uint32_t c = __ldg(book.wlist_word + j);
         const int lex = __ldg(book.wlist_lex + j);
         word_cands<S>(book, sh, c, nmk, thr,
@@ -653,7 +664,7 @@ __global__ void __launch_bounds__(kSearchThreads, kSearchMinBlocks) search_kerne
       sh.xs_order[tid] = order;
       __syncthreads();
       if (tid == 0) {
-        for (int t = 1; t < kSearchThreads; ++t) {
+        for (int t = 1; t < T; ++t) {
           if (sh.xs_best[t] > best || (sh.xs_best[t] == best && sh.xs_order[t] < order)) {
             best = sh.xs_best[t];
             order = sh.xs_order[t];
@@ -767,11 +778,11 @@ static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book,
     int dev;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, search_kernel<S>, kSearchThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, search_kernel<S>, Ops<S>::kThreads, 0);
     if (blocks_per_sm < 1) blocks_per_sm = 1;
   }
   const int64_t grid = std::min<int64_t>(n, (int64_t)sms * blocks_per_sm);
-  search_kernel<S><<<(unsigned)grid, kSearchThreads, 0, stream>>>(x, n, book, pair, score);
+  search_kernel<S><<<(unsigned)grid, Ops<S>::kThreads, 0, stream>>>(x, n, book, pair, score);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   finalize_kernel<S><<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(x, n, book, pair, score, index, pair, score);
