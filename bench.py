@@ -46,10 +46,10 @@ SMS = 148
 FP32_LANES = 128
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) measured with ncu
 # on smaller launches of the same kernels, per unit, for the roofline
-# `traffic` entry: the search kernel on 65,536 blocks (6,676,992 + 52,480 B)
-# and the bf16 dequant kernel on 9,797,632 indices (78,546,432 + 410,793,728 B).
-SEARCH_DRAM_BYTES_PER_BLOCK = (6_676_992 + 52_480) / 65_536
-DEQUANT_DRAM_BYTES_PER_INDEX = (78_546_432 + 410_793_728) / 9_797_632
+# `traffic` entry: the search kernel on 65,536 blocks (6,622,720 + 663,040 B)
+# and the bf16 dequant kernel on 9,797,632 indices (78,706,688 + 418,110,976 B).
+SEARCH_DRAM_BYTES_PER_BLOCK = (6_622_720 + 663_040) / 65_536
+DEQUANT_DRAM_BYTES_PER_INDEX = (78_706_688 + 418_110_976) / 9_797_632
 
 
 def log(*a):
