@@ -21,21 +21,6 @@ constexpr int kDeqThreads = 256;
 // dequant workload; the decode is issue-bound and latency-bound in turn.
 constexpr int kDeqMinBlocks = 5;
 
-// Index i of a source: one 8-byte load, or the packed bytes (6-byte indices,
-// the 48-bit codebook's, as three 2-byte loads); all-ones packed -> -1.
-__device__ __forceinline__ int64_t load_index(IndexSource src, int64_t i) {
-  if (src.bytes == 8) return __ldg(static_cast<const int64_t*>(src.ptr) + i);
-  uint64_t v = 0;
-  if (src.bytes == 6) {
-    const uint16_t* h = static_cast<const uint16_t*>(src.ptr) + i * 3;
-    v = (uint64_t)__ldg(h) | ((uint64_t)__ldg(h + 1) << 16) | ((uint64_t)__ldg(h + 2) << 32);
-  } else {
-    const uint8_t* b = static_cast<const uint8_t*>(src.ptr) + i * src.bytes;
-    for (int k = 0; k < src.bytes; ++k) v |= (uint64_t)__ldg(b + k) << (8 * k);
-  }
-  return v == (~0ull >> (64 - 8 * src.bytes)) ? -1 : (int64_t)v;
-}
-
 template <int KIND>
 __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(IndexSource index, int64_t n,
                                                               DevBook book, void* __restrict__ out,

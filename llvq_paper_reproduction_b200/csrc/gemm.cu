@@ -299,6 +299,7 @@ cudaError_t gemm_staged_launch(const Codebook& cb, IndexSource idx, int64_t n_ou
                                const uint16_t* rscale, const void* a, int64_t m, int64_t k, float* y,
                                int* error_flag, void* staging, int64_t staging_bytes, cudaStream_t stream) {
   if (m <= 0 || n_out <= 0) return cudaSuccess;
+  if (m <= kGemvMaxM) return gemv_decode_launch(cb, idx, n_out, bpr, rscale, a, m, k, y, stream);
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;

@@ -29,8 +29,24 @@
 #include <cstdint>
 
 #include "llvq_device.cuh"
+#include "llvq_internal.h"
 
 namespace llvq {
+
+// Index i of a source: one 8-byte load, or the packed bytes (6-byte indices,
+// the 48-bit codebook's, as three 2-byte loads); all-ones packed -> -1.
+__device__ __forceinline__ int64_t load_index(IndexSource src, int64_t i) {
+  if (src.bytes == 8) return __ldg(static_cast<const int64_t*>(src.ptr) + i);
+  uint64_t v = 0;
+  if (src.bytes == 6) {
+    const uint16_t* h = static_cast<const uint16_t*>(src.ptr) + i * 3;
+    v = (uint64_t)__ldg(h) | ((uint64_t)__ldg(h + 1) << 16) | ((uint64_t)__ldg(h + 2) << 32);
+  } else {
+    const uint8_t* b = static_cast<const uint8_t*>(src.ptr) + i * src.bytes;
+    for (int k = 0; k < src.bytes; ++k) v |= (uint64_t)__ldg(b + k) << (8 * k);
+  }
+  return v == (~0ull >> (64 - 8 * src.bytes)) ? -1 : (int64_t)v;
+}
 
 constexpr int kMaxSmemClasses = 1024;
 constexpr int kDecodeThreads = 256;  // blocks up to this size get per-thread rows
@@ -256,7 +272,7 @@ __device__ __forceinline__ uint32_t wide_step(WidePart& p, int rem, int nb, cons
 // step takes the 64-bit form while any index of the warp has N >= 2^32, and
 // tests as many boundaries as the warp's largest part needs (nvals: this
 // index's largest count of distinct values in a part).
-__device__ __noinline__ void decode_wide(uint32_t word, bool odd, int nfirst, uint64_t rank, uint64_t N, uint64_t cnt,
+static __device__ __noinline__ void decode_wide(uint32_t word, bool odd, int nfirst, uint64_t rank, uint64_t N, uint64_t cnt,
                                          uint64_t rank2, uint64_t N2, uint64_t cnt2, uint64_t pv0, uint64_t pv1,
                                          int nvals, const DecodeShared& sh, uint8_t* row) {
   const unsigned lanes = __activemask();  // every lane here runs the 24 steps
@@ -282,7 +298,7 @@ __device__ __noinline__ void decode_wide(uint32_t word, bool odd, int nfirst, ui
 // with more than four values, or N >= 2^32 after a part's first step): the
 // general step, a nibble sequence of value indices, then the scatter.  Kept
 // out of line: rarely run, and the decoder's hot code must stay small.
-__device__ __noinline__ void decode_general(uint32_t word, bool odd, int nfirst, uint64_t rank, uint64_t N, uint64_t cnt,
+static __device__ __noinline__ void decode_general(uint32_t word, bool odd, int nfirst, uint64_t rank, uint64_t N, uint64_t cnt,
                                             uint64_t rank2, uint64_t N2, uint64_t cnt2, uint64_t pv0, uint64_t pv1,
                                             const DecodeShared& sh, uint32_t* mag) {
   uint64_t seq_lo = 0, seq_hi = 0;  // 4-bit value indices, step order

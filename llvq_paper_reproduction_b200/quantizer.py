@@ -242,7 +242,9 @@ class LeechLatticeVectorQuantizerGpu:
         """Dequant-GEMM: ``a @ W.T`` in fp32 for bf16 activations ``a`` [m, k]
         and a weight given by its indices [n, blocks] (int64, or packed uint8
         [n, blocks, index_bytes]; W[n] = dequantize(indices[n]).flatten()[:k]
-        * row_scale[n]).  The weight is decoded into a bf16 staging buffer
+        * row_scale[n]).  For m <= 4 one kernel decodes each weight block in
+        registers and multiplies it there (one warp per output row, a fixed
+        reduction order); larger m decode into a bf16 staging buffer
         (stream-ordered, at most 256 MiB, chunk by chunk beyond that) that a
         pipelined tcgen05 GEMM reads.  ``rotation=(block, signs)`` first
         rotates the activations with the seeded Hadamard transform the weight

@@ -53,6 +53,25 @@ def test_gemm_matches_dequantize_matmul(m_act, n, bpr, k):
     assert rel_err(y2, reference(q, a, idx, None, k)) <= TOL
 
 
+# m <= 4 takes the fused decode-in-registers kernel (no staging): partial
+# last blocks (k not a multiple of 24), each batch-size template, wide rows,
+# and the first staged size (5)
+@pytest.mark.parametrize("m_act,n,bpr,k", [(1, 77, 33, 784), (2, 40, 3, 64), (3, 129, 20, 472), (4, 64, 171, 4104),
+                                           (1, 1000, 598, 14336), (4, 9, 171, 4096), (5, 300, 20, 472)])
+def test_small_batch_gemm(m_act, n, bpr, k):
+    q = api()
+    g = torch.Generator(device="cuda").manual_seed(6)
+    idx = torch.randint(0, q.total_count, (n, bpr), generator=g, device="cuda")
+    a = torch.randn((m_act, k), generator=g, device="cuda").to(torch.bfloat16)
+    scale = (torch.rand(n, generator=g, device="cuda") * 0.04 + 0.005).to(torch.float16)
+    y = q.gemm(a, idx, scale)
+    assert y.shape == (m_act, n)
+    assert rel_err(y, reference(q, a, idx, scale, k)) <= TOL
+    assert torch.equal(y, q.gemm(a, idx, scale))  # one summation order: the same result every call
+    packed = q.pack_indices(idx)
+    assert torch.equal(y, q.gemm(a, packed, scale))
+
+
 def test_gemm_argument_checks():
     q = api(4)
     idx = torch.zeros((4, 2), dtype=torch.long, device="cuda")
