@@ -94,7 +94,10 @@ int llvq_dequantize_bf16(const llvq_codebook* cb, const int64_t* indices, int64_
  * dequantized indices[n * blocks_per_row + b] (b = 0 .. blocks_per_row-1,
  * 24 columns each) times row_scale[n] (fp16 bits; NULL means 1).  a: bf16
  * [m, k] row-major, 16-byte aligned, k % 8 == 0, k <= 24 * blocks_per_row
- * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  The weights
+ * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  For m <= 4
+ * one kernel decodes each weight block in registers and multiplies it there
+ * (a warp per output row, a fixed summation order; nothing is allocated).
+ * Otherwise the weights
  * are decoded into a bf16 staging buffer (at most 256 MiB, chunk by chunk
  * beyond that; stream-ordered on `stream` from a library-owned memory pool
  * that keeps its reservation between calls) that a pipelined

@@ -601,6 +601,9 @@ int gemm_impl(const llvq_codebook* h, llvq::IndexSource src, int64_t n_out, int6
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
   if (m == 0 || n_out == 0) return LLVQ_OK;
   return on_device(h, [&] {
+    if (m <= llvq::kGemvMaxM)  // decoded in registers: no staging
+      return llvq::gemv_decode_launch(h->cb, src, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
+                                      (cudaStream_t)stream);
     // stream-ordered staging buffer from the library's pool, released on the
     // same stream after the GEMM
     const int64_t bytes = llvq::gemm_staging_bytes(n_out, blocks_per_row, kGemmStagingBudget);
