@@ -176,10 +176,13 @@ class _Emitter:
 # Golay words per weight; the scoring code a word runs is the odd classes'
 # plus the even classes' of its weight.
 WORDS_BY_WEIGHT = {0: 1, 8: 759, 12: 2576, 16: 759, 24: 1}
-# Codebooks whose scoring code issues more FFMAs per word than this (shell 32:
-# 2112; shells 2..13: 495; shell 23: 667) run 512-thread CTAs, one per SM:
-# 16 warps realigned at every pair share the instruction cache (+44% at
-# shell 32), where the smaller codes run best with 3 CTAs of 256 threads.
+# CTA shape by the FFMAs per word of the scoring code (shell 32: 2112; shell
+# 23: 667; shells 2..13: 495; shell 13: 111; shell 11: 77).  Up to
+# SMALL_CODE the code fits the instruction cache as it is: 6 CTAs of 128
+# threads, no realignment.  Up to LARGE_CODE: 3 CTAs of 256 threads whose
+# warps realign at every pair (a barrier) so they share the cache.  Beyond:
+# one 512-thread CTA per SM, 16 warps realigned (+44% at shell 32 over 256).
+SMALL_CODE_FFMA_PER_WORD = 200
 LARGE_CODE_FFMA_PER_WORD = 1000
 
 
@@ -210,7 +213,9 @@ def emit_spec(name, classes):
     min_shell = min(c.shell for c in classes)
     max_shell = max(c.shell for c in classes)
     chains = ordered_chains(classes)
-    large = ffma_per_word(classes, chains) > LARGE_CODE_FFMA_PER_WORD
+    fpw = ffma_per_word(classes, chains)
+    threads, min_blocks = (128, 6) if fpw <= SMALL_CODE_FFMA_PER_WORD else \
+        (256, 3) if fpw <= LARGE_CODE_FFMA_PER_WORD else (512, 1)
     lines = []
     L = lines.append
     l1max, mg, am = window_constants(classes, chains)
@@ -230,8 +235,9 @@ def emit_spec(name, classes):
     L(f"  static constexpr int kWinMG = {mg};")
     L(f"  static constexpr int kWinAM = {am};")
     L(f"  static constexpr bool kHasOdd = {'true' if has_odd else 'false'};")
-    L(f"  static constexpr int kCtaThreads = {512 if large else 256};")
-    L(f"  static constexpr int kCtaMinBlocks = {1 if large else 3};")
+    L(f"  static constexpr int kCtaThreads = {threads};")
+    L(f"  static constexpr int kCtaMinBlocks = {min_blocks};")
+    L(f"  static constexpr bool kCtaRealign = {'true' if threads > 128 else 'false'};")
     for w in WEIGHTS:
         L(f"  static constexpr int kR0Max_w{w} = {r0max[w]};")
         L(f"  static constexpr bool kHasEven_w{w} = {'true' if has_w[w] else 'false'};")

@@ -47,15 +47,17 @@ __device__ __forceinline__ float llvq_max3(float a, float b, float c) {
 namespace llvq {
 
 // CTA shape of the search, per codebook (the generated Spec's kCtaThreads /
-// kCtaMinBlocks; table-driven codebooks use the first): 256 threads (8 pairs
-// each), at least 3 CTAs per SM (<= 85 registers: 24 resident warps; the
-// search is issue-bound and the extra warps outweigh a few spilled bytes), or
-// for the largest scoring codes 512 threads (4 pairs each), one CTA per SM.
-// The CTA's warps realign at every pair (a barrier), so they run the same
-// stretch of the generated scoring code and share the instruction cache: 128
-// threads without the barrier ran 3.6% slower on shells 2..13, 26% slower on
-// shell 23 and 37% slower on shell 32; on shell 32, 512 threads gain another
-// 44% over 256.
+// kCtaMinBlocks / kCtaRealign, chosen by the size of its scoring code;
+// table-driven codebooks use 256 threads, 3 CTAs): small codes (shells 2..11,
+// 13 alone) run 6 CTAs of 128 threads (16 pairs each, <= 85 registers); the
+// shells 2..13 and shell 23 codes 3 CTAs of 256 threads (8 pairs each); the
+// shell 32 code one CTA of 512 (4 pairs each).  The search is issue-bound and
+// the resident warps outweigh a few spilled bytes.  In the larger shapes the
+// CTA's warps realign at every pair (a barrier), so they run the same stretch
+// of the generated scoring code and share the instruction cache: 128 threads
+// without the barrier ran 3.6% slower on shells 2..13, 26% slower on shell 23
+// and 37% slower on shell 32; on shell 32, 512 threads gain another 44% over
+// 256.  On the small codes the barrier costs about 2%.
 constexpr int kMaxSearchThreads = 512;
 constexpr int kSearchThreads = 256;
 constexpr int kSearchMinBlocks = 3;
@@ -192,6 +194,7 @@ template <class S>
 struct Ops {
   static constexpr int kThreads = S::kCtaThreads;
   static constexpr int kMinBlocks = S::kCtaMinBlocks;
+  static constexpr bool kRealign = S::kCtaRealign;
   static constexpr int kNumShells = S::kNumShells;
   static constexpr int kMinShellC = S::kMinShell;
   static constexpr bool kHasOdd = S::kHasOdd;
@@ -250,6 +253,7 @@ template <>
 struct Ops<RuntimeSpec> {
   static constexpr int kThreads = kSearchThreads;
   static constexpr int kMinBlocks = kSearchMinBlocks;
+  static constexpr bool kRealign = true;
   static constexpr int kNumShells = kRuntimeShells;
   static constexpr int kMinShellC = -1;
   static constexpr bool kHasOdd = true;
@@ -625,7 +629,7 @@ __global__ void __launch_bounds__(Ops<S>::kThreads, Ops<S>::kMinBlocks) search_k
       }
     };
     for (int i = 0; i < kPairsPerThread; ++i) {
-      __syncthreads();  // realign the CTA's warps (instruction cache)
+      if constexpr (Ops<S>::kRealign) __syncthreads();  // realign the CTA's warps (instruction cache)
       const int j = i * T + tid;
       const uint32_t c = __ldg(book.plist_word + j);
       const int lex = __ldg(book.plist_lex + j);
