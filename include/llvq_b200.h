@@ -116,7 +116,8 @@ int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, in
  * fail on out-of-memory halfway): the decoded weights are staged in a fixed
  * LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 MiB) array compiled into the library,
  * one per device, instead of a stream-ordered pool buffer, a chunk of rows at a
- * time.  Same arguments, results and error flag as llvq_gemm, plus the limit
+ * time (batches of m <= 4 are decoded in registers, as in llvq_gemm, and do
+ * not use the array).  Same arguments, results and error flag as llvq_gemm, plus the limit
  * blocks_per_row <= LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW (2730: one 128-row
  * tile of rows up to 65536 columns fits the array); wider rows return
  * LLVQ_ERR_INVALID_ARGUMENT.  The array needs no initial contents.  The first
