@@ -31,6 +31,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 
@@ -304,13 +305,13 @@ cudaError_t gemm_staged_launch(const Codebook& cb, IndexSource idx, int64_t n_ou
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  static bool configured[kMaxDevices] = {};
+  static std::atomic<bool> configured[kMaxDevices];  // kernel attributes set (idempotent if raced)
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     e = gemm_configure_device();
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   const int ldw = (int)gemm_staging_ldw(bpr);
   CUtensorMap ta;

@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <climits>
 #include <cmath>
@@ -777,15 +778,24 @@ __global__ void __launch_bounds__(128) finalize_kernel(const float* __restrict__
 template <class S>
 static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book, long long* index, long long* pair,
                                  float* score, cudaStream_t stream) {
-  static int blocks_per_sm = 0, sms = 0;
-  if (!blocks_per_sm) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, search_kernel<S>, Ops<S>::kThreads, 0);
-    if (blocks_per_sm < 1) blocks_per_sm = 1;
+  // persistent grid: SMs x resident CTAs, looked up once per device (host
+  // threads that race here compute the same value)
+  static std::atomic<int> grid_cap[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  int cap = grid_cap[dev].load(std::memory_order_relaxed);
+  if (cap <= 0) {
+    int sms = 0, blocks_per_sm = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, search_kernel<S>, Ops<S>::kThreads, 0);
+    if (e != cudaSuccess) return e;
+    cap = sms * std::max(blocks_per_sm, 1);
+    grid_cap[dev].store(cap, std::memory_order_relaxed);
   }
-  const int64_t grid = std::min<int64_t>(n, (int64_t)sms * blocks_per_sm);
+  const int64_t grid = std::min<int64_t>(n, (int64_t)cap);
   search_kernel<S><<<(unsigned)grid, Ops<S>::kThreads, 0, stream>>>(x, n, book, pair, score);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
