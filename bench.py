@@ -292,16 +292,19 @@ def run_gpu_arm(args) -> None:
         raise RuntimeError("end-to-end indices differ from the device-resident run")
 
     extra = {}
+    mq = None
     if args.model_layers > 0:  # every rank takes part (sharded by matrix)
         mq = model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks)
-        if rank == 0:
-            extra["model_quant"] = mq
-    if rank == 0 and world == 1 and not args.skip_dequant:
-        extra["dequant"] = dequant_bench(q, device, stream, args)
-    if rank == 0 and world == 1 and not args.skip_gemm:
-        extra["gemm"] = gemm_bench(q, device, stream, args)
     if rank == 0 and world == 1 and args.sweep_rows > 0:
         extra["rate_sweep"] = rate_sweep_bench(q, x, device, stream, args)
+    if rank == 0 and world == 1 and not args.skip_gemm:
+        extra["gemm"] = gemm_bench(q, device, stream, args)
+    if rank == 0 and world == 1 and not args.skip_dequant:
+        extra["dequant"] = dequant_bench(q, device, stream, args)
+    if rank == 0 and world == 1 and not args.skip_config1:
+        extra["config1"] = config1_bench(q, device, stream)
+    if rank == 0 and mq is not None:
+        extra["model_quant"] = mq  # last: the end of the line is what a truncated log keeps
     cpu = None
     if rank == 0 and world == 1 and args.cpu_sample > 0:
         sample = x_host[: args.cpu_sample].numpy()
@@ -366,7 +369,19 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    secs = max_over_ranks(e0.elapsed_time(e1) / 1000.0)
+    own_s = e0.elapsed_time(e1) / 1000.0
+    secs = max_over_ranks(own_s)
+    # strong-scaling efficiency: the job rate against N times the mean of
+    # the ranks' own rates on their shards (each rank runs the one-GPU code
+    # path on its matrices, so that mean stands for the one-GPU rate)
+    own_blocks = sum(specs[i].blocks for i in mine)
+    mean_rate = own_blocks / own_s
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([mean_rate], dtype=torch.float64, device=device)
+        dist.all_reduce(t)
+        mean_rate = float(t.item()) / world
     t0 = time.perf_counter()
     local = {k: (r["indices"], r["row_scale"]) for k, r in results.items()}  # stay on the device
     index_bytes = (mq.sg.bits + 7) // 8  # 48-bit shape-gain index -> 6 bytes per block on the wire
@@ -376,11 +391,11 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
     total = sum(s.blocks for s in specs)
     if rank == 0 and len(gathered) != len(specs):
         raise RuntimeError("gather lost matrices")
-    return {"workload": f"Llama-2-7B linears, {args.model_layers} layers ({len(specs)} matrices, {total} blocks), "
-                        "fp16 N(0, sigma_row^2) seed 2, Hadamard rotation, shape-gain 2 bits/dim, sharded by "
-                        "matrix", "n_gpus": world, "blocks": total, "seconds": secs, "blocks_per_s": total / secs,
-            "gather_seconds": gather_s, "gather_bytes": total * index_bytes + sum(s.out_features for s in specs) * 4,
-            "scaling": "strong (fixed model, split over the GPUs)"}
+    return {"workload": f"Llama-2-7B linears x{args.model_layers} layers, {total} blocks, shape-gain 2 b/dim, "
+                        "sharded by matrix (strong scaling)", "n_gpus": world, "seconds": secs,
+            "blocks_per_s": total / secs, "mean_gpu_blocks_per_s": mean_rate,
+            "strong_efficiency": (total / secs) / (world * mean_rate),
+            "gather_seconds": gather_s, "gather_bytes": total * index_bytes + sum(s.out_features for s in specs) * 4}
 
 
 def rate_sweep_bench(q, x, device, stream, args) -> dict:
@@ -433,6 +448,55 @@ def rate_sweep_bench(q, x, device, stream, args) -> dict:
     out["spherical_2.0"]["beta"] = sph.beta
     return {"workload": "the first blocks of the same N(0,1) batch (seed 1); blocks/s of the whole quantize call "
                         "(search + gain code + packing), SQNR = 10 log10(|x|^2 / |x - x_hat|^2)", "by_rate": out}
+
+
+def config1_bench(q, device, stream) -> dict:
+    """The 65,536-block Gaussian workload (N(0,1) fp32, torch CPU generator
+    seed 0): shape-gain at 2 bits/dim (shell-11 shape, 45 bits, + 3-bit
+    chi(24) gain code = 48 bits per block) and the reference's own quantize
+    over shells 2..13.  Indices are compared one by one with the committed
+    fixture of the oracle (the reference CPU quantizer restated, run over
+    every block: tests/golden/make_config1.py); SQNR of each reconstruction."""
+    import hashlib
+    import math
+
+    import torch
+
+    from llvq_paper_reproduction_b200.shaping import ShapeGainQuantizer
+
+    x = torch.randn((65536, 24), generator=torch.Generator().manual_seed(0), dtype=torch.float32)
+    fx_path = ROOT / "tests" / "golden" / "config1_indices.npz"
+    fx = np.load(fx_path) if fx_path.exists() else None
+    digest_ok = fx is not None and hashlib.sha256(x.numpy().tobytes()).hexdigest() == str(fx["sha256"])
+
+    def unpack6(b):
+        out = np.zeros((b.shape[0], 8), dtype=np.uint8)
+        out[:, :6] = b
+        return out.view("<u8").reshape(-1).astype(np.int64)
+
+    def sqnr_db(rec):
+        xd = x.double()
+        return 10.0 * math.log10(xd.pow(2).sum().item() / (xd - rec.double().cpu()).pow(2).sum().item())
+
+    xd = x.to(device)
+    sg = ShapeGainQuantizer.for_rate(2.0, device=device)
+    sg.quantize_parts(xd[:1024])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    sidx, gidx = sg.quantize_parts(xd)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_sg = e0.elapsed_time(e1) / 1000.0
+    ball = q.quantize(xd)
+    out = {"blocks": 65536, "input_sha256_matches_fixture": digest_ok,
+           "shape_gain_2.0": {"shell": sg.shell, "bits": sg.bits, "blocks_per_s": 65536 / t_sg,
+                              "sqnr_db": sqnr_db(sg.dequantize_parts(sidx, gidx))},
+           "ball_2..13": {"bits": q.shape_bits, "sqnr_db_at_unit_scale": sqnr_db(q.dequantize(ball))}}
+    if fx is not None:
+        out["shape_gain_2.0"]["shape_index_equal"] = int((sidx.cpu().numpy() == unpack6(fx["shape"])).sum())
+        out["ball_2..13"]["index_equal"] = int((ball.cpu().numpy() == unpack6(fx["ball"])).sum())
+    return out
 
 
 def dequant_bench(q, device, stream, args) -> dict:
@@ -565,6 +629,7 @@ def main():
     ap.add_argument("--dequant-layers", type=int, default=32)
     ap.add_argument("--cpu-dequant-sample", type=int, default=200_000)
     ap.add_argument("--skip-gemm", action="store_true")
+    ap.add_argument("--skip-config1", action="store_true")
     ap.add_argument("--model-layers", type=int, default=32,
                     help="Llama-2-7B layers of the whole-model quantization section (0 skips it)")
     ap.add_argument("--sweep-rows", type=int, default=4_194_304,

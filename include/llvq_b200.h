@@ -117,14 +117,18 @@ int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, in
  * LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 MiB) array compiled into the library,
  * one per device, instead of a stream-ordered pool buffer, a chunk of rows at a
  * time (batches of m <= 4 are decoded in registers, as in llvq_gemm, and do
- * not use the array).  Same arguments, results and error flag as llvq_gemm, plus the limit
- * blocks_per_row <= LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW (2730: one 128-row
- * tile of rows up to 65536 columns fits the array); wider rows return
- * LLVQ_ERR_INVALID_ARGUMENT.  The array needs no initial contents.  The first
- * call on each device does one-time setup (looks up the array's address with
- * cudaGetSymbolAddress, sets the kernels' shared-memory attributes) and should
- * come before any stream capture.  Calls that overlap on one device (unordered
- * streams, concurrent host threads) share the array and race: order them. */
+ * not use the array).  Same arguments, results and error flag as llvq_gemm, plus,
+ * for m > 4, the limit blocks_per_row <= LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW
+ * (2730: one 128-row tile of rows up to 65536 columns fits the array); wider
+ * rows return LLVQ_ERR_INVALID_ARGUMENT.  The array needs no initial contents.
+ * The array is device memory that the CUDA runtime allocates when it loads
+ * the library module holding it, which (with lazy module loading, the CUDA 12
+ * default) is the first call of this function on each device.  So make one
+ * call per device -- an empty one (m = 0 or n_out = 0) is enough -- before
+ * reserving the GPU's memory and before any stream capture; that call also
+ * sets the kernels' shared-memory limits.  Calls that overlap on one device
+ * (unordered streams, concurrent host threads) share the array and race:
+ * order them. */
 #define LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 << 20)
 #define LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW 2730
 int llvq_gemm_noalloc(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
@@ -175,6 +179,18 @@ int llvq_hadamard_ex(const void* in, int32_t in_type, void* out, int32_t out_typ
  * llvq_encode_host:    LeechLatticeVectorQuantizer.encode_codeword (CPU module :247-280) */
 int llvq_codeword_host(const llvq_codebook* cb, int64_t index, int32_t* out24);
 int llvq_encode_host(const llvq_codebook* cb, const int32_t* codeword24, int64_t* index);
+
+/* Integer codewords [n,24] of indices [n] on the host, decoded with the same
+ * tables and code as the GPU kernels' table-driven decoder (the entry point
+ * its CPU tests use).  Needs a codebook with tables (llvq_codebook_tables);
+ * out-of-range indices give zero rows and are counted in *bad (may be NULL).
+ * Host counterpart of dequantize_lattice_cuda (impl/llvq_cuda_dequantize.py:
+ * 221-261); the reference's CPU codeword() is impl/leech_lattice_vector_quantizer.py:235-245. */
+int llvq_codeword_batch_host(const llvq_codebook* cb, const int64_t* indices, int64_t n, int32_t* out, int64_t* bad);
+/* Whether the codebook's decoder is table-driven (1) or unranks arithmetically
+ * (0: parts too large to tabulate), the tables' size in bytes and the most
+ * table lookups one index takes.  No reference counterpart. */
+int llvq_codebook_tables(const llvq_codebook* cb, int32_t* tabulated, int64_t* table_bytes, int32_t* max_lookups);
 
 const char* llvq_status_string(int status);
 const char* llvq_last_error(void);

@@ -36,7 +36,7 @@ EXPORTS = (
     "llvq_dequantize_lattice", "llvq_dequantize", "llvq_dequantize_bf16", "llvq_codeword_host",
     "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version", "llvq_gemm",
     "llvq_hadamard", "llvq_gemm_noalloc", "llvq_pack_indices", "llvq_unpack_indices", "llvq_dequantize_packed",
-    "llvq_gemm_packed", "llvq_hadamard_ex",
+    "llvq_gemm_packed", "llvq_hadamard_ex", "llvq_codeword_batch_host", "llvq_codebook_tables",
 )
 
 _lib = None
@@ -73,6 +73,8 @@ def load() -> ctypes.CDLL:
             "llvq_dequantize_packed": (ctypes.c_int, [vp, vp, i32, i64, vp, i32, vp, i64, vp, vp]),
             "llvq_gemm_packed": (ctypes.c_int, [vp, vp, i32, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_codeword_host": (ctypes.c_int, [vp, i64, vp]),
+            "llvq_codeword_batch_host": (ctypes.c_int, [vp, vp, i64, vp, P(i64)]),
+            "llvq_codebook_tables": (ctypes.c_int, [vp, P(i32), P(i64), P(i32)]),
             "llvq_encode_host": (ctypes.c_int, [vp, vp, P(i64)]),
             "llvq_status_string": (ctypes.c_char_p, [ctypes.c_int]),
             "llvq_last_error": (ctypes.c_char_p, []),
@@ -142,6 +144,24 @@ class NativeCodebook:
         out = (ctypes.c_int32 * 24)()
         check(self._lib.llvq_codeword_host(self.handle, int(index), out), "llvq_codeword_host")
         return tuple(out)
+
+    def codeword_batch(self, indices) -> tuple[np.ndarray, int]:
+        """Integer codewords [n, 24] of int64 indices on the host with the
+        table-driven decoder the kernels use; (codewords, count out of range)."""
+        idx = np.ascontiguousarray(indices, dtype=np.int64).reshape(-1)
+        out = np.zeros((idx.shape[0], 24), dtype=np.int32)
+        bad = ctypes.c_int64()
+        check(self._lib.llvq_codeword_batch_host(self.handle, idx.ctypes.data, idx.shape[0], out.ctypes.data,
+                                                 ctypes.byref(bad)), "llvq_codeword_batch_host")
+        return out, bad.value
+
+    def tables(self) -> dict:
+        """Whether the decoder is table-driven, its table bytes and the most
+        lookups one index takes."""
+        tab, nbytes, jobs = ctypes.c_int32(), ctypes.c_int64(), ctypes.c_int32()
+        check(self._lib.llvq_codebook_tables(self.handle, ctypes.byref(tab), ctypes.byref(nbytes),
+                                             ctypes.byref(jobs)), "llvq_codebook_tables")
+        return {"tabulated": bool(tab.value), "bytes": nbytes.value, "max_lookups": jobs.value}
 
     def encode(self, vector: Sequence[int]) -> int:
         v = (ctypes.c_int32 * 24)(*[int(a) for a in vector])
@@ -215,6 +235,43 @@ def hadamard(in_ptr: int, in_is_half: bool, out_ptr: int, rows: int, cols: int, 
 
 
 _CACHE: dict = {}
+
+
+class MetadataBooks:
+    """Codebooks of the reference's metadata dicts, for the launcher shims.
+
+    The dicts hold device tensors; reading them back to build a content key
+    would synchronise the host on every launch, which the reference's
+    launchers never do.  An entry is therefore reused only while every
+    tensor it was built from is the very same live object, unmodified
+    (same ``_version``): a new dict whose tensors happen to reuse freed
+    device memory at the same addresses gets its own codebook, and the
+    codebook itself is shared by content through ``codebook_for``."""
+
+    def __init__(self, keys: Sequence[str], classes_from_meta):
+        self._keys = tuple(keys)
+        self._classes = classes_from_meta
+        self._entries: dict = {}
+        self._mu = threading.Lock()
+
+    def get(self, meta: dict, device: int) -> "NativeCodebook":
+        import weakref
+
+        tensors = [meta[k] for k in self._keys]
+        key = (tuple(t.data_ptr() for t in tensors), int(device))
+        with self._mu:
+            hit = self._entries.get(key)
+            if hit is not None:
+                refs, versions, book = hit
+                if all(r() is t for r, t in zip(refs, tensors)) and \
+                        all(v == t._version for v, t in zip(versions, tensors)):
+                    return book
+        shell, parity, leaders = self._classes(meta)
+        book = codebook_for(shell, parity, leaders, device)
+        with self._mu:
+            self._entries = {k: e for k, e in self._entries.items() if all(r() is not None for r in e[0])}
+            self._entries[key] = ([weakref.ref(t) for t in tensors], [t._version for t in tensors], book)
+        return book
 
 
 def codebook_for(shells, parities, leaders, device: int) -> NativeCodebook:

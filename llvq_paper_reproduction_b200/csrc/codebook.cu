@@ -18,6 +18,7 @@
 #include "../../include/llvq_b200.h"
 #include "llvq_device.cuh"
 #include "llvq_internal.h"
+#include "llvq_tables.cuh"
 
 struct llvq_codebook {
   llvq::Codebook cb;
@@ -389,7 +390,22 @@ int upload(llvq::Codebook& cb, int device) {
   const size_t o_plex = off; off = align256(off + (kNumGolay / 2) * sizeof(uint16_t));
   const size_t o_toff = off; off = align256(off + kTailKeys * sizeof(uint32_t));
   const size_t o_tseq = off; off = align256(off + kTailSeqs * sizeof(uint16_t));
+  const TabHost& tb = cb.tab;
+  const size_t o_tstate = off; off = align256(off + tb.state.size() * sizeof(uint4));
+  const size_t o_tentry = off; off = align256(off + tb.entry.size() * sizeof(uint4));
+  const size_t o_tguide = off; off = align256(off + tb.guide.size() * sizeof(uint16_t));
+  const size_t o_ttail = off; off = align256(off + tb.tail.size() * sizeof(unsigned long long));
+  const size_t o_tcls = off; off = align256(off + tb.cls.size() * sizeof(uint2));
+  const size_t o_texp = off; off = align256(off + tb.expand.size() * sizeof(uint32_t));
   std::vector<unsigned char> host(off, 0);
+  if (tb.ok) {
+    std::memcpy(host.data() + o_tstate, tb.state.data(), tb.state.size() * sizeof(uint4));
+    std::memcpy(host.data() + o_tentry, tb.entry.data(), tb.entry.size() * sizeof(uint4));
+    std::memcpy(host.data() + o_tguide, tb.guide.data(), tb.guide.size() * sizeof(uint16_t));
+    std::memcpy(host.data() + o_ttail, tb.tail.data(), tb.tail.size() * sizeof(unsigned long long));
+    std::memcpy(host.data() + o_tcls, tb.cls.data(), tb.cls.size() * sizeof(uint2));
+    std::memcpy(host.data() + o_texp, tb.expand.data(), tb.expand.size() * sizeof(uint32_t));
+  }
   {
     std::vector<DecodeClass> dc(n);
     for (size_t k = 0; k < n; ++k) {
@@ -471,6 +487,16 @@ int upload(llvq::Codebook& cb, int device) {
   d.plist_lex = reinterpret_cast<const uint16_t*>(base + o_plex);
   d.tail_off = reinterpret_cast<const uint32_t*>(base + o_toff);
   d.tail_seq = reinterpret_cast<const uint16_t*>(base + o_tseq);
+  d.tab = TabView{};
+  if (tb.ok) {
+    d.tab.state = reinterpret_cast<const uint4*>(base + o_tstate);
+    d.tab.entry = reinterpret_cast<const uint4*>(base + o_tentry);
+    d.tab.guide = reinterpret_cast<const uint16_t*>(base + o_tguide);
+    d.tab.tail = reinterpret_cast<const unsigned long long*>(base + o_ttail);
+    d.tab.cls = reinterpret_cast<const uint2*>(base + o_tcls);
+    d.tab.expand = reinterpret_cast<const uint4*>(base + o_texp);
+    d.tab.max_jobs = tb.max_jobs;
+  }
   std::copy(cb.weight_start, cb.weight_start + 25, d.weight_start);
   d.n_classes = (int32_t)n;
   d.min_shell = cb.min_shell;
@@ -510,6 +536,8 @@ int llvq_codebook_create(int32_t n_classes, const int32_t* shell, const int32_t*
   llvq_codebook* h = new (std::nothrow) llvq_codebook();
   if (!h) return fail(LLVQ_ERR_OUT_OF_MEMORY, "codebook");
   int st = build(h->cb, n_classes, shell, parity, leader);
+  if (st == LLVQ_OK && !llvq::build_decode_tables(h->cb, h->cb.tab, &h->cb.tab_why) && h->cb.tab_why.empty())
+    h->cb.tab_why = "tables not built";
   if (st == LLVQ_OK && device >= 0) st = upload(h->cb, device);
   if (st != LLVQ_OK) {
     delete h;
@@ -529,6 +557,28 @@ void llvq_codebook_destroy(llvq_codebook* h) {
     if (prev != h->cb.device && prev >= 0) cudaSetDevice(prev);
   }
   delete h;
+}
+
+int llvq_codeword_batch_host(const llvq_codebook* h, const int64_t* indices, int64_t n, int32_t* out, int64_t* bad) {
+  if (!h) return fail(LLVQ_ERR_INVALID_ARGUMENT, "null codebook");
+  if (n < 0 || (n > 0 && (!indices || !out))) return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad codeword arguments");
+  if (!h->cb.tab.ok) return fail(LLVQ_ERR_UNSUPPORTED, "codebook has no decoder tables: " + h->cb.tab_why);
+  int64_t nbad = 0;
+  for (int64_t i = 0; i < n; ++i)
+    if (!llvq::decode_index_tables_host(h->cb, indices[i], out + i * llvq::kDim)) ++nbad;
+  if (bad) *bad = nbad;
+  return LLVQ_OK;
+}
+
+int llvq_codebook_tables(const llvq_codebook* h, int32_t* tabulated, int64_t* table_bytes, int32_t* max_lookups) {
+  if (!h) return fail(LLVQ_ERR_INVALID_ARGUMENT, "null codebook");
+  const llvq::TabHost& t = h->cb.tab;
+  if (tabulated) *tabulated = t.ok ? 1 : 0;
+  if (table_bytes)
+    *table_bytes = (int64_t)(t.state.size() * 16 + t.entry.size() * 16 + t.guide.size() * 2 + t.tail.size() * 8 +
+                             t.cls.size() * 8 + t.expand.size() * 4);
+  if (max_lookups) *max_lookups = t.max_jobs;
+  return LLVQ_OK;
 }
 
 int llvq_codebook_info(const llvq_codebook* h, int64_t* total_count, int32_t* n_classes, int32_t* min_shell,
@@ -689,17 +739,17 @@ int llvq_gemm_noalloc(const llvq_codebook* h, const int64_t* indices, int64_t n_
                       int32_t* error_flag, void* stream) {
   if (m < 0 || n_out < 0 || blocks_per_row <= 0 || k <= 0 || k % 8 || k > 24 * blocks_per_row)
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes: need k % 8 == 0 and 0 < k <= 24 * blocks_per_row");
-  if (blocks_per_row > LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW)
+  if (m > llvq::kGemvMaxM && blocks_per_row > LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW)
     return fail(LLVQ_ERR_INVALID_ARGUMENT,
                 "gemm_noalloc: blocks_per_row > 2730 (rows wider than 65536 columns) does not fit the 16 MiB "
-                "static staging buffer; use llvq_gemm");
+                "static staging buffer when m > 4; use llvq_gemm");
   if (m > 0 && n_out > 0 && (!indices || !a_bf16 || !y || (reinterpret_cast<uintptr_t>(a_bf16) & 15)))
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm pointers: null, or activations not 16-byte aligned");
   if (m > (int64_t)INT32_MAX || n_out > (int64_t)INT32_MAX)
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gemm shapes exceed 32-bit extents");
   return on_device(h, [&] {  // setup runs even for empty shapes, so a first empty call prepares the device
     void* staging = nullptr;
-    cudaError_t e = llvq::noalloc_staging(&staging);  // first call on a device: symbol lookup
+    cudaError_t e = llvq::noalloc_staging(&staging);  // first call on a device: loads the array's module
     if (e != cudaSuccess) return e;
     return llvq::gemm_staged_launch(h->cb, {indices, 8}, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
                                     error_flag, staging, llvq::kNoAllocStagingBytes, (cudaStream_t)stream);

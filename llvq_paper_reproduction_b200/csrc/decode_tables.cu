@@ -1,0 +1,358 @@
+// Host builder of the table-driven decoder's tables (llvq_tables.cuh) and the
+// host batch decoder that uses them.
+//
+// States are count vectors of a class part's values still to place (value
+// index j = the j-th largest value of the part, the order in which the
+// reference's multiset rank tries values, impl/leech_lattice_vector_quantizer.py
+// :870-889).  From every class part's full multiset the builder walks the
+// states the decoder can reach: a state with at most kTabTail positions left
+// becomes a tail (all its orderings, in rank order); a larger one a search
+// over its next h = min(kTabHead, positions - kTabTail) positions (every
+// h-prefix in rank order with the rank where its completions start and the
+// state it leaves), with a guide table.  States are keyed by their counts
+// alone, so classes with equal part multisets share them.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "llvq_internal.h"
+#include "llvq_tables.cuh"
+
+namespace llvq {
+
+namespace {
+
+using u128 = unsigned __int128;
+
+constexpr int kTabMaxVals = 8;                    // value indices must fit a byte-permute selector
+constexpr size_t kTabMaxEntries = 1u << 24;       // search entries (16 B each)
+constexpr size_t kTabMaxTail = 3u << 23;          // tail entries (8 B each): at most 192 MiB
+constexpr uint32_t kTabMaxStateEntries = 1u << 16;  // guide slots hold 16-bit entry numbers
+
+u128 multinomial_counts(const int* c) {
+  u128 out = 1;
+  int rem = 0;
+  for (int j = 0; j < kTabMaxVals; ++j) {
+    for (int k = 1; k <= c[j]; ++k) {
+      ++rem;
+      out = out * (u128)rem / (u128)k;
+    }
+  }
+  return out;
+}
+
+uint64_t pack_counts(const int* c) {
+  uint64_t k = 0;
+  for (int j = 0; j < kTabMaxVals; ++j) k |= (uint64_t)c[j] << (5 * j);
+  return k;
+}
+
+void unpack_counts(uint64_t k, int* c) {
+  for (int j = 0; j < kTabMaxVals; ++j) c[j] = (int)((k >> (5 * j)) & 31u);
+}
+
+struct Builder {
+  TabHost& t;
+  std::unordered_map<uint64_t, uint32_t> ids;
+  std::vector<uint64_t> keys;
+  std::vector<int> depth;  // lookups from a state to the end of its part
+  std::string why;
+
+  explicit Builder(TabHost& tab) : t(tab) {}
+
+  uint32_t get(const int* c) {
+    const uint64_t key = pack_counts(c);
+    auto it = ids.find(key);
+    if (it != ids.end()) return it->second;
+    const uint32_t id = (uint32_t)keys.size();
+    ids.emplace(key, id);
+    keys.push_back(key);
+    return id;
+  }
+
+  // Every ordering of the remaining counts, in rank order (value index
+  // ascending at each position), as nibble strings.
+  void tail_state(int* c, int rem, uint64_t prefix, int pos, std::vector<unsigned long long>& out) {
+    if (pos == rem) {
+      out.push_back(prefix);
+      return;
+    }
+    for (int j = 0; j < kTabMaxVals; ++j) {
+      if (!c[j]) continue;
+      --c[j];
+      tail_state(c, rem, prefix | ((uint64_t)j << (4 * pos)), pos + 1, out);
+      ++c[j];
+    }
+  }
+
+  struct Prefix {
+    u128 start;
+    uint32_t next;
+    uint32_t nib;
+  };
+
+  void search_state(int* c, int h, int pos, uint32_t nib, u128& cursor, std::vector<Prefix>& out) {
+    if (pos == h) {
+      const uint32_t nx = get(c);
+      out.push_back({cursor, nx, nib});
+      cursor += multinomial_counts(c);
+      return;
+    }
+    for (int j = 0; j < kTabMaxVals; ++j) {
+      if (!c[j]) continue;
+      --c[j];
+      search_state(c, h, pos + 1, nib | ((uint32_t)j << (4 * pos)), cursor, out);
+      ++c[j];
+    }
+  }
+
+  bool run() {
+    // states are processed in creation order; children are created while
+    // their parent is processed, so the vector grows behind the cursor
+    for (size_t s = 0; s < keys.size(); ++s) {
+      int c[kTabMaxVals];
+      unpack_counts(keys[s], c);
+      int rem = 0;
+      for (int j = 0; j < kTabMaxVals; ++j) rem += c[j];
+      const u128 n = multinomial_counts(c);
+      if (n >> 58) return fail("a part has 2^58 or more orderings");
+      uint4 rec{0, 0, 0, 0};
+      if (rem <= kTabTail) {
+        if (t.tail.size() + (size_t)n > kTabMaxTail) return fail("tail tables too large");
+        rec.x = (uint32_t)t.tail.size();
+        rec.w = kTabTailBit | (uint32_t)rem;
+        tail_state(c, rem, 0, 0, t.tail);
+      } else {
+        const int h = std::min(kTabHead, rem - kTabTail);
+        std::vector<Prefix> pre;
+        u128 cursor = 0;
+        search_state(c, h, 0, 0, cursor, pre);
+        if (cursor != n) return fail("prefix counts do not add up");
+        if (pre.size() > kTabMaxStateEntries) return fail("a search state has too many prefixes");
+        if (t.entry.size() + pre.size() > kTabMaxEntries) return fail("search tables too large");
+        int lg = 0;
+        while ((1u << lg) < 2 * pre.size()) ++lg;
+        const uint32_t slots = 1u << lg;
+        rec.x = (uint32_t)t.entry.size();
+        rec.y = (uint32_t)t.guide.size();
+        const float gn = (float)((double)slots / (double)(uint64_t)n);
+        std::memcpy(&rec.z, &gn, 4);
+        rec.w = (uint32_t)pre.size() | ((uint32_t)lg << 17) | ((uint32_t)h << 22);
+        for (const Prefix& p : pre)
+          t.entry.push_back({(uint32_t)(uint64_t)p.start, (uint32_t)((uint64_t)p.start >> 32), p.next, p.nib});
+        size_t j = 0;
+        for (uint32_t g = 0; g < slots; ++g) {
+          u128 lo = ((u128)g * n + slots - 1) / slots;  // ceil(g N / G)
+          if (lo >= n) lo = n - 1;
+          while (j + 1 < pre.size() && pre[j + 1].start <= lo) ++j;
+          t.guide.push_back((uint16_t)j);
+        }
+      }
+      t.state.push_back(rec);
+    }
+    // lookups to the end of a part from each state (children come later in
+    // creation order, so walk backwards)
+    depth.assign(keys.size(), 1);
+    for (size_t s = keys.size(); s-- > 0;) {
+      const uint4& rec = t.state[s];
+      if (rec.w & kTabTailBit) continue;
+      int d = 0;
+      for (uint32_t e = 0; e < (rec.w & 0x1FFFFu); ++e) d = std::max(d, depth[t.entry[rec.x + e].z]);
+      depth[s] = 1 + d;
+    }
+    return true;
+  }
+
+  bool fail(const char* msg) {
+    why = msg;
+    return false;
+  }
+};
+
+// Move masks of the bit-wise expand by mask m (Hacker's Delight, section 7-5,
+// the inverse of compress): stage i moves the bits marked in mv[i] left by
+// 2^i positions, applied for i = 4 down to 0.
+void expand_masks(uint32_t m, uint32_t mv[5]) {
+  uint32_t mk = ~m << 1;
+  for (int i = 0; i < 5; ++i) {
+    uint32_t mp = mk ^ (mk << 1);
+    mp ^= mp << 2;
+    mp ^= mp << 4;
+    mp ^= mp << 8;
+    mp ^= mp << 16;
+    const uint32_t v = mp & m;
+    mv[i] = v;
+    m = (m ^ v) | (v >> (1 << i));
+    mk &= ~mp;
+  }
+}
+
+// Each of the 24 mask bits widened to a nibble, as three u32.
+void nibble_spread(uint32_t m, uint32_t* out) {
+  for (int k = 0; k < 3; ++k) {
+    uint32_t v = 0;
+    for (int i = 0; i < 8; ++i)
+      if ((m >> (8 * k + i)) & 1u) v |= 0xFu << (4 * i);
+    out[k] = v;
+  }
+}
+
+bool build_expand(const std::vector<uint32_t>& golay, std::vector<uint32_t>& out, std::string& why) {
+  out.assign((size_t)kNumGolay * kTabExpandWords, 0);
+  uint32_t seed = 12345u;
+  for (int gi = 0; gi < kNumGolay; ++gi) {
+    uint32_t* e = out.data() + (size_t)gi * kTabExpandWords;
+    const uint32_t w = golay[gi];
+    for (int part = 0; part < 2; ++part) {
+      uint32_t mv[5];
+      expand_masks(part ? (~w & kFull24) : w, mv);
+      for (int i = 0; i < 5; ++i) nibble_spread(mv[i], e + 15 * part + 3 * i);
+    }
+    nibble_spread(w, e + 30);
+    // self-check: random nibble strings (garbage beyond each part's length)
+    // land on the right positions
+    for (int trial = 0; trial < 4; ++trial) {
+      uint32_t xa[3], xb[3], want_a[24], want_b[24];
+      int ia = 0, ib = 0;
+      for (int k = 0; k < 3; ++k) {
+        seed = seed * 1664525u + 1013904223u;
+        xa[k] = seed;
+        seed = seed * 1664525u + 1013904223u;
+        xb[k] = seed;
+      }
+      auto nib = [](const uint32_t* x, int t) { return (x[t / 8] >> (4 * (t % 8))) & 15u; };
+      for (int d = 0; d < kDim; ++d) {
+        if ((w >> d) & 1u) want_a[d] = nib(xa, ia++);
+        else want_b[d] = nib(xb, ib++);
+      }
+      tab_expand(xa, e);
+      tab_expand(xb, e + 15);
+      for (int d = 0; d < kDim; ++d) {
+        const uint32_t got = ((w >> d) & 1u) ? nib(xa, d) : nib(xb, d);
+        if (got != (((w >> d) & 1u) ? want_a[d] : want_b[d])) {
+          why = "expand self-check failed";
+          return false;
+        }
+      }
+    }
+  }
+  return true;
+}
+
+}  // namespace
+
+bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
+  t = TabHost{};
+  Builder b(t);
+  auto bad = [&](const std::string& msg) {
+    t = TabHost{};
+    if (why_out) *why_out = msg;
+    return false;
+  };
+  const size_t n = cb.cls.size();
+  t.cls.resize(n);
+  std::vector<int> jobs(n, 0);
+  for (size_t k = 0; k < n; ++k) {
+    const DevClass& c = cb.cls[k];
+    if (c.nv0 + c.nv1 > kTabMaxVals) return bad("a class has more than 8 distinct magnitudes");
+    int a[kTabMaxVals] = {0}, z[kTabMaxVals] = {0};
+    if (c.parity) {
+      for (int j = 0; j < c.nv0; ++j) a[j] = c.m0[j];
+      t.cls[k] = make_uint2(b.get(a), kTabEnd);
+    } else {
+      for (int j = 0; j < c.nv1; ++j) a[j] = c.m1[j];
+      for (int j = 0; j < c.nv0; ++j) z[j] = c.m0[j];
+      t.cls[k] = make_uint2(c.even_weight > 0 ? b.get(a) : kTabEnd, c.even_weight < kDim ? b.get(z) : kTabEnd);
+    }
+  }
+  if (!b.run()) return bad(b.why);
+  for (size_t k = 0; k < n; ++k) {
+    const uint2 s = t.cls[k];
+    jobs[k] = (s.x != kTabEnd ? b.depth[s.x] : 0) + (s.y != kTabEnd ? b.depth[s.y] : 0);
+    t.max_jobs = std::max(t.max_jobs, jobs[k]);
+  }
+  std::string why;
+  if (!build_expand(cb.golay, t.expand, why)) return bad(why);
+  t.ok = true;
+  return true;
+}
+
+namespace {
+
+// deposit4[m * 16 + s]: the low popc(m) bits of s placed on the set bits of m.
+const uint8_t* host_deposit4() {
+  static uint8_t table[256];
+  static bool ready = false;
+  if (!ready) {
+    for (int i = 0; i < 256; ++i) {
+      const uint32_t m = i >> 4;
+      uint32_t src = i & 15, dep = 0;
+      for (int bit = 0; bit < 4; ++bit)
+        if ((m >> bit) & 1u) {
+          dep |= (src & 1u) << bit;
+          src >>= 1;
+        }
+      table[i] = (uint8_t)dep;
+    }
+    ready = true;
+  }
+  return table;
+}
+
+}  // namespace
+
+// Host decode of one index with the tables (the same tab_* code the kernels
+// run); false and zeros outside the codebook or for a bad sign rank.
+bool decode_index_tables_host(const Codebook& cb, int64_t v, int32_t* out) {
+  const TabHost& t = cb.tab;
+  for (int d = 0; d < kDim; ++d) out[d] = 0;
+  if (!t.ok || v < 0 || v >= cb.total) return false;
+  const int k = find_class(cb.class_start.data(), (int)cb.cls.size(), v);
+  const DevClass& c = cb.cls[k];
+  const uint64_t local = (uint64_t)(v - c.start);
+  const uint64_t prank = local % c.perm_count, cur = local / c.perm_count;
+  TabView tv{};
+  tv.state = t.state.data();
+  tv.entry = t.entry.data();
+  tv.guide = t.guide.data();
+  tv.tail = t.tail.data();
+  tv.cls = t.cls.data();
+  tv.expand = reinterpret_cast<const uint4*>(t.expand.data());
+  tv.max_jobs = t.max_jobs;
+  const uint2 st = t.cls[k];
+  uint64_t vals = 0;
+  uint32_t word;
+  int word_lex, d0;
+  uint64_t sign = 0, ra, rb;
+  if (c.parity) {
+    word = cb.golay[cur];
+    word_lex = kNumGolay - 1;
+    d0 = 0;
+    ra = prank;
+    rb = 0;
+    for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
+  } else {
+    sign = cur & (c.sign_count - 1);
+    const uint64_t g = cur >> c.sign_shift;
+    word_lex = cb.by_weight[cb.weight_start[c.even_weight] + (int)g];
+    word = cb.golay[word_lex];
+    d0 = c.nv0;
+    ra = prank % c.f1_perm;
+    rb = prank / c.f1_perm;
+    for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
+    for (int j = 0; j < c.nv1; ++j) vals |= (uint64_t)(uint8_t)c.v1[j] << (8 * (d0 + j));
+  }
+  uint32_t mag[6];
+  tab_magnitudes(tv, st.x, ra, st.y, rb, word_lex, d0, vals, mag);
+  int y[kDim];
+  if (!tab_signs(mag, word, c.parity != 0, sign, c.required, host_deposit4(), y)) return false;
+  for (int d = 0; d < kDim; ++d) out[d] = y[d];
+  return true;
+}
+
+}  // namespace llvq

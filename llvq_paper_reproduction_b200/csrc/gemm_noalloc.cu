@@ -24,28 +24,31 @@ namespace llvq {
 
 static __device__ __align__(256) unsigned char g_gemm_staging[kNoAllocStagingBytes];
 
-// Address of this device's staging array, looked up with cudaGetSymbolAddress
-// once per device (the current device at the time of the call) and cached.
-// The same first call also sets the GEMM kernels' shared-memory limits on
-// that device.
+// Address of this device's staging array (the current device at the time
+// of the call).  cudaGetSymbolAddress runs on every call: once the module is
+// loaded it is a host-side lookup, and a cached address could go stale if the
+// caller resets the device (the module, and with it the array, is then loaded
+// again, possibly elsewhere).  The first call on a device loads the module
+// that holds the array -- this is when the CUDA runtime allocates its 16 MiB
+// -- and sets the GEMM kernels' shared-memory limits on that device.
 cudaError_t noalloc_staging(void** ptr) {
   static std::mutex mu;
-  static void* cached[kMaxDevices] = {};
+  static bool configured[kMaxDevices] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_gemm_staging);
+  if (e != cudaSuccess) return e;
+  if (!p) return cudaErrorInvalidSymbol;
   std::lock_guard<std::mutex> lock(mu);
-  if (!cached[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_gemm_staging);
-    if (e != cudaSuccess) return e;
-    if (!p) return cudaErrorInvalidSymbol;
+  if (!configured[dev]) {
     e = gemm_configure_device();
     if (e != cudaSuccess) return e;
-    cached[dev] = p;
+    configured[dev] = true;
   }
-  *ptr = cached[dev];
+  *ptr = p;
   return cudaSuccess;
 }
 

@@ -88,6 +88,17 @@ constexpr int kTailLen = 8;
 constexpr int kTailKeys = 9 * 9 * 9;
 constexpr int kTailSeqs = 1 << (2 * kTailLen);
 
+// Tables of the table-driven decoder (layout in llvq_tables.cuh).
+struct TabView {
+  const uint4* state;
+  const uint4* entry;
+  const uint16_t* guide;
+  const unsigned long long* tail;
+  const uint2* cls;        // per class: {state of part A, state of part B}
+  const uint4* expand;     // per Golay word (lexicographic index): kTabExpandWords u32
+  int max_jobs;            // lookups of the longest class (both parts)
+};
+
 // Everything a kernel needs about one codebook (plain pointers, passed by value).
 struct DevBook {
   const DevClass* cls;
@@ -109,6 +120,9 @@ struct DevBook {
   int64_t total;
   // window constants of the active scoring code (see quantize.cu)
   float l1max, win_mg, win_am;
+  // table-driven decoder (llvq_tables.cuh); state == nullptr when the
+  // codebook is not tabulated
+  TabView tab;
 };
 
 // ---------------------------------------------------------------- integers

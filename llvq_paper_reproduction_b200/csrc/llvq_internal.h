@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <string>
 #include <vector>
 
 #include "llvq_device.cuh"
@@ -21,6 +22,19 @@ struct SpecEntry {
   SearchLauncher launch;
   const char* name;
   float l1max, win_mg, win_am;
+};
+
+// Host copy of the table-driven decoder's tables (llvq_tables.cuh; built by
+// decode_tables.cu).  ok is false when the codebook's parts are too large to
+// tabulate; the kernels then unrank arithmetically (llvq_decode.cuh).
+struct TabHost {
+  bool ok = false;
+  std::vector<uint4> state, entry;
+  std::vector<uint16_t> guide;
+  std::vector<unsigned long long> tail;
+  std::vector<uint2> cls;
+  std::vector<uint32_t> expand;
+  int max_jobs = 0;
 };
 
 struct Codebook {
@@ -42,7 +56,14 @@ struct Codebook {
   size_t dev_bytes = 0;
   const SpecEntry* spec = nullptr;     // generated search code for this class list, or null
   float rt_l1max = 0, rt_mg = 0, rt_am = 0;  // window constants of the table-driven chains
+  TabHost tab;                         // table-driven decoder (host copy)
+  std::string tab_why;                 // why the tables are off, when they are
 };
+
+// Build the table-driven decoder's tables of a codebook (false: not
+// tabulable, with the reason); decode one index on the host with them.
+bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why);
+bool decode_index_tables_host(const Codebook& cb, int64_t v, int32_t* out);
 
 const SpecEntry* spec_table(int* count);
 

@@ -16,7 +16,6 @@ import torch
 
 from . import _native
 
-_BOOKS: dict = {}
 
 
 def classes_from_codeword_meta(meta: dict) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
@@ -43,15 +42,13 @@ def classes_from_codeword_meta(meta: dict) -> tuple[np.ndarray, np.ndarray, np.n
     return shells, parity, leaders
 
 
+# Every metadata tensor the class list is read from (see classes_from_codeword_meta).
+_BOOKS = _native.MetadataBooks(("parity", "f0_counts", "f0_values", "f1_counts", "f1_values", "odd_counts",
+                                "odd_values"), classes_from_codeword_meta)
+
+
 def _book_for(meta: dict, device: torch.device) -> _native.NativeCodebook:
-    t = meta["parity"]
-    key = (t.data_ptr(), t.numel(), meta["class_starts"].data_ptr(), device.index)
-    book = _BOOKS.get(key)
-    if book is None:
-        shell, parity, leaders = classes_from_codeword_meta(meta)
-        book = _native.codebook_for(shell, parity, leaders, device.index)
-        _BOOKS[key] = book
-    return book
+    return _BOOKS.get(meta, device.index)
 
 
 def dequantize_lattice_cuda(indices: torch.Tensor, out: torch.Tensor, meta: dict, comb: torch.Tensor) -> torch.Tensor:

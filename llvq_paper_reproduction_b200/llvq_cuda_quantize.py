@@ -16,7 +16,6 @@ import torch
 
 from . import _native
 
-_BOOKS: dict = {}
 
 
 def classes_from_quantize_meta(meta: dict) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
@@ -41,15 +40,13 @@ def classes_from_quantize_meta(meta: dict) -> tuple[np.ndarray, np.ndarray, np.n
     return shell, parity, leaders
 
 
+# Every metadata tensor the class list is read from (see classes_from_quantize_meta).
+_BOOKS = _native.MetadataBooks(("class_parity", "class_shell", "class_f0_mags", "class_f1_mags", "class_f0_len",
+                                "class_f1_len", "class_odd_leaders"), classes_from_quantize_meta)
+
+
 def _book_for(meta: dict, device: torch.device) -> _native.NativeCodebook:
-    t = meta["class_parity"]
-    key = (t.data_ptr(), t.numel(), meta["class_odd_leaders"].data_ptr(), device.index)
-    book = _BOOKS.get(key)
-    if book is None:
-        shell, parity, leaders = classes_from_quantize_meta(meta)
-        book = _native.codebook_for(shell, parity, leaders, device.index)
-        _BOOKS[key] = book
-    return book
+    return _BOOKS.get(meta, device.index)
 
 
 def quantize_lattice_cuda(x: torch.Tensor, indices: torch.Tensor, best_pair: torch.Tensor, best_score: torch.Tensor,

@@ -18,8 +18,8 @@ Sharding: matrices are independent, so ranks own whole matrices (greedy
 balance of block counts), quantize them with no inter-GPU traffic,
 checkpoint each finished matrix (atomic write; a restart skips finished
 ones), and finally gather every index tensor (packed to 6 bytes per block)
-and row scale to rank 0 with one all-gather over the process group (NCCL on
-GPUs, gloo in CPU tests).
+and row scale to rank 0 over the process group (NCCL on GPUs, gloo in CPU
+tests).
 """
 from __future__ import annotations
 
@@ -147,31 +147,53 @@ class MatrixQuantizer:
 
 
 def _save_atomic(path: Path, obj) -> None:
+    """Write to a temporary file, flush it to disk, then rename over `path`,
+    so a crash leaves either the old file or the complete new one."""
     tmp = path.with_suffix(path.suffix + f".tmp{os.getpid()}")
-    torch.save(obj, tmp)
+    with open(tmp, "wb") as fh:
+        torch.save(obj, fh)
+        fh.flush()
+        os.fsync(fh.fileno())
     tmp.replace(path)
 
 
+def _checkpoint_meta(spec: MatrixSpec, fingerprint: dict | None) -> dict:
+    return {"key": spec.key, "out_features": spec.out_features, "in_features": spec.in_features,
+            "blocks_per_row": spec.blocks_per_row, **(fingerprint or {})}
+
+
 def run_shard(specs: Sequence[MatrixSpec], rank: int, world: int, out_dir: Path,
-              quantize_fn: Callable[[MatrixSpec], dict], log: Callable[[str], None] = lambda s: None) -> dict:
+              quantize_fn: Callable[[MatrixSpec], dict], log: Callable[[str], None] = lambda s: None,
+              fingerprint: dict | None = None) -> dict:
     """Quantize this rank's matrices (skipping finished checkpoints) and
-    return {key: (indices, row_scale)} on CPU."""
+    return {key: (indices, row_scale)} on CPU.  A checkpoint is reused only
+    when it loads, carries the same matrix shape and the same `fingerprint`
+    (the settings that determine its contents, e.g. rate and seed), and holds
+    tensors of the expected shapes; anything else is quantized again."""
     out_dir.mkdir(parents=True, exist_ok=True)
     mine = plan_shards(specs, world)[rank]
     done = {}
     for i in mine:
         spec = specs[i]
         path = out_dir / f"{spec.key}.pt"
+        meta = _checkpoint_meta(spec, fingerprint)
         res = None
         if path.exists():
             try:
                 res = torch.load(path, map_location="cpu")
-                log(f"rank {rank}: resumed {spec.key}")
+                ok = (res.get("meta") == meta
+                      and tuple(res["indices"].shape) == (spec.out_features, spec.blocks_per_row)
+                      and tuple(res["row_scale"].shape) == (spec.out_features,))
+                if ok:
+                    log(f"rank {rank}: resumed {spec.key}")
+                else:
+                    log(f"rank {rank}: stale checkpoint {spec.key}, quantizing again")
+                    res = None
             except Exception:
                 res = None
         if res is None:
             r = quantize_fn(spec)
-            res = {"indices": r["indices"].cpu(), "row_scale": r["row_scale"].cpu()}
+            res = {"indices": r["indices"].cpu(), "row_scale": r["row_scale"].cpu(), "meta": meta}
             _save_atomic(path, res)
         done[spec.key] = (res["indices"], res["row_scale"])
     return done
@@ -193,11 +215,13 @@ def unpack_le_bytes(packed: torch.Tensor, index_bytes: int) -> torch.Tensor:
 
 def gather_to_rank0(specs: Sequence[MatrixSpec], local: dict, rank: int, world: int, device,
                     index_bytes: int = 8) -> dict | None:
-    """One all-gather of every rank's indices (as index_bytes little-endian
-    bytes each: 6 for the 48-bit shape-gain index, a quarter less than int64)
-    and row scales, flattened and padded to the largest shard, entirely on
-    `device` (indices that are already there never visit the host); rank 0
-    unpacks them per matrix into int64 tensors on `device`."""
+    """Gather every rank's indices (as index_bytes little-endian bytes each:
+    6 for the 48-bit shape-gain index, a quarter less than int64) and row
+    scales to rank 0, flattened and padded to the largest shard, entirely on
+    `device` (indices that are already there never visit the host).  Two
+    gathers to rank 0 (not all-gathers: only rank 0 keeps the result, so each
+    other rank sends its shard once and receives nothing); rank 0 unpacks
+    them per matrix into int64 tensors on `device`."""
     import torch.distributed as dist
 
     plan = plan_shards(specs, world)
@@ -214,10 +238,10 @@ def gather_to_rank0(specs: Sequence[MatrixSpec], local: dict, rank: int, world: 
         flat_idx[: cat.numel()] = pack_le_bytes(cat, index_bytes)
         cs = torch.cat(mine_sc)
         flat_sc[: cs.numel()] = cs
-    all_idx = [torch.empty_like(flat_idx) for _ in range(world)]
-    all_sc = [torch.empty_like(flat_sc) for _ in range(world)]
-    dist.all_gather(all_idx, flat_idx)
-    dist.all_gather(all_sc, flat_sc)
+    all_idx = [torch.empty_like(flat_idx) for _ in range(world)] if rank == 0 else None
+    all_sc = [torch.empty_like(flat_sc) for _ in range(world)] if rank == 0 else None
+    dist.gather(flat_idx, all_idx, dst=0)
+    dist.gather(flat_sc, all_sc, dst=0)
     if rank != 0:
         return None
     result = {}
@@ -255,7 +279,8 @@ def main():
     torch.cuda.synchronize()
     dist.barrier()
     t0 = time.perf_counter()
-    local_res = run_shard(specs, rank, world, args.out, mq.quantize)
+    local_res = run_shard(specs, rank, world, args.out, mq.quantize,
+                          fingerprint={"rate": args.rate, "seed": args.seed, "scale_down": args.scale_down})
     torch.cuda.synchronize()
     t_local = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=device)
     dist.all_reduce(t_local, op=dist.ReduceOp.MAX)

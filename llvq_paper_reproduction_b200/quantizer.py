@@ -181,19 +181,22 @@ class LeechLatticeVectorQuantizerGpu:
         (the invalid-index marker) lies above every index (6 at shells 2..13)."""
         return max(1, (self.total_count.bit_length() + 7) // 8)
 
-    def pack_indices(self, indices: torch.Tensor) -> torch.Tensor:
+    def pack_indices(self, indices: torch.Tensor, check: bool = False) -> torch.Tensor:
         """int64 indices [...] -> uint8 [..., index_bytes] little-endian; -1
-        (a NaN/Inf row) becomes all-ones.  No reference counterpart."""
+        (a NaN/Inf row) becomes all-ones.  An index that does not fit is
+        stored as all-ones and counted in the pending error flags (see
+        ``raise_pending_errors``); ``check=True`` synchronises and raises
+        IndexError at once.  No reference counterpart."""
         self._require_cuda("pack_indices")
         idx = indices.to(device=self.device, dtype=torch.long).contiguous()
         b = self.index_bytes
         out = torch.empty((*idx.shape, b), dtype=torch.uint8, device=self.device)
-        err = self._error_counter()
+        flags = self._flags()
         with torch.cuda.device(self.device):
-            _native.pack_indices(idx.data_ptr(), idx.numel(), b, out.data_ptr(), err.data_ptr(),
+            _native.pack_indices(idx.data_ptr(), idx.numel(), b, out.data_ptr(), flags[self.FLAG_RANGE].data_ptr(),
                                  torch.cuda.current_stream().cuda_stream)
-        if int(err.item()):
-            raise IndexError("index does not fit the packed width")
+        if check:
+            self.raise_pending_errors()
         return out
 
     def unpack_indices(self, packed: torch.Tensor) -> torch.Tensor:
@@ -211,10 +214,13 @@ class LeechLatticeVectorQuantizerGpu:
             raise ValueError(f"packed indices must be uint8 [..., {self.index_bytes}]")
         return packed.to(self.device).contiguous()
 
-    def dequantize_bf16(self, indices: torch.Tensor, row_scale: torch.Tensor) -> torch.Tensor:
+    def dequantize_bf16(self, indices: torch.Tensor, row_scale: torch.Tensor, check: bool = False) -> torch.Tensor:
         """bf16 weights: bf16(dequantize(indices) * row_scale[row]) for indices
         [rows, blocks_per_row] (int64, or packed uint8 [rows, blocks_per_row,
-        index_bytes]) and fp16 row_scale [rows] (no reference counterpart)."""
+        index_bytes]) and fp16 row_scale [rows] (no reference counterpart).
+        Asynchronous: an out-of-range index gives a zero block and is counted
+        in the pending error flags (``raise_pending_errors``); ``check=True``
+        synchronises and raises IndexError at once."""
         self._require_cuda("dequantize_bf16")
         packed = indices.dtype == torch.uint8
         rows_blocks = indices.shape[:-1] if packed else indices.shape
@@ -223,7 +229,7 @@ class LeechLatticeVectorQuantizerGpu:
         rows, bpr = rows_blocks
         sc = row_scale.to(self.device).contiguous()
         out = torch.empty((rows, bpr * DIM), dtype=torch.bfloat16, device=self.device)
-        err = self._error_counter()
+        err = self._flags()[self.FLAG_RANGE]
         stream = torch.cuda.current_stream(self.device).cuda_stream
         with torch.cuda.device(self.device):
             if packed:
@@ -234,11 +240,12 @@ class LeechLatticeVectorQuantizerGpu:
                 idx = indices.to(device=self.device, dtype=torch.long).contiguous()
                 self._book().dequantize_bf16(idx.data_ptr(), idx.numel(), sc.data_ptr(), bpr, out.data_ptr(),
                                              err.data_ptr(), stream)
-        self._raise_if_bad(err)
+        if check:
+            self.raise_pending_errors()
         return out
 
     def gemm(self, a: torch.Tensor, indices: torch.Tensor, row_scale: torch.Tensor | None = None,
-             rotation: tuple[int, torch.Tensor] | None = None) -> torch.Tensor:
+             rotation: tuple[int, torch.Tensor] | None = None, check: bool = False) -> torch.Tensor:
         """Dequant-GEMM: ``a @ W.T`` in fp32 for bf16 activations ``a`` [m, k]
         and a weight given by its indices [n, blocks] (int64, or packed uint8
         [n, blocks, index_bytes]; W[n] = dequantize(indices[n]).flatten()[:k]
@@ -249,8 +256,11 @@ class LeechLatticeVectorQuantizerGpu:
         pipelined tcgen05 GEMM reads.  ``rotation=(block, signs)`` first
         rotates the activations with the seeded Hadamard transform the weight
         was quantized under (int8 +-1 signs [k], block a power of two dividing
-        k), rounding them to bf16 once: x W^T = (x R)(W R)^T.  No reference
-        counterpart."""
+        k), rounding them to bf16 once: x W^T = (x R)(W R)^T.  The call is
+        asynchronous on the current stream (no host synchronisation): a
+        tensor-core wait that timed out sets the pending error flags
+        (``raise_pending_errors``); ``check=True`` synchronises and raises
+        RuntimeError at once.  No reference counterpart."""
         self._require_cuda("gemm")
         packed = indices.dtype == torch.uint8
         if a.dim() != 2 or indices.dim() != (3 if packed else 2):
@@ -275,7 +285,7 @@ class LeechLatticeVectorQuantizerGpu:
                 raise ValueError("row_scale must have one entry per weight row")
             sc = row_scale.to(device=self.device, dtype=torch.float16).contiguous()
         y = torch.empty((m, n), dtype=torch.float32, device=self.device)
-        err = self._error_counter()
+        err = self._flags()[self.FLAG_GEMM]
         with torch.cuda.device(self.device):
             stream = torch.cuda.current_stream().cuda_stream
             sp = sc.data_ptr() if sc is not None else None
@@ -285,8 +295,8 @@ class LeechLatticeVectorQuantizerGpu:
             else:
                 self._book().gemm(idx.data_ptr(), n, bpr, sp, a16.data_ptr(), m, k, y.data_ptr(), err.data_ptr(),
                                   stream)
-        if int(err.item()):
-            raise RuntimeError("tensor-core wait timed out in the dequant-GEMM")
+        if check:
+            self.raise_pending_errors()
         return y
 
     def _dequantize_lattice_cuda(self, indices: torch.Tensor) -> torch.Tensor:
@@ -302,6 +312,36 @@ class LeechLatticeVectorQuantizerGpu:
 
     def _error_counter(self) -> torch.Tensor:
         return torch.zeros((1,), dtype=torch.int32, device=self.device)
+
+    # Sticky device-side error flags of the asynchronous (non-reference)
+    # paths: [0] indices outside the codebook or the packed width
+    # (dequantize_bf16, pack_indices), [1] a timed-out tensor-core wait (gemm).
+    FLAG_RANGE = 0
+    FLAG_GEMM = 1
+
+    def _flags(self) -> torch.Tensor:
+        f = getattr(self, "_pending", None)
+        if f is None:
+            f = self._pending = torch.zeros((2,), dtype=torch.int32, device=self.device)
+        return f
+
+    def pending_errors(self) -> dict:
+        """Counts recorded by the asynchronous paths since the last reset
+        (synchronises the host with the device)."""
+        v = self._flags().tolist()
+        return {"index_range": int(v[self.FLAG_RANGE]), "gemm_timeout": int(v[self.FLAG_GEMM])}
+
+    def raise_pending_errors(self) -> None:
+        """Read and clear the pending error flags; raise IndexError for
+        indices outside the codebook (or the packed width), RuntimeError for
+        a timed-out dequant-GEMM."""
+        errs = self.pending_errors()
+        if errs["index_range"] or errs["gemm_timeout"]:
+            self._flags().zero_()
+        if errs["gemm_timeout"]:
+            raise RuntimeError("tensor-core wait timed out in the dequant-GEMM")
+        if errs["index_range"]:
+            raise IndexError("global index outside codebook range (or the packed index width)")
 
     @staticmethod
     def _raise_if_bad(err: torch.Tensor) -> None:

@@ -191,25 +191,11 @@ def multiset_permutation_count(multiplicities: dict[int, int]) -> int:
     return out
 
 
-def _even_f0_multiplicities(leader: ClassLeader) -> dict[int, int]:
-    return {m: c for m, c in leader.multiplicities.items() if m % 4 == 0}
-
-
-def _even_f1_multiplicities(leader: ClassLeader) -> dict[int, int]:
-    return {m: c for m, c in leader.multiplicities.items() if m % 4 == 2}
-
-
-def _odd_multiplicities(leader: ClassLeader) -> dict[int, int]:
-    return {m: c for m, c in leader.multiplicities.items() if m % 2 == 1}
-
-
-def _ascending_multiset(multiplicities: dict[int, int]) -> tuple[int, ...]:
-    return tuple(m for m in sorted(multiplicities) for _ in range(multiplicities[m]))
-
-
-def _odd_signed_leader_values(leader: ClassLeader) -> tuple[int, ...]:
-    """Odd leader magnitudes with the sign that makes each value = 1 (mod 4)."""
-    return tuple(v for m, c in _odd_multiplicities(leader).items() for v in [m if m % 4 == 1 else -m] * c)
+def _residue_counts(leader: ClassLeader, modulus: int, residues: tuple[int, ...]) -> dict[int, int]:
+    """Magnitude counts of the leader restricted to magnitudes whose residue
+    modulo `modulus` is one of `residues` (an even class splits into its
+    |v| = 0 and |v| = 2 (mod 4) parts; an odd class keeps every magnitude)."""
+    return {m: c for m, c in leader.multiplicities.items() if m % modulus in residues}
 
 
 # ------------------------------------------------------------- class leaders
@@ -230,12 +216,12 @@ def build_local_structure(shell: int, class_index: int, leader: ClassLeader,
             signs = 0
         else:
             signs = 1 << (leader.nonzero_count - (0 if w == 0 else 1))
-        perms = multiset_permutation_count(_even_f0_multiplicities(leader)) * \
-            multiset_permutation_count(_even_f1_multiplicities(leader))
+        perms = multiset_permutation_count(_residue_counts(leader, 4, (0,))) * \
+            multiset_permutation_count(_residue_counts(leader, 4, (2,)))
     elif leader.parity == "odd":
         golay = tuple(range(len(golay_codewords)))
         signs = 1
-        perms = multiset_permutation_count(_odd_multiplicities(leader))
+        perms = multiset_permutation_count(_residue_counts(leader, 2, (1,)))
     else:
         raise ValueError(f"unknown parity {leader.parity!r}")
     return ClassLocalStructure(shell, class_index, leader, golay, signs, perms)

@@ -840,7 +840,9 @@ int oracle_quantize_batch(const oracle_book* b, const float* x, int64_t n, int m
     return 0;
 }
 
-/* Batch codeword(): out is n*24 int32; returns the number of failed rows. */
+/* Batch codeword(): out is n*24 int32; returns the number of failed rows
+ * (zero-filled).  oracle_codeword_batch_mt splits the rows into `threads`
+ * contiguous ranges, one POSIX thread each. */
 int64_t oracle_codeword_batch(const oracle_book* b, const int64_t* idx, int64_t n, int32_t* out) {
     int64_t bad = 0;
     for (int64_t r = 0; r < n; ++r) {
@@ -848,6 +850,40 @@ int64_t oracle_codeword_batch(const oracle_book* b, const int64_t* idx, int64_t 
             memset(out + r * DIM, 0, DIM * sizeof(int32_t));
             bad++;
         }
+    }
+    return bad;
+}
+
+typedef struct {
+    const oracle_book* b;
+    const int64_t* idx;
+    int64_t n;
+    int32_t* out;
+    int64_t bad;
+} codeword_job;
+
+static void* codeword_worker(void* arg) {
+    codeword_job* j = (codeword_job*)arg;
+    j->bad = oracle_codeword_batch(j->b, j->idx, j->n, j->out);
+    return NULL;
+}
+
+int64_t oracle_codeword_batch_mt(const oracle_book* b, const int64_t* idx, int64_t n, int32_t* out, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    if ((int64_t)threads > n) threads = n > 0 ? (int)n : 1;
+    pthread_t th[256];
+    codeword_job jobs[256];
+    const int64_t per = (n + threads - 1) / threads;
+    for (int t = 0; t < threads; ++t) {
+        const int64_t lo = per * t < n ? per * t : n, hi = per * (t + 1) < n ? per * (t + 1) : n;
+        jobs[t].b = b; jobs[t].idx = idx + lo; jobs[t].n = hi - lo; jobs[t].out = out + lo * DIM; jobs[t].bad = 0;
+        pthread_create(&th[t], NULL, codeword_worker, &jobs[t]);
+    }
+    int64_t bad = 0;
+    for (int t = 0; t < threads; ++t) {
+        pthread_join(th[t], NULL);
+        bad += jobs[t].bad;
     }
     return bad;
 }

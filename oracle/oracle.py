@@ -57,6 +57,8 @@ def _load():
     lib.oracle_codeword.argtypes = [vp, i64, vp]
     lib.oracle_codeword_batch.restype = i64
     lib.oracle_codeword_batch.argtypes = [vp, vp, i64, vp]
+    lib.oracle_codeword_batch_mt.restype = i64
+    lib.oracle_codeword_batch_mt.argtypes = [vp, vp, i64, vp, ctypes.c_int]
     lib.oracle_encode.restype = i64
     lib.oracle_encode.argtypes = [vp, vp]
     lib.oracle_rank_even_signs.restype = i64
@@ -164,10 +166,17 @@ class OracleBook:
             raise IndexError(index)
         return tuple(int(v) for v in y)
 
-    def codeword_batch(self, indices) -> np.ndarray:
+    def codeword_batch(self, indices, threads: int = 1) -> np.ndarray:
+        """Integer codewords [n, 24] (int32) of int64 indices; threads > 1
+        splits the rows over that many POSIX threads (0: all host cores)."""
         idx = np.ascontiguousarray(indices, dtype=np.int64).reshape(-1)
         out = np.zeros((idx.shape[0], DIM), dtype=np.int32)
-        bad = self._lib.oracle_codeword_batch(self._h, idx.ctypes.data, idx.shape[0], out.ctypes.data)
+        threads = threads or os.cpu_count() or 1
+        if threads > 1:
+            bad = self._lib.oracle_codeword_batch_mt(self._h, idx.ctypes.data, idx.shape[0], out.ctypes.data,
+                                                     threads)
+        else:
+            bad = self._lib.oracle_codeword_batch(self._h, idx.ctypes.data, idx.shape[0], out.ctypes.data)
         if bad:
             raise IndexError(f"{bad} indices out of range")
         return out

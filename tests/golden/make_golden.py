@@ -19,6 +19,7 @@ import contextlib
 import io
 import json
 import multiprocessing as mp
+import os
 import random
 import sys
 import time
@@ -189,10 +190,13 @@ def metadata(root: str, shells=(4, 13)) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("LLVQ_REFERENCE_ROOT"),
+                    help="root of the reference checkout (default: $LLVQ_REFERENCE_ROOT)")
     ap.add_argument("--procs", type=int, default=8)
     ap.add_argument("--only-metadata", action="store_true")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set LLVQ_REFERENCE_ROOT")
     (HERE / "reference_metadata.json").write_text(json.dumps({
         "source": "impl/leech_lattice_vector_quantizer_gpu.py _quantize_cuda_metadata / _codeword_cuda_metadata",
         "shells": metadata(args.reference),

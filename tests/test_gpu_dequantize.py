@@ -101,3 +101,41 @@ def test_every_class_vs_oracle(lo, hi):
     got = q.dequantize_lattice(torch.from_numpy(idx).cuda()).cpu().numpy()
     np.testing.assert_array_equal(got, ob.codeword_batch(idx))
     assert q.total_count == ob.total_count
+
+
+def _class_uniform_indices(q, n: int, seed: int) -> np.ndarray:
+    """Random valid indices drawn like the dequant benchmark's workload:
+    uniform shell, uniform class within the shell, uniform local index."""
+    rng = np.random.default_rng(seed)
+    shells = sorted(q.classes_by_shell)
+    starts = [[q.shell_offsets[s] + o for o in q.class_offsets[s]] for s in shells]
+    counts = [[st.count for st in q.local_structures[s]] for s in shells]
+    sh = rng.integers(0, len(shells), n)
+    out = np.empty(n, dtype=np.int64)
+    for i, s in enumerate(shells):
+        sel = np.nonzero(sh == i)[0]
+        cls = rng.integers(0, len(starts[i]), sel.shape[0])
+        st = np.asarray(starts[i], dtype=np.int64)[cls]
+        cnt = np.asarray(counts[i], dtype=np.float64)[cls]
+        out[sel] = st + np.minimum((rng.random(sel.shape[0]) * cnt).astype(np.int64), cnt.astype(np.int64) - 1)
+    return out
+
+
+def test_llama3_layer_bf16_vs_oracle():
+    """One whole Llama-3-8B layer (q, k, v, o, gate, up, down: 9,103,360
+    indices, bf16 out, fp16 row scales), int64 and packed indices, bit for
+    bit against the oracle's codewords scaled as the kernel defines it:
+    bf16(fp32(fp32(1/sqrt 8) * k) * s)."""
+    q = api(13)
+    shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
+    g = torch.Generator().manual_seed(3)
+    for j, (rows, cols) in enumerate(shapes):
+        bpr = (cols + 23) // 24
+        idx = _class_uniform_indices(q, rows * bpr, seed=30 + j)
+        scale = (torch.rand(rows, generator=g) * 0.04 + 0.005).to(torch.float16)
+        k = torch.from_numpy(oracle_book(13).codeword_batch(idx, threads=0)).view(rows, bpr * 24)
+        want = ((k.float() * np.float32(0.35355339059327373)) * scale.float()[:, None]).to(torch.bfloat16)
+        it = torch.from_numpy(idx).cuda().view(rows, bpr)
+        sc = scale.cuda()
+        assert torch.equal(q.dequantize_bf16(it, sc, check=True).cpu(), want)
+        assert torch.equal(q.dequantize_bf16(q.pack_indices(it, check=True), sc, check=True).cpu(), want)

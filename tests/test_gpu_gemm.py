@@ -118,3 +118,58 @@ def test_gemm_with_activation_rotation():
     # the rotation is exactly a bf16 Hadamard of the activations, then the plain GEMM
     xr = rotate(x.float(), signs, block).to(torch.bfloat16)
     assert torch.equal(y, q.gemm(xr, idx, scale))
+
+
+@pytest.mark.parametrize("m_act", [1, 64])
+def test_gemm_does_not_synchronise_the_host(m_act):
+    """The dequant-GEMM returns while the GPU is still busy: behind a long
+    device-side sleep on the same stream the call comes back before the
+    stream drains; errors wait in the pending flags."""
+    q = api()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    idx = torch.randint(0, q.total_count, (512, 171), generator=g, device="cuda")
+    a = torch.randn((m_act, 4096), generator=g, device="cuda").to(torch.bfloat16)
+    want = q.gemm(a, idx, check=True)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    torch.cuda._sleep(2_000_000_000)  # about a second of device time
+    y = q.gemm(a, idx)
+    assert not stream.query()
+    torch.cuda.synchronize()
+    assert torch.equal(y, want)
+    q.raise_pending_errors()
+
+
+
+@pytest.fixture(scope="module")
+def llama3_mlp():
+    """The Llama-3-8B MLP weights at their real shapes, random valid indices
+    (seed 4), fp16 row scales, and each W decoded by the oracle (the
+    reference's codeword() restated) in fp32: W = fp32(1/sqrt 8) * k * s."""
+    from conftest import oracle_book
+
+    q = api()
+    g = torch.Generator(device="cuda").manual_seed(4)
+    mats = []
+    for n_out, k in ((14336, 4096), (4096, 14336)):
+        bpr = (k + 23) // 24
+        idx = torch.randint(0, q.total_count, (n_out, bpr), generator=g, device="cuda")
+        scale = (torch.rand(n_out, generator=g, device="cuda") * 0.04 + 0.005).to(torch.float16)
+        cw = oracle_book(13).codeword_batch(idx.cpu().numpy().reshape(-1), threads=0)
+        w = torch.from_numpy(cw).cuda().view(n_out, bpr * 24)[:, :k].float() * np.float32(1 / np.sqrt(8.0))
+        mats.append((idx, scale, w * scale.float()[:, None], k))
+    return mats
+
+
+@pytest.mark.parametrize("m_act", [1, 8, 64, 512, 4096])
+def test_gemm_llama3_mlp_shapes(llama3_mlp, m_act):
+    """W 14336 x 4096 and 4096 x 14336 at every batch size of the benchmark
+    against an fp32 matmul with the oracle's decoded weights (relative
+    Frobenius error <= 1e-3)."""
+    q = api()
+    g = torch.Generator(device="cuda").manual_seed(100 + m_act)
+    for idx, scale, w, k in llama3_mlp:
+        a = torch.randn((m_act, k), generator=g, device="cuda").to(torch.bfloat16)
+        y = q.gemm(a, idx, scale, check=True)
+        ref = a.float() @ w.T
+        assert rel_err(y, ref) <= TOL

@@ -41,9 +41,15 @@ def test_pack_roundtrip(m, bytes_):
 def test_pack_rejects_what_does_not_fit():
     q = api(2)
     with pytest.raises(IndexError):
-        q.pack_indices(torch.tensor([0, 1 << 24], device="cuda"))
+        q.pack_indices(torch.tensor([0, 1 << 24], device="cuda"), check=True)
     with pytest.raises(IndexError):
-        q.pack_indices(torch.tensor([-2], device="cuda"))
+        q.pack_indices(torch.tensor([-2], device="cuda"), check=True)
+    # without check the call stays asynchronous; the count waits in the flags
+    q.pack_indices(torch.tensor([-2], device="cuda"))
+    assert q.pending_errors()["index_range"] == 1
+    with pytest.raises(IndexError):
+        q.raise_pending_errors()
+    assert q.pending_errors() == {"index_range": 0, "gemm_timeout": 0}
 
 
 def test_dequantize_packed_every_kind():
@@ -76,7 +82,7 @@ def test_packed_invalid_index_raises():
     q = api()
     pk = q.pack_indices(torch.tensor([[5, -1]], device="cuda"))
     with pytest.raises(IndexError):
-        q.dequantize_bf16(pk, torch.ones(1, dtype=torch.float16, device="cuda"))
+        q.dequantize_bf16(pk, torch.ones(1, dtype=torch.float16, device="cuda"), check=True)
 
 
 @pytest.mark.parametrize("m_act,n,bpr,k", [(8, 300, 20, 472), (513, 384, 171, 4096)])

@@ -108,6 +108,28 @@ def test_gloo_two_ranks_gather_and_resume(tmp_path):
     assert all(torch.equal(res2[k][0], res[k][0]) for k in res)
 
 
+def test_stale_checkpoints_are_quantized_again(tmp_path):
+    """A checkpoint from another configuration (other fingerprint, other
+    shape) is not reused; a matching one is."""
+    specs = llama2_7b_matrices(layers=1, scale_down=64)
+    calls = []
+
+    def q(spec):
+        calls.append(spec.key)
+        return fake_quantize(spec)
+
+    run_shard(specs, 0, 1, tmp_path, q, fingerprint={"rate": 2.0, "seed": 2})
+    assert len(calls) == len(specs)
+    run_shard(specs, 0, 1, tmp_path, q, fingerprint={"rate": 2.0, "seed": 2})
+    assert len(calls) == len(specs)  # all resumed
+    run_shard(specs, 0, 1, tmp_path, q, fingerprint={"rate": 2.5, "seed": 2})
+    assert len(calls) == 2 * len(specs)  # other rate: every matrix again
+    wider = llama2_7b_matrices(layers=1, scale_down=32)  # same keys, more rows
+    run_shard(wider, 0, 1, tmp_path, q, fingerprint={"rate": 2.5, "seed": 2})
+    assert len(calls) == 3 * len(specs)
+    assert not list(tmp_path.glob("*.tmp*"))
+
+
 def test_gloo_failing_rank_is_reported(tmp_path):
     codes = _spawn(2, tmp_path, fail_rank=1)
     assert codes[1] != 0  # the failing rank exits with an error

@@ -75,3 +75,13 @@ def test_noalloc_widest_rows_accepted_and_wider_rejected():
     a = torch.zeros((300, 64), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError, match="2730"):
         _run(q, "gemm_noalloc", wide, a, torch.ones(4, dtype=torch.float16, device="cuda"))
+
+
+def test_noalloc_empty_call_then_small_batch_wide_rows():
+    """An empty call prepares the device (loads the array's module); batches
+    of m <= 4 decode in registers, so rows wider than the array's limit are
+    accepted there and match llvq_gemm."""
+    q = _quantizer()
+    idx, a, scale = _case(q, 3, 40, MAX_BPR + 7, 24 * (MAX_BPR + 7), seed=14)
+    _run(q, "gemm_noalloc", idx, a[:0], scale)  # m = 0: setup only
+    assert torch.equal(_run(q, "gemm_noalloc", idx, a, scale), _run(q, "gemm", idx, a, scale))
