@@ -75,6 +75,21 @@ int llvq_quantize(const llvq_codebook* cb, const float* x, int64_t n, int64_t* i
 int llvq_quantize_ex(const llvq_codebook* cb, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
                      float* best_score, uint32_t flags, void* stream);
 
+/* Shape-gain quantization in one pass (no reference counterpart: the
+ * reference lists shape-gain in its README only).  The shape is llvq_quantize's
+ * codeword (for a single-shell codebook: the shell point of largest
+ * correlation with x); the gain g = <x, y> / |y| (the same compensated fp64
+ * projection as the score, |y| = sqrt(16 shell)), divided by row_sigma[i /
+ * blocks_per_row] when row_sigma (fp32, device) is not NULL, is coded as the
+ * number of the 2^gain_bits - 1 ascending fp64 gain_thresholds (device) below
+ * it.  gain_index[i] (int32, may be NULL) receives the code; with pack != 0,
+ * indices[i] = shape << gain_bits | code (shape bits + gain_bits <= 63),
+ * else the shape index.  Rows with NaN/Inf: index -1, code -1.  Same
+ * launches, scratch and stream rules as llvq_quantize. */
+int llvq_quantize_gain(const llvq_codebook* cb, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
+                       float* best_score, const double* gain_thresholds, int32_t gain_bits, const float* row_sigma,
+                       int64_t blocks_per_row, int32_t* gain_index, int32_t pack, void* stream);
+
 /* Integer codewords [n,24] of indices [n].  Out-of-range indices give zero
  * rows and are counted into *error_count (device int, may be NULL).
  * Replaces dequantize_lattice_cuda (impl/llvq_cuda_dequantize.py:221-261). */

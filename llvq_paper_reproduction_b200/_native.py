@@ -37,6 +37,7 @@ EXPORTS = (
     "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version", "llvq_gemm",
     "llvq_hadamard", "llvq_gemm_noalloc", "llvq_pack_indices", "llvq_unpack_indices", "llvq_dequantize_packed",
     "llvq_gemm_packed", "llvq_hadamard_ex", "llvq_codeword_batch_host", "llvq_codebook_tables",
+    "llvq_quantize_gain",
 )
 
 _lib = None
@@ -61,6 +62,7 @@ def load() -> ctypes.CDLL:
             "llvq_codebook_info": (ctypes.c_int, [vp, P(i64), P(i32), P(i32), P(i32), P(i32)]),
             "llvq_quantize": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, vp]),
             "llvq_quantize_ex": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, ctypes.c_uint32, vp]),
+            "llvq_quantize_gain": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, vp, i32, vp, i64, vp, i32, vp]),
             "llvq_dequantize_lattice": (ctypes.c_int, [vp, vp, i64, vp, vp, vp]),
             "llvq_dequantize": (ctypes.c_int, [vp, vp, i64, vp, i32, vp, vp]),
             "llvq_dequantize_bf16": (ctypes.c_int, [vp, vp, i64, vp, i64, vp, vp, vp]),
@@ -174,6 +176,13 @@ class NativeCodebook:
                  flags: int = 0) -> None:
         check(self._lib.llvq_quantize_ex(self.handle, x_ptr, n, idx_ptr, pair_ptr, score_ptr, flags, stream),
               "llvq_quantize")
+
+    def quantize_gain(self, x_ptr: int, n: int, idx_ptr: int, pair_ptr: int, score_ptr: int, thr_ptr: int,
+                      gain_bits: int, sigma_ptr: int | None, blocks_per_row: int, gain_ptr: int | None, pack: bool,
+                      stream: int) -> None:
+        check(self._lib.llvq_quantize_gain(self.handle, x_ptr, n, idx_ptr, pair_ptr, score_ptr, thr_ptr, gain_bits,
+                                           sigma_ptr, blocks_per_row, gain_ptr, int(pack), stream),
+              "llvq_quantize_gain")
 
     def dequantize_lattice(self, idx_ptr: int, n: int, out_ptr: int, err_ptr: int | None, stream: int) -> None:
         check(self._lib.llvq_dequantize_lattice(self.handle, idx_ptr, n, out_ptr, err_ptr, stream),

@@ -603,6 +603,30 @@ int llvq_quantize_ex(const llvq_codebook* h, const float* x, int64_t n, int64_t*
   });
 }
 
+int llvq_quantize_gain(const llvq_codebook* h, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
+                       float* best_score, const double* gain_thresholds, int32_t gain_bits, const float* row_sigma,
+                       int64_t blocks_per_row, int32_t* gain_index, int32_t pack, void* stream) {
+  if (n < 0 || (n > 0 && (!x || !indices || !best_pair || !best_score || !gain_thresholds)))
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad quantize arguments");
+  if (gain_bits < 1 || gain_bits > 16 || (row_sigma && blocks_per_row <= 0))
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "gain code: need 1 <= gain_bits <= 16 and blocks_per_row > 0");
+  if (!h) return fail(LLVQ_ERR_INVALID_ARGUMENT, "null codebook");
+  if (pack && (h->cb.total > 0 ? 64 - __builtin_clzll((unsigned long long)(h->cb.total - 1)) : 1) + gain_bits > 63)
+    return fail(LLVQ_ERR_UNSUPPORTED, "packed shape-gain index exceeds 63 bits");
+  llvq::GainCode gc;
+  gc.thr = gain_thresholds;
+  gc.nthr = (1 << gain_bits) - 1;
+  gc.bits = gain_bits;
+  gc.sigma = row_sigma;
+  gc.bpr = row_sigma ? blocks_per_row : 1;
+  gc.gain_out = gain_index;
+  gc.pack = pack != 0;
+  return on_device(h, [&] {
+    return llvq::quantize_launch(h->cb, x, n, reinterpret_cast<long long*>(indices),
+                                 reinterpret_cast<long long*>(best_pair), best_score, (cudaStream_t)stream, false, gc);
+  });
+}
+
 int llvq_quantize(const llvq_codebook* h, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
                   float* best_score, void* stream) {
   return llvq_quantize_ex(h, x, n, indices, best_pair, best_score, 0u, stream);

@@ -208,16 +208,21 @@ bool build_expand(const std::vector<uint32_t>& golay, std::vector<uint32_t>& out
   for (int gi = 0; gi < kNumGolay; ++gi) {
     uint32_t* e = out.data() + (size_t)gi * kTabExpandWords;
     const uint32_t w = golay[gi];
-    for (int part = 0; part < 2; ++part) {
-      uint32_t mv[5];
-      expand_masks(part ? (~w & kFull24) : w, mv);
-      for (int i = 0; i < 5; ++i) nibble_spread(mv[i], e + 15 * part + 3 * i);
+    uint32_t mva[5], mvb[5], ma[3], mb[3], m0[3];
+    expand_masks(w, mva);
+    expand_masks(~w & kFull24, mvb);
+    nibble_spread(w, m0);
+    for (int q = 0; q < 5; ++q) {  // stage q applies the shift by 2^(4-q) positions
+      nibble_spread(mva[4 - q], ma);
+      nibble_spread(mvb[4 - q], mb);
+      uint32_t* st = e + 8 * q;
+      st[0] = ma[0]; st[1] = ma[1]; st[2] = ma[2]; st[3] = mb[0];
+      st[4] = mb[1]; st[5] = mb[2]; st[6] = q < 3 ? m0[q] : 0u; st[7] = 0;
     }
-    nibble_spread(w, e + 30);
     // self-check: random nibble strings (garbage beyond each part's length)
     // land on the right positions
     for (int trial = 0; trial < 4; ++trial) {
-      uint32_t xa[3], xb[3], want_a[24], want_b[24];
+      uint32_t xa[3], xb[3], want_a[24], want_b[24], m[3];
       int ia = 0, ib = 0;
       for (int k = 0; k < 3; ++k) {
         seed = seed * 1664525u + 1013904223u;
@@ -230,11 +235,11 @@ bool build_expand(const std::vector<uint32_t>& golay, std::vector<uint32_t>& out
         if ((w >> d) & 1u) want_a[d] = nib(xa, ia++);
         else want_b[d] = nib(xb, ib++);
       }
-      tab_expand(xa, e);
-      tab_expand(xb, e + 15);
+      tab_expand2(xa, xb, reinterpret_cast<const uint4*>(e), m);
       for (int d = 0; d < kDim; ++d) {
-        const uint32_t got = ((w >> d) & 1u) ? nib(xa, d) : nib(xb, d);
-        if (got != (((w >> d) & 1u) ? want_a[d] : want_b[d])) {
+        const bool on = (w >> d) & 1u;
+        const uint32_t got = on ? nib(xa, d) : nib(xb, d);
+        if (got != (on ? want_a[d] : want_b[d]) || nib(m, d) != (on ? 15u : 0u)) {
           why = "expand self-check failed";
           return false;
         }

@@ -21,7 +21,7 @@ constexpr int kDeqThreads = 256;
 // dequant workload; the decode is issue-bound and latency-bound in turn.
 constexpr int kDeqMinBlocks = 5;
 
-template <int KIND>
+template <int KIND, bool TAB>
 __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(IndexSource index, int64_t n,
                                                               DevBook book, void* __restrict__ out,
                                                               const uint16_t* __restrict__ row_scale,
@@ -33,7 +33,7 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(Ind
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   int y[kDim];
-  const bool ok = decode_index(load_index(index, i), book, sh, y);
+  const bool ok = decode_any<TAB>(load_index(index, i), book, sh, y);
   if (!ok && error_count) atomicAdd(error_count, 1);
   if constexpr (KIND == 0) {
     longlong2* o = reinterpret_cast<longlong2*>(static_cast<long long*>(out) + i * kDim);
@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(Ind
 // Weight staging for the large-batch GEMM: indices [rows, bpr] -> bf16
 // integer codewords [rows, ldw] (columns >= 24 * bpr zero), one thread per
 // (row, block) plus the padding.
+template <bool TAB>
 __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(IndexSource index, int rows,
                                                                        int bpr, int ldw, DevBook book,
                                                                        __nv_bfloat16* __restrict__ out, uint64_t magic_per_row) {
@@ -85,7 +86,7 @@ __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(IndexSour
   __nv_bfloat16* o = out + (int64_t)r * ldw;
   if (b < bpr) {
     int y[kDim];
-    decode_index(load_index(index, (int64_t)r * bpr + b), book, sh, y);
+    decode_any<TAB>(load_index(index, (int64_t)r * bpr + b), book, sh, y);
     uint4* dst = reinterpret_cast<uint4*>(o + b * kDim);
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
@@ -106,8 +107,14 @@ cudaError_t decode_rows_bf16_launch(const Codebook& cb, IndexSource index, int r
                                     cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const int64_t n = (int64_t)rows * (ldw / kDim + 1);
-  decode_rows_bf16_kernel<<<(unsigned)((n + kDeqThreads - 1) / kDeqThreads), kDeqThreads, 0, stream>>>(
-      index, rows, bpr, ldw, cb.dev, static_cast<__nv_bfloat16*>(out), ~0ull / (uint64_t)(ldw / kDim + 1));
+  const unsigned grid = (unsigned)((n + kDeqThreads - 1) / kDeqThreads);
+  const uint64_t magic = ~0ull / (uint64_t)(ldw / kDim + 1);
+  if (cb.dev.tab.state)
+    decode_rows_bf16_kernel<true><<<grid, kDeqThreads, 0, stream>>>(index, rows, bpr, ldw, cb.dev,
+                                                                     static_cast<__nv_bfloat16*>(out), magic);
+  else
+    decode_rows_bf16_kernel<false><<<grid, kDeqThreads, 0, stream>>>(index, rows, bpr, ldw, cb.dev,
+                                                                      static_cast<__nv_bfloat16*>(out), magic);
   return cudaGetLastError();
 }
 
@@ -117,13 +124,20 @@ cudaError_t dequantize_launch(const Codebook& cb, IndexSource index, int64_t n, 
   if (n <= 0) return cudaSuccess;
   const unsigned blocks = (unsigned)((n + kDeqThreads - 1) / kDeqThreads);
   const uint64_t magic_bpr = ~0ull / (uint64_t)(blocks_per_row > 0 ? blocks_per_row : 1);
+  const bool tab = cb.dev.tab.state != nullptr;
+#define LLVQ_DEQ(K)                                                                                            \
+  (tab ? dequant_kernel<K, true><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale,          \
+                                                                      blocks_per_row, magic_bpr, error_count)  \
+       : dequant_kernel<K, false><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale,         \
+                                                                       blocks_per_row, magic_bpr, error_count))
   switch (kind) {
-    case 0: dequant_kernel<0><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, magic_bpr, error_count); break;
-    case 1: dequant_kernel<1><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, magic_bpr, error_count); break;
-    case 2: dequant_kernel<2><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, magic_bpr, error_count); break;
-    case 3: dequant_kernel<3><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row, magic_bpr, error_count); break;
+    case 0: LLVQ_DEQ(0); break;
+    case 1: LLVQ_DEQ(1); break;
+    case 2: LLVQ_DEQ(2); break;
+    case 3: LLVQ_DEQ(3); break;
     default: return cudaErrorInvalidValue;
   }
+#undef LLVQ_DEQ
   return cudaGetLastError();
 }
 

@@ -36,7 +36,7 @@ __device__ __forceinline__ float dot8(uint4 v, const float* w, float acc) {
   return acc;
 }
 
-template <int MB>
+template <int MB, bool TAB>
 __global__ void __launch_bounds__(kGemvThreads) gemv_decode_kernel(IndexSource index, int n_out, int bpr,
                                                                     DevBook book, const uint16_t* __restrict__ rscale,
                                                                     const __nv_bfloat16* __restrict__ a, int m, int k,
@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_decode_kernel(IndexSource i
   for (int i = 0; i < MB; ++i) acc[i] = 0.f;
   for (int b = lane; b < bpr && 24 * b < k; b += 32) {
     int w[kDim];
-    decode_index(load_index(index, (int64_t)n * bpr + b), book, sh, w);
+    decode_any<TAB>(load_index(index, (int64_t)n * bpr + b), book, sh, w);
     float wf[kDim];
 #pragma unroll
     for (int d = 0; d < kDim; ++d) wf[d] = (float)w[d];
@@ -90,12 +90,19 @@ cudaError_t gemv_decode_launch(const Codebook& cb, IndexSource idx, int64_t n_ou
   const unsigned grid = (unsigned)((n_out + kGemvThreads / 32 - 1) / (kGemvThreads / 32));
   const auto* ab = static_cast<const __nv_bfloat16*>(a);
   const int n = (int)n_out, b = (int)bpr, mm = (int)m, kk = (int)k;
+  const bool tab = cb.dev.tab.state != nullptr;
+#define LLVQ_GEMV(MB)                                                                                      \
+  (tab ? gemv_decode_kernel<MB, true><<<grid, kGemvThreads, 0, stream>>>(idx, n, b, cb.dev, rscale, ab, mm, \
+                                                                          kk, y)                           \
+       : gemv_decode_kernel<MB, false><<<grid, kGemvThreads, 0, stream>>>(idx, n, b, cb.dev, rscale, ab, mm, \
+                                                                           kk, y))
   if (m == 1)
-    gemv_decode_kernel<1><<<grid, kGemvThreads, 0, stream>>>(idx, n, b, cb.dev, rscale, ab, mm, kk, y);
+    LLVQ_GEMV(1);
   else if (m == 2)
-    gemv_decode_kernel<2><<<grid, kGemvThreads, 0, stream>>>(idx, n, b, cb.dev, rscale, ab, mm, kk, y);
+    LLVQ_GEMV(2);
   else
-    gemv_decode_kernel<4><<<grid, kGemvThreads, 0, stream>>>(idx, n, b, cb.dev, rscale, ab, mm, kk, y);
+    LLVQ_GEMV(4);
+#undef LLVQ_GEMV
   return cudaGetLastError();
 }
 

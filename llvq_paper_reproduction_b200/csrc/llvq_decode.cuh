@@ -30,6 +30,7 @@
 
 #include "llvq_device.cuh"
 #include "llvq_internal.h"
+#include "llvq_tables.cuh"
 
 namespace llvq {
 
@@ -528,6 +529,66 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
     for (int d = 0; d < kDim; ++d) y[d] = 0;
   }
   return ok;
+}
+
+// Integer codeword of index v with the table-driven decoder (llvq_tables.cuh):
+// class, record and the class-local split as in decode_index, then a part's
+// sequence from at most three table lookups per part instead of one
+// unranking step per coordinate.  false and zeros outside the codebook.
+__device__ __forceinline__ bool decode_index_tab(int64_t v, const DevBook& book, const DecodeShared& sh,
+                                                 int (&y)[kDim]) {
+  if (!(v >= 0 && v < book.total)) {
+#pragma unroll
+    for (int d = 0; d < kDim; ++d) y[d] = 0;
+    return false;
+  }
+  const int k = find_class_bucketed(book, book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start, v);
+  const uint4* rp = reinterpret_cast<const uint4*>(book.dcls + k);
+  const uint4 w0 = __ldg(rp), w1 = __ldg(rp + 1), w2 = __ldg(rp + 2), w3 = __ldg(rp + 3), w4 = __ldg(rp + 4);
+  const uint2 st = __ldg(book.tab.cls + k);
+  auto u64 = [](uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; };
+  const uint64_t start = u64(w0.x, w0.y), perm = u64(w0.z, w0.w), magic_perm = u64(w1.x, w1.y);
+  const uint32_t f1p = w2.x, meta = w2.y, gbase = w2.z;
+  const uint64_t magic_f1 = u64(w3.x, w3.y), pv0 = u64(w3.z, w3.w), pv1 = u64(w4.z, w4.w);
+  const bool odd = meta & 1;
+  const int sshift = (meta >> 6) & 31;
+  uint64_t prank;
+  const uint64_t cur = div_magic((uint64_t)v - start, perm, magic_perm, prank);
+  uint32_t word;
+  int word_lex, d0;
+  uint64_t sign = 0, ra, rb = 0, vals;
+  if (odd) {
+    word = __ldg(book.golay + (int)cur);
+    word_lex = kNumGolay - 1;  // part A covers every position
+    d0 = 0;
+    ra = prank;
+    vals = pv0;
+  } else {
+    sign = cur & ((1ull << sshift) - 1);
+    word_lex = __ldg(book.by_weight + gbase + (int)(cur >> sshift));
+    word = __ldg(book.golay + word_lex);
+    uint64_t r1;
+    rb = div_magic(prank, f1p, magic_f1, r1);
+    ra = r1;
+    d0 = (int)((meta >> 11) & 15u);
+    vals = pv0 | (d0 < 8 ? pv1 << (8 * d0) : 0ull);
+  }
+  uint32_t mag[6];
+  tab_magnitudes(book.tab, st.x, ra, st.y, rb, word_lex, d0, vals, mag);
+  const bool ok = tab_signs(mag, word, odd, sign, (int)((meta >> 19) & 1u), sh.deposit4, y);
+  if (!ok) {
+#pragma unroll
+    for (int d = 0; d < kDim; ++d) y[d] = 0;
+  }
+  return ok;
+}
+
+// The codebook's decoder: table-driven when its tables exist (TAB, decided
+// per launch), else the arithmetic unranking.
+template <bool TAB>
+__device__ __forceinline__ bool decode_any(int64_t v, const DevBook& book, DecodeShared& sh, int (&y)[kDim]) {
+  if constexpr (TAB) return decode_index_tab(v, book, sh, y);
+  else return decode_index(v, book, sh, y);
 }
 
 }  // namespace llvq

@@ -12,8 +12,23 @@
 
 namespace llvq {
 
+// Optional gain code written by the quantizer's finalize step (shape-gain
+// quantization): thresholds (ascending fp64, nthr of them, 2^bits - 1 for a
+// bits-bit code), optional per-row divisor sigma (one per bpr blocks), the
+// gain code per block into gain_out (may be null) and, with pack, the index
+// replaced by index << bits | gain.  thr == null: no gain code.
+struct GainCode {
+  const double* thr = nullptr;
+  int nthr = 0;
+  int bits = 0;
+  const float* sigma = nullptr;
+  int64_t bpr = 1;
+  int* gain_out = nullptr;
+  int pack = 0;
+};
+
 using SearchLauncher = cudaError_t (*)(const float*, int64_t, const DevBook&, long long*, long long*, float*,
-                                       cudaStream_t);
+                                       const GainCode&, cudaStream_t);
 
 // A generated search specialisation: its class signature, launcher and the
 // window constants of its FFMA chains.
@@ -68,7 +83,7 @@ bool decode_index_tables_host(const Codebook& cb, int64_t v, int32_t* out);
 const SpecEntry* spec_table(int* count);
 
 cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long long* index, long long* pair,
-                            float* score, cudaStream_t stream, bool force_runtime);
+                            float* score, cudaStream_t stream, bool force_runtime, const GainCode& gc = GainCode{});
 
 // Where a kernel reads its indices: int64 (bytes = 8) or packed little-endian
 // unsigned integers of 1..7 bytes, the all-ones value standing for an

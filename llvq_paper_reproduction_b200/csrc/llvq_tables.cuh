@@ -34,7 +34,7 @@ namespace llvq {
 constexpr int kTabTail = 12;              // positions a tail state covers
 constexpr int kTabHead = 6;               // positions one search covers
 constexpr uint32_t kTabEnd = 0xFFFFFFFFu; // no state: the part is empty / finished
-constexpr int kTabExpandWords = 36;       // u32 per Golay word in the expand table
+constexpr int kTabExpandWords = 40;       // u32 per Golay word in the expand table
 
 // State record (uint4):
 //   tail:   x = first entry in `tail`, w = kTabTailBit | positions
@@ -140,19 +140,34 @@ LLVQ_HD void tab_shl96(const uint32_t (&x)[3], uint32_t (&t)[3]) {
   }
 }
 
-// Nibble-wise expand of x by the move masks m[0..14] (stage i, register k at
-// m[3 i + k]): source nibble t goes to the t-th set position of the mask the
-// masks were made from.  Positions outside that mask hold garbage.
-LLVQ_HD void tab_expand(uint32_t (&x)[3], const uint32_t* m) {
+// Expand table layout, per Golay word (lexicographic index), kTabExpandWords
+// u32 as five 32-byte stages q = 0..4 (applied in that order; stage q moves
+// nibbles by 2^(4-q) positions): {A0, A1, A2, B0}, {B1, B2, M_q, 0}, where
+// A0..A2 / B0..B2 are the nibble-wide move masks of the expand by the word /
+// by its complement (three u32 covering positions 0-7, 8-15, 16-23) and
+// M_0..M_2 the word itself widened to nibbles.
+//
+// Nibble-wise expand of both parts at once: source nibble t of xa goes to
+// the t-th position of the word, source nibble t of xb to the t-th position
+// outside it; m receives the word's nibble mask.  Positions outside each
+// part's mask hold garbage.
+LLVQ_HD void tab_expand2(uint32_t (&xa)[3], uint32_t (&xb)[3], const uint4* e, uint32_t (&m)[3]) {
   uint32_t t[3];
-#define LLVQ_EXPAND_STAGE(I, S)                                              \
-  tab_shl96<S>(x, t);                                                        \
-  for (int k = 0; k < 3; ++k) x[k] = (x[k] & ~m[3 * (I) + k]) | (t[k] & m[3 * (I) + k]);
-  LLVQ_EXPAND_STAGE(4, 64)
-  LLVQ_EXPAND_STAGE(3, 32)
+#define LLVQ_EXPAND_STAGE(Q, S)                                                           \
+  {                                                                                        \
+    const uint4 u = tab_ld(e + 2 * (Q)), v = tab_ld(e + 2 * (Q) + 1);                       \
+    const uint32_t ma[3] = {u.x, u.y, u.z}, mb[3] = {u.w, v.x, v.y};                      \
+    if ((Q) < 3) m[(Q) < 3 ? (Q) : 0] = v.z;                                               \
+    tab_shl96<S>(xa, t);                                                                   \
+    for (int k = 0; k < 3; ++k) xa[k] = (xa[k] & ~ma[k]) | (t[k] & ma[k]);                  \
+    tab_shl96<S>(xb, t);                                                                   \
+    for (int k = 0; k < 3; ++k) xb[k] = (xb[k] & ~mb[k]) | (t[k] & mb[k]);                  \
+  }
+  LLVQ_EXPAND_STAGE(0, 64)
+  LLVQ_EXPAND_STAGE(1, 32)
   LLVQ_EXPAND_STAGE(2, 16)
-  LLVQ_EXPAND_STAGE(1, 8)
-  LLVQ_EXPAND_STAGE(0, 4)
+  LLVQ_EXPAND_STAGE(3, 8)
+  LLVQ_EXPAND_STAGE(4, 4)
 #undef LLVQ_EXPAND_STAGE
 }
 
@@ -190,21 +205,14 @@ LLVQ_HD void tab_magnitudes(const TabView& tv, uint32_t sa, uint64_t ra, uint32_
   const uint64_t add = (uint64_t)d0 * 0x1111111111111111ull;
   a_lo += add;
   a_hi += add & 0xFFFFFFFFull;
-  const uint4* ex = tv.expand + (size_t)word_lex * (kTabExpandWords / 4);
-  uint32_t m[kTabExpandWords];
-#pragma unroll
-  for (int q = 0; q < kTabExpandWords / 4; ++q) {
-    const uint4 v = tab_ld(ex + q);
-    m[4 * q] = v.x; m[4 * q + 1] = v.y; m[4 * q + 2] = v.z; m[4 * q + 3] = v.w;
-  }
   uint32_t xa[3] = {(uint32_t)a_lo, (uint32_t)(a_lo >> 32), (uint32_t)a_hi};
   uint32_t xb[3] = {(uint32_t)b_lo, (uint32_t)(b_lo >> 32), (uint32_t)b_hi};
-  tab_expand(xa, m);
-  tab_expand(xb, m + 15);
+  uint32_t m[3];
+  tab_expand2(xa, xb, tv.expand + (size_t)word_lex * (kTabExpandWords / 4), m);
   const uint32_t vlo = (uint32_t)vals, vhi = (uint32_t)(vals >> 32);
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
-    const uint32_t x = (xa[k] & m[30 + k]) | (xb[k] & ~m[30 + k]);
+    const uint32_t x = (xa[k] & m[k]) | (xb[k] & ~m[k]);
     mag[2 * k] = tab_prmt(vlo, vhi, x & 0xFFFFu);
     mag[2 * k + 1] = tab_prmt(vlo, vhi, x >> 16);
   }

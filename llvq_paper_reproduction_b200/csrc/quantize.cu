@@ -127,7 +127,7 @@ __device__ __forceinline__ double window_width(float K, const DevBook& b) {
 
 // CPython 3.12 sum() of the float products x_d * y_d (Neumaier-compensated),
 // then LATTICE_SCALE * proj - shell, every operation separately rounded.
-__device__ double reference_score(const float* x, const int* y, int shell) {
+__device__ double reference_projection(const float* x, const int* y) {
   double f = __dadd_rn(0.0, __dmul_rn((double)x[0], (double)y[0]));
   double c = 0.0;
 #pragma unroll
@@ -139,7 +139,11 @@ __device__ double reference_score(const float* x, const int* y, int shell) {
     f = t;
   }
   if (c != 0.0 && isfinite(c)) f = __dadd_rn(f, c);
-  return __dsub_rn(__dmul_rn(kLatticeScaleD, f), (double)shell);
+  return f;
+}
+
+__device__ double reference_score(const float* x, const int* y, int shell) {
+  return __dsub_rn(__dmul_rn(kLatticeScaleD, reference_projection(x, y)), (double)shell);
 }
 
 // The reference's best codeword of class c for Golay word `word`
@@ -517,9 +521,26 @@ __device__ __noinline__ void consider_exact(const float* x, const int8_t* apos, 
   }
 }
 
-// Rebuild the winning codeword, its fp64 reference score and its index.
+// Gain code of the winning codeword for shape-gain quantization (gc.thr
+// null: none).  g = <x, y> / |y| (the projection is the reference score's
+// compensated fp64 sum; |y| = sqrt(16 shell)), divided by gc.sigma[row /
+// gc.bpr] when given; the code is the number of thresholds below g.
+__device__ __forceinline__ int gain_code(const GainCode& gc, const float* x, const int* y, int shell, int64_t row) {
+  double g = __ddiv_rn(reference_projection(x, y), __dsqrt_rn(16.0 * (double)shell));
+  if (gc.sigma) g = __ddiv_rn(g, (double)__ldg(gc.sigma + row / gc.bpr));
+  int lo = 0, hi = gc.nthr;  // first threshold >= g
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(gc.thr + mid) < g) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+// Rebuild the winning codeword, its fp64 reference score and its index (and
+// its gain code).
 __device__ __noinline__ void write_winner(const float* x, const int8_t* apos, const DevBook& book, long long order,
-                                          int64_t row, long long* index_out, long long* pair_out, float* score_out) {
+                                          int64_t row, long long* index_out, long long* pair_out, float* score_out,
+                                          GainCode gc) {
   const int lex = (int)(order / book.n_classes), k = (int)(order % book.n_classes);
   const DevClass& c = book.cls[k];
   const uint32_t word = book.golay[lex];
@@ -527,7 +548,13 @@ __device__ __noinline__ void write_winner(const float* x, const int8_t* apos, co
   build_candidate(x, apos, c, word, y);
   const double s = reference_score(x, y, c.shell);
   const int choice = c.parity ? lex : (int)book.golay_wrank[lex];
-  index_out[row] = rank_codeword(c, y, word, choice);
+  long long idx = rank_codeword(c, y, word, choice);
+  if (gc.thr) {
+    const int g = gain_code(gc, x, y, c.shell, row);
+    if (gc.gain_out) gc.gain_out[row] = g;
+    if (gc.pack) idx = (idx << gc.bits) | g;
+  }
+  index_out[row] = idx;
   pair_out[row] = (long long)k * kNumGolay + lex;
   score_out[row] = (float)s;
 }
@@ -691,7 +718,8 @@ __global__ void __launch_bounds__(Ops<S>::kThreads, Ops<S>::kMinBlocks) search_k
 template <class S>
 __global__ void __launch_bounds__(128) finalize_kernel(const float* __restrict__ x, int64_t n, DevBook book,
                                                        const long long* tag_in, const float* m_in,
-                                                       long long* index_out, long long* pair_out, float* score_out) {
+                                                       long long* index_out, long long* pair_out, float* score_out,
+                                                       GainCode gc) {
   const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= n) return;
   const long long tag = tag_in[row];
@@ -699,6 +727,7 @@ __global__ void __launch_bounds__(128) finalize_kernel(const float* __restrict__
     index_out[row] = -1;
     pair_out[row] = -1;
     score_out[row] = NAN;
+    if (gc.gain_out) gc.gain_out[row] = -1;
     return;
   }
   RowLocal r;
@@ -767,17 +796,18 @@ __global__ void __launch_bounds__(128) finalize_kernel(const float* __restrict__
       index_out[row] = -1;
       pair_out[row] = -1;
       score_out[row] = NAN;
+      if (gc.gain_out) gc.gain_out[row] = -1;
       return;
     }
   }
-  write_winner(r.x, r.apos, book, order, row, index_out, pair_out, score_out);
+  write_winner(r.x, r.apos, book, order, row, index_out, pair_out, score_out, gc);
 }
 
 // ------------------------------------------------------------- launchers
 
 template <class S>
 static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book, long long* index, long long* pair,
-                                 float* score, cudaStream_t stream) {
+                                 float* score, const GainCode& gc, cudaStream_t stream) {
   // persistent grid: SMs x resident CTAs, looked up once per device (host
   // threads that race here compute the same value)
   static std::atomic<int> grid_cap[kMaxDevices];
@@ -799,7 +829,8 @@ static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book,
   search_kernel<S><<<(unsigned)grid, Ops<S>::kThreads, 0, stream>>>(x, n, book, pair, score);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
-  finalize_kernel<S><<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(x, n, book, pair, score, index, pair, score);
+  finalize_kernel<S><<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(x, n, book, pair, score, index, pair, score,
+                                                                      gc);
   return cudaGetLastError();
 }
 
@@ -814,7 +845,7 @@ const SpecEntry* spec_table(int* count) {
 }
 
 cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long long* index, long long* pair,
-                            float* score, cudaStream_t stream, bool force_runtime) {
+                            float* score, cudaStream_t stream, bool force_runtime, const GainCode& gc) {
   if (n <= 0) return cudaSuccess;
   DevBook book = cb.dev;
   SearchLauncher launch;
@@ -829,7 +860,7 @@ cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long 
     book.win_mg = cb.rt_mg;
     book.win_am = cb.rt_am;
   }
-  return launch(x, n, book, index, pair, score, stream);
+  return launch(x, n, book, index, pair, score, gc, stream);
 }
 
 }  // namespace llvq

@@ -18,7 +18,10 @@ but the package does not exist); it is defined here as:
     a b-bit Lloyd-Max quantizer designed for the chi(24) density scaled by
     sigma (the norm of a 24-D N(0, sigma^2 I) block);
   * index = shape_index * 2^b + gain_index, reconstruction g_q * u.
-Every tensor step runs on the GPU; the shape search is the library kernel.
+The shape search and the gain code run in one library call
+(llvq_quantize_gain): the finalize kernel that ranks the winning codeword
+also forms g = <x, y> / |y| in fp64 (the compensated projection of the
+reference score) and codes it against fp64 thresholds.
 """
 from __future__ import annotations
 
@@ -156,7 +159,7 @@ class ShapeGainQuantizer:
         self.sigma = sigma
         levels, thr = chi_lloyd_max(gain_bits)
         self.levels = torch.tensor(levels * sigma, dtype=torch.float32, device=self.shape.device)
-        self.thresholds = torch.tensor(thr * sigma, dtype=torch.float32, device=self.shape.device)
+        self.thresholds = torch.tensor(thr * sigma, dtype=torch.float64, device=self.shape.device)
         self.norm = math.sqrt(2.0 * shell)  # |y| / sqrt(8) for every point of the shell
 
     @classmethod
@@ -170,20 +173,42 @@ class ShapeGainQuantizer:
 
     def quantize_parts(self, x: torch.Tensor,
                        row_sigma: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-        """x [..., 24] -> (shape index, gain index), both int64.  row_sigma
-        (broadcast to x[..., 0]) rescales the gain code per block, e.g. per
-        weight row."""
-        x = x.to(device=self.shape.device, dtype=torch.float32)
-        sidx = self.shape.quantize(x)
-        u = self.shape.dequantize(sidx) / self.norm
-        g = (x * u).sum(-1)
+        """x [..., 24] -> (shape index int64, gain index int32).  row_sigma
+        (broadcast to x[..., 0]) divides the gain before coding, e.g. per
+        weight row.  One library call: search, ranking and gain code."""
+        idx, gain = self._run(x, row_sigma, pack=False)
+        return idx, gain
+
+    def _run(self, x: torch.Tensor, row_sigma: torch.Tensor | None, pack: bool):
+        from . import _native
+
+        dev = self.shape.device
+        if dev.type != "cuda":
+            raise ValueError("shape-gain quantization requires a CUDA device")
+        x = torch.as_tensor(x, dtype=torch.float32, device=dev)
+        if x.shape[-1] != DIM:
+            raise ValueError(f"expected last dimension {DIM}, got {x.shape[-1]}")
+        shape = x.shape[:-1]
+        xs = x.reshape(-1, DIM).contiguous()
+        n = xs.shape[0]
+        idx = torch.empty(n, dtype=torch.long, device=dev)
+        pair = torch.empty(n, dtype=torch.long, device=dev)
+        score = torch.empty(n, dtype=torch.float32, device=dev)
+        gain = None if pack else torch.empty(n, dtype=torch.int32, device=dev)
+        sig = None
         if row_sigma is not None:
-            g = g / row_sigma
-        return sidx, torch.bucketize(g.contiguous(), self.thresholds)
+            sig = torch.broadcast_to(torch.as_tensor(row_sigma, dtype=torch.float32, device=dev),
+                                     shape).reshape(-1).contiguous()
+        with torch.cuda.device(dev):
+            self.shape._book().quantize_gain(
+                xs.data_ptr(), n, idx.data_ptr(), pair.data_ptr(), score.data_ptr(), self.thresholds.data_ptr(),
+                self.gain_bits, sig.data_ptr() if sig is not None else None, 1,
+                gain.data_ptr() if gain is not None else None, pack, torch.cuda.current_stream().cuda_stream)
+        return idx.reshape(shape), (gain.reshape(shape) if gain is not None else None)
 
     def dequantize_parts(self, sidx: torch.Tensor, gidx: torch.Tensor,
                          row_sigma: torch.Tensor | None = None) -> torch.Tensor:
-        g = self.levels[gidx.to(self.shape.device)]
+        g = self.levels[gidx.to(device=self.shape.device, dtype=torch.long)]
         if row_sigma is not None:
             g = g * row_sigma
         return self.shape.dequantize(sidx.to(self.shape.device)) * (g / self.norm).unsqueeze(-1)
@@ -193,8 +218,7 @@ class ShapeGainQuantizer:
         whose index exceeds 63 bits (3.0 bits/dim: 62 + 10) raise ValueError;
         use quantize_parts for them."""
         self._check_packable()
-        sidx, gidx = self.quantize_parts(x, row_sigma)
-        return sidx * (1 << self.gain_bits) + gidx
+        return self._run(x, row_sigma, pack=True)[0]
 
     def dequantize(self, indices: torch.Tensor, row_sigma: torch.Tensor | None = None) -> torch.Tensor:
         self._check_packable()

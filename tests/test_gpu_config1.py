@@ -61,15 +61,14 @@ def test_every_shape_index_and_gain_code_2_bits(workload):
     assert (sg.shell, sg.bits) == (11, 48)
     sidx, gidx = sg.quantize_parts(x.cuda())
     assert int((sidx.cpu().numpy() != shape).sum()) == 0
-    # gain index: the least-squares gain <x, y/|y|> of the oracle's codeword
-    # in fp64, coded with the same thresholds; the GPU computes it in fp32,
-    # so it may only differ where the gain lies within 1e-5 of a threshold
-    y = oracle_book(11, 11).codeword_batch(shape, threads=0).astype(np.float64)
-    g = (x.numpy().astype(np.float64) * y).sum(1) / np.linalg.norm(y, axis=1)
-    thr = sg.thresholds.cpu().numpy().astype(np.float64)
-    want = np.searchsorted(thr, g, side="left")
-    diff = gidx.cpu().numpy() != want
-    near = np.min(np.abs(g[:, None] - thr[None, :]), axis=1) < 1e-5
-    assert not np.any(diff & ~near)
+    # gain code: the reference's compensated fp64 projection <x, y> over
+    # |y| = sqrt(16 * 11), against the fp64 thresholds: exactly the kernel's
+    from oracle.oracle import ref_projection
+
+    y = oracle_book(11, 11).codeword_batch(shape, threads=0)
+    xd = x.numpy().astype(np.float64)
+    g = np.array([ref_projection(xd[i], y[i]) for i in range(N)]) / np.sqrt(16.0 * 11)
+    want = np.searchsorted(sg.thresholds.cpu().numpy(), g, side="left")
+    np.testing.assert_array_equal(gidx.cpu().numpy(), want)
     sqnr = _sqnr_db(x, sg.dequantize_parts(sidx, gidx))
     assert 10.5 < sqnr < 11.5  # measured 10.9 dB at this rate

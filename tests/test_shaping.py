@@ -87,6 +87,24 @@ def test_gpu_shape_gain_roundtrip():
     assert mse < 0.2  # 2 bits/dim on a unit Gaussian
 
 
+def expected_gain(book, sg, x, shape_idx, sigma=None):
+    """Gain codes from the oracle's codewords: the reference's fp64
+    projection <x, y> (CPython's compensated sum, restated by the oracle)
+    over |y| = sqrt(16 shell), divided by sigma, counted against the
+    thresholds."""
+    from oracle.oracle import ref_projection
+
+    thr = sg.thresholds.cpu().numpy()
+    out = []
+    for i, s in enumerate(shape_idx):
+        y = np.asarray(book.codeword(int(s)), dtype=np.int32)
+        g = ref_projection(x[i].astype(np.float64), y) / np.sqrt(16.0 * sg.shell)
+        if sigma is not None:
+            g = g / np.float64(np.float32(sigma[i]))
+        out.append(int(np.searchsorted(thr, g, side="left")))
+    return np.asarray(out, dtype=np.int32)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("rate", [1.0, 1.5, 2.0, 2.5, 3.0])
 def test_gpu_shape_gain_every_rate_matches_oracle(rate):
@@ -104,6 +122,12 @@ def test_gpu_shape_gain_every_rate_matches_oracle(rate):
     s2, g2 = sg.quantize_parts(x.cuda())
     assert torch.equal(s2.cpu(), torch.from_numpy(ref))
     assert int(g2.min()) >= 0 and int(g2.max()) < (1 << sg.gain_bits)
+    # the gain code: <x, y> / |y| with the reference's compensated fp64
+    # projection, coded against the fp64 thresholds, exactly
+    np.testing.assert_array_equal(g2.cpu().numpy(), expected_gain(book, sg, x.numpy(), ref))
+    sigma = torch.rand(48, generator=torch.Generator().manual_seed(3)) + 0.5
+    _, g3 = sg.quantize_parts(x.cuda(), row_sigma=sigma.cuda())
+    np.testing.assert_array_equal(g3.cpu().numpy(), expected_gain(book, sg, x.numpy(), ref, sigma.numpy()))
     recon = sg.dequantize_parts(s2, g2)
     assert recon.shape == x.shape and bool(torch.isfinite(recon).all())
     if sg.bits <= 63:
