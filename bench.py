@@ -400,8 +400,9 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
 
 def rate_sweep_bench(q, x, device, stream, args) -> dict:
     """Shape-gain quantization of the same N(0,1) blocks at 1.0 ... 3.0
-    bits/dim (single shell + chi(24)-matched gain code, shaping.rate_split)
-    and the spherical-shaping variant at 2 bits/dim (shells 2..13 ball, global
+    bits/dim (single shell + chi(24)-matched gain code, shaping.rate_split),
+    the multi-shell shape-gain variant at 1.5 and 2.0 bits/dim (shells 2..5 and
+    2..10 by correlation per unit norm) and the spherical-shaping variant at 2 bits/dim (shells 2..13 ball, global
     beta): blocks/s of the full quantize call (shape search, gain, index
     packing) on a sample of the batch, and SQNR in dB of the reconstruction.
     The sample is the first --sweep-rows blocks, cut so that one rate takes
@@ -442,6 +443,11 @@ def rate_sweep_bench(q, x, device, stream, args) -> dict:
         # (shape, gain) index pairs: 3.0 bits/dim needs 72 bits
         run(f"shape_gain_{rate}", sg.quantize_parts, lambda p, sg=sg: sg.dequantize_parts(*p), sg.bits / 24)
         out[f"shape_gain_{rate}"].update({"shell": sg.shell, "gain_bits": sg.gain_bits})
+        del sg
+    for rate in (1.5, 2.0):  # multi-shell shape (shells 2..m by correlation per unit norm) + gain
+        sg = ShapeGainQuantizer.for_rate(rate, device=device, multi_shell=True)
+        run(f"multi_shell_{rate}", sg.quantize_parts, lambda p, sg=sg: sg.dequantize_parts(*p), sg.bits / 24)
+        out[f"multi_shell_{rate}"].update({"shells": [sg.min_shell, sg.shell], "gain_bits": sg.gain_bits})
         del sg
     sph = SphericalShaping(q)
     run("spherical_2.0", sph.quantize, sph.dequantize, q.shape_bits / 24)

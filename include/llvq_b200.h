@@ -82,13 +82,19 @@ int llvq_quantize_ex(const llvq_codebook* cb, const float* x, int64_t n, int64_t
  * projection as the score, |y| = sqrt(16 shell)), divided by row_sigma[i /
  * blocks_per_row] when row_sigma (fp32, device) is not NULL, is coded as the
  * number of the 2^gain_bits - 1 ascending fp64 gain_thresholds (device) below
- * it.  gain_index[i] (int32, may be NULL) receives the code; with pack != 0,
- * indices[i] = shape << gain_bits | code (shape bits + gain_bits <= 63),
- * else the shape index.  Rows with NaN/Inf: index -1, code -1.  Same
- * launches, scratch and stream rules as llvq_quantize. */
+ * it.  gain_index[i] (int32, may be NULL) receives the code; with
+ * LLVQ_GAIN_PACK in flags, indices[i] = shape << gain_bits | code (shape bits
+ * + gain_bits <= 63), else the shape index.  With LLVQ_GAIN_ANGULAR the shape
+ * is the multi-shell one: the codeword of largest <x, y> / |y| over all the
+ * codebook's shells (fp64, ties in the reference's loop order), which needs
+ * generated angular search code for the class list (else
+ * LLVQ_ERR_UNSUPPORTED); without it, the reference's nearest codeword.  Rows
+ * with NaN/Inf: index -1, code -1.  Same launches, scratch and stream rules as
+ * llvq_quantize. */
+enum { LLVQ_GAIN_PACK = 1, LLVQ_GAIN_ANGULAR = 2 };
 int llvq_quantize_gain(const llvq_codebook* cb, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
                        float* best_score, const double* gain_thresholds, int32_t gain_bits, const float* row_sigma,
-                       int64_t blocks_per_row, int32_t* gain_index, int32_t pack, void* stream);
+                       int64_t blocks_per_row, int32_t* gain_index, uint32_t flags, void* stream);
 
 /* Integer codewords [n,24] of indices [n].  Out-of-range indices give zero
  * rows and are counted into *error_count (device int, may be NULL).

@@ -29,6 +29,8 @@ OUT_F32 = 1
 OUT_F32_DOUBLE = 2
 OUT_BF16_ROWSCALE = 3
 FLAG_TABLE_DRIVEN = 1
+GAIN_PACK = 1
+GAIN_ANGULAR = 2
 
 # Every symbol the public header declares (checked by the CPU test suite).
 EXPORTS = (
@@ -62,7 +64,8 @@ def load() -> ctypes.CDLL:
             "llvq_codebook_info": (ctypes.c_int, [vp, P(i64), P(i32), P(i32), P(i32), P(i32)]),
             "llvq_quantize": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, vp]),
             "llvq_quantize_ex": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, ctypes.c_uint32, vp]),
-            "llvq_quantize_gain": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, vp, i32, vp, i64, vp, i32, vp]),
+            "llvq_quantize_gain": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, vp, i32, vp, i64, vp, ctypes.c_uint32,
+                                                  vp]),
             "llvq_dequantize_lattice": (ctypes.c_int, [vp, vp, i64, vp, vp, vp]),
             "llvq_dequantize": (ctypes.c_int, [vp, vp, i64, vp, i32, vp, vp]),
             "llvq_dequantize_bf16": (ctypes.c_int, [vp, vp, i64, vp, i64, vp, vp, vp]),
@@ -179,9 +182,10 @@ class NativeCodebook:
 
     def quantize_gain(self, x_ptr: int, n: int, idx_ptr: int, pair_ptr: int, score_ptr: int, thr_ptr: int,
                       gain_bits: int, sigma_ptr: int | None, blocks_per_row: int, gain_ptr: int | None, pack: bool,
-                      stream: int) -> None:
+                      stream: int, angular: bool = False) -> None:
+        flags = (GAIN_PACK if pack else 0) | (GAIN_ANGULAR if angular else 0)
         check(self._lib.llvq_quantize_gain(self.handle, x_ptr, n, idx_ptr, pair_ptr, score_ptr, thr_ptr, gain_bits,
-                                           sigma_ptr, blocks_per_row, gain_ptr, int(pack), stream),
+                                           sigma_ptr, blocks_per_row, gain_ptr, flags, stream),
               "llvq_quantize_gain")
 
     def dequantize_lattice(self, idx_ptr: int, n: int, out_ptr: int, err_ptr: int | None, stream: int) -> None:

@@ -33,6 +33,11 @@ INCLUDE = PKG.parent / "include"
 # Other codebooks run the table-driven chains.
 SPECS = (("m2_4", 2, 4), ("m2_13", 2, 13), ("s2", 2, 2), ("s5", 5, 5), ("s11", 11, 11), ("s13", 13, 13),
          ("s23", 23, 23), ("s32", 32, 32))
+# Angular specs: the multi-shell shape search of shape-gain quantization
+# (correlation per unit norm over shells 2..max): 2..4 for fast parity tests,
+# 2..5 (33 shape bits, 1.5 bits/dim with 3 gain bits) and 2..10 (44 shape
+# bits, 2 bits/dim with 4 gain bits).
+ANGULAR_SPECS = (("a2_4", 2, 4), ("a2_5", 2, 5), ("a2_10", 2, 10))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
@@ -47,7 +52,8 @@ def nvcc() -> str:
 
 
 def generate() -> None:
-    args = [sys.executable, str(CSRC / "gen_search.py"), str(GEN)] + [f"{n}:{lo}:{hi}" for n, lo, hi in SPECS]
+    args = [sys.executable, str(CSRC / "gen_search.py"), str(GEN)] + [f"{n}:{lo}:{hi}" for n, lo, hi in SPECS] + \
+        [f"{n}:{lo}:{hi}:a" for n, lo, hi in ANGULAR_SPECS]
     subprocess.run(args, check=True)
 
 

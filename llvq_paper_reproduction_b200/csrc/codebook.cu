@@ -295,8 +295,11 @@ int build(llvq::Codebook& cb, int32_t n, const int32_t* shell, const int32_t* pa
       same = e[0] == shell[k] && e[1] == parity[k] && std::equal(e + 2, e + 2 + kDim, leader + (size_t)k * kDim);
     }
     if (same) {
-      cb.spec = &specs[s];
-      break;
+      if (specs[s].angular) {
+        if (!cb.spec_ang) cb.spec_ang = &specs[s];
+      } else if (!cb.spec) {
+        cb.spec = &specs[s];
+      }
     }
   }
   return LLVQ_OK;
@@ -392,18 +395,18 @@ int upload(llvq::Codebook& cb, int device) {
   const size_t o_tseq = off; off = align256(off + kTailSeqs * sizeof(uint16_t));
   const TabHost& tb = cb.tab;
   const size_t o_tstate = off; off = align256(off + tb.state.size() * sizeof(uint4));
+  const size_t o_tcrec = off; off = align256(off + tb.crec.size() * sizeof(uint4));
   const size_t o_tentry = off; off = align256(off + tb.entry.size() * sizeof(uint4));
   const size_t o_tguide = off; off = align256(off + tb.guide.size() * sizeof(uint16_t));
   const size_t o_ttail = off; off = align256(off + tb.tail.size() * sizeof(unsigned long long));
-  const size_t o_tcls = off; off = align256(off + tb.cls.size() * sizeof(uint2));
   const size_t o_texp = off; off = align256(off + tb.expand.size() * sizeof(uint32_t));
   std::vector<unsigned char> host(off, 0);
   if (tb.ok) {
     std::memcpy(host.data() + o_tstate, tb.state.data(), tb.state.size() * sizeof(uint4));
+    std::memcpy(host.data() + o_tcrec, tb.crec.data(), tb.crec.size() * sizeof(uint4));
     std::memcpy(host.data() + o_tentry, tb.entry.data(), tb.entry.size() * sizeof(uint4));
     std::memcpy(host.data() + o_tguide, tb.guide.data(), tb.guide.size() * sizeof(uint16_t));
     std::memcpy(host.data() + o_ttail, tb.tail.data(), tb.tail.size() * sizeof(unsigned long long));
-    std::memcpy(host.data() + o_tcls, tb.cls.data(), tb.cls.size() * sizeof(uint2));
     std::memcpy(host.data() + o_texp, tb.expand.data(), tb.expand.size() * sizeof(uint32_t));
   }
   {
@@ -490,11 +493,12 @@ int upload(llvq::Codebook& cb, int device) {
   d.tab = TabView{};
   if (tb.ok) {
     d.tab.state = reinterpret_cast<const uint4*>(base + o_tstate);
+    d.tab.crec = reinterpret_cast<const uint4*>(base + o_tcrec);
     d.tab.entry = reinterpret_cast<const uint4*>(base + o_tentry);
     d.tab.guide = reinterpret_cast<const uint16_t*>(base + o_tguide);
     d.tab.tail = reinterpret_cast<const unsigned long long*>(base + o_ttail);
-    d.tab.cls = reinterpret_cast<const uint2*>(base + o_tcls);
     d.tab.expand = reinterpret_cast<const uint4*>(base + o_texp);
+    d.tab.n_states = (int)(tb.state.size() / 2);
     d.tab.max_jobs = tb.max_jobs;
   }
   std::copy(cb.weight_start, cb.weight_start + 25, d.weight_start);
@@ -575,8 +579,8 @@ int llvq_codebook_tables(const llvq_codebook* h, int32_t* tabulated, int64_t* ta
   const llvq::TabHost& t = h->cb.tab;
   if (tabulated) *tabulated = t.ok ? 1 : 0;
   if (table_bytes)
-    *table_bytes = (int64_t)(t.state.size() * 16 + t.entry.size() * 16 + t.guide.size() * 2 + t.tail.size() * 8 +
-                             t.cls.size() * 8 + t.expand.size() * 4);
+    *table_bytes = (int64_t)(t.state.size() * 16 + t.crec.size() * 16 + t.entry.size() * 16 + t.guide.size() * 2 +
+                             t.tail.size() * 8 + t.expand.size() * 4);
   if (max_lookups) *max_lookups = t.max_jobs;
   return LLVQ_OK;
 }
@@ -605,7 +609,8 @@ int llvq_quantize_ex(const llvq_codebook* h, const float* x, int64_t n, int64_t*
 
 int llvq_quantize_gain(const llvq_codebook* h, const float* x, int64_t n, int64_t* indices, int64_t* best_pair,
                        float* best_score, const double* gain_thresholds, int32_t gain_bits, const float* row_sigma,
-                       int64_t blocks_per_row, int32_t* gain_index, int32_t pack, void* stream) {
+                       int64_t blocks_per_row, int32_t* gain_index, uint32_t flags, void* stream) {
+  const bool pack = (flags & LLVQ_GAIN_PACK) != 0, angular = (flags & LLVQ_GAIN_ANGULAR) != 0;
   if (n < 0 || (n > 0 && (!x || !indices || !best_pair || !best_score || !gain_thresholds)))
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "bad quantize arguments");
   if (gain_bits < 1 || gain_bits > 16 || (row_sigma && blocks_per_row <= 0))
@@ -620,10 +625,13 @@ int llvq_quantize_gain(const llvq_codebook* h, const float* x, int64_t n, int64_
   gc.sigma = row_sigma;
   gc.bpr = row_sigma ? blocks_per_row : 1;
   gc.gain_out = gain_index;
-  gc.pack = pack != 0;
+  gc.pack = pack;
+  if (angular && !h->cb.spec_ang)
+    return fail(LLVQ_ERR_UNSUPPORTED, "no angular (multi-shell shape) search code for this class list");
   return on_device(h, [&] {
     return llvq::quantize_launch(h->cb, x, n, reinterpret_cast<long long*>(indices),
-                                 reinterpret_cast<long long*>(best_pair), best_score, (cudaStream_t)stream, false, gc);
+                                 reinterpret_cast<long long*>(best_pair), best_score, (cudaStream_t)stream, false, gc,
+                                 angular);
   });
 }
 
@@ -678,6 +686,22 @@ int gemm_impl(const llvq_codebook* h, llvq::IndexSource src, int64_t n_out, int6
     if (m <= llvq::kGemvMaxM)  // decoded in registers: no staging
       return llvq::gemv_decode_launch(h->cb, src, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
                                       (cudaStream_t)stream);
+    if (llvq::gemm_fused_ok(h->cb, m)) {  // decoded into shared memory: a small partial-sum workspace only
+      int sms = 0;
+      cudaError_t e = llvq::device_sms(&sms);
+      if (e != cudaSuccess) return e;
+      const int64_t bytes = llvq::gemm_fused_workspace_bytes(n_out, blocks_per_row, m, sms);
+      cudaMemPool_t pool;
+      e = llvq::gemm_staging_pool(&pool);
+      if (e != cudaSuccess) return e;
+      void* ws = nullptr;
+      e = cudaMallocFromPoolAsync(&ws, (size_t)bytes, pool, (cudaStream_t)stream);
+      if (e != cudaSuccess) return e;
+      e = llvq::gemm_fused_launch(h->cb, src, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y, error_flag, ws,
+                                  bytes, sms, (cudaStream_t)stream);
+      const cudaError_t ef = cudaFreeAsync(ws, (cudaStream_t)stream);
+      return e != cudaSuccess ? e : ef;
+    }
     // stream-ordered staging buffer from the library's pool, released on the
     // same stream after the GEMM
     const int64_t bytes = llvq::gemm_staging_bytes(n_out, blocks_per_row, kGemmStagingBudget);
@@ -775,6 +799,14 @@ int llvq_gemm_noalloc(const llvq_codebook* h, const int64_t* indices, int64_t n_
     void* staging = nullptr;
     cudaError_t e = llvq::noalloc_staging(&staging);  // first call on a device: loads the array's module
     if (e != cudaSuccess) return e;
+    if (llvq::gemm_fused_ok(h->cb, m)) {  // the fused path's partial sums fit the array: use it as workspace
+      int sms = 0;
+      e = llvq::device_sms(&sms);
+      if (e != cudaSuccess) return e;
+      if (llvq::gemm_fused_workspace_bytes(n_out, blocks_per_row, m, sms) <= llvq::kNoAllocStagingBytes)
+        return llvq::gemm_fused_launch(h->cb, {indices, 8}, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
+                                       error_flag, staging, llvq::kNoAllocStagingBytes, sms, (cudaStream_t)stream);
+    }
     return llvq::gemm_staged_launch(h->cb, {indices, 8}, n_out, blocks_per_row, row_scale_f16, a_bf16, m, k, y,
                                     error_flag, staging, llvq::kNoAllocStagingBytes, (cudaStream_t)stream);
   });

@@ -32,7 +32,6 @@ using u128 = unsigned __int128;
 constexpr int kTabMaxVals = 8;                    // value indices must fit a byte-permute selector
 constexpr size_t kTabMaxEntries = 1u << 24;       // search entries (16 B each)
 constexpr size_t kTabMaxTail = 3u << 23;          // tail entries (8 B each): at most 192 MiB
-constexpr uint32_t kTabMaxStateEntries = 1u << 16;  // guide slots hold 16-bit entry numbers
 
 u128 multinomial_counts(const int* c) {
   u128 out = 1;
@@ -120,12 +119,12 @@ struct Builder {
       int rem = 0;
       for (int j = 0; j < kTabMaxVals; ++j) rem += c[j];
       const u128 n = multinomial_counts(c);
-      if (n >> 58) return fail("a part has 2^58 or more orderings");
-      uint4 rec{0, 0, 0, 0};
+      if (n >> 46) return fail("a part has 2^46 or more orderings");
+      uint4 r0{0, 0, 0, 0}, r1{0, 0, 0, 0};
       if (rem <= kTabTail) {
         if (t.tail.size() + (size_t)n > kTabMaxTail) return fail("tail tables too large");
-        rec.x = (uint32_t)t.tail.size();
-        rec.w = kTabTailBit | (uint32_t)rem;
+        r0.x = (uint32_t)t.tail.size();
+        r0.z = kTabTailBit | (uint32_t)rem;
         tail_state(c, rem, 0, 0, t.tail);
       } else {
         const int h = std::min(kTabHead, rem - kTabTail);
@@ -133,36 +132,50 @@ struct Builder {
         u128 cursor = 0;
         search_state(c, h, 0, 0, cursor, pre);
         if (cursor != n) return fail("prefix counts do not add up");
-        if (pre.size() > kTabMaxStateEntries) return fail("a search state has too many prefixes");
+        if (pre.size() >= (size_t)kTabMaxStateEntries) return fail("a search state has too many prefixes");
         if (t.entry.size() + pre.size() > kTabMaxEntries) return fail("search tables too large");
         int lg = 0;
-        while ((1u << lg) < 2 * pre.size()) ++lg;
+        while ((1u << lg) < 4 * pre.size()) ++lg;
         const uint32_t slots = 1u << lg;
-        rec.x = (uint32_t)t.entry.size();
-        rec.y = (uint32_t)t.guide.size();
-        const float gn = (float)((double)slots / (double)(uint64_t)n);
-        std::memcpy(&rec.z, &gn, 4);
-        rec.w = (uint32_t)pre.size() | ((uint32_t)lg << 17) | ((uint32_t)h << 22);
+        if ((n * (u128)(slots + 1)) >> 63) return fail("guide slot arithmetic would overflow");
+        r0.x = (uint32_t)t.entry.size();
+        r0.y = (uint32_t)t.guide.size();
+        r0.z = (uint32_t)pre.size() | ((uint32_t)lg << 16) | ((uint32_t)h << 21);
+        const uint64_t n64 = (uint64_t)n;
+        const double gn = (double)slots / (double)n64;
+        uint64_t gbits;
+        std::memcpy(&gbits, &gn, 8);
+        r1 = make_uint4((uint32_t)n64, (uint32_t)(n64 >> 32), (uint32_t)gbits, (uint32_t)(gbits >> 32));
         for (const Prefix& p : pre)
           t.entry.push_back({(uint32_t)(uint64_t)p.start, (uint32_t)((uint64_t)p.start >> 32), p.next, p.nib});
-        size_t j = 0;
+        // slot g holds the ranks ceil(g N / G) .. ceil((g + 1) N / G) - 1
+        auto entry_of = [&](u128 rank) {
+          size_t lo = 0, hi = pre.size();
+          while (lo + 1 < hi) {
+            const size_t mid = (lo + hi) / 2;
+            if (pre[mid].start <= rank) lo = mid; else hi = mid;
+          }
+          return lo;
+        };
         for (uint32_t g = 0; g < slots; ++g) {
-          u128 lo = ((u128)g * n + slots - 1) / slots;  // ceil(g N / G)
-          if (lo >= n) lo = n - 1;
-          while (j + 1 < pre.size() && pre[j + 1].start <= lo) ++j;
-          t.guide.push_back((uint16_t)j);
+          const u128 first = ((u128)g * n + slots - 1) / slots;
+          const u128 next = ((u128)(g + 1) * n + slots - 1) / slots;
+          const size_t j = entry_of(first < n ? first : n - 1);
+          const bool ambiguous = next > first && entry_of(next - 1) != j;
+          t.guide.push_back((uint16_t)(j | (ambiguous ? kTabGuideAmbiguous : 0)));
         }
       }
-      t.state.push_back(rec);
+      t.state.push_back(r0);
+      t.state.push_back(r1);
     }
     // lookups to the end of a part from each state (children come later in
     // creation order, so walk backwards)
     depth.assign(keys.size(), 1);
     for (size_t s = keys.size(); s-- > 0;) {
-      const uint4& rec = t.state[s];
-      if (rec.w & kTabTailBit) continue;
+      const uint4& r0 = t.state[2 * s];
+      if (r0.z & kTabTailBit) continue;
       int d = 0;
-      for (uint32_t e = 0; e < (rec.w & 0x1FFFFu); ++e) d = std::max(d, depth[t.entry[rec.x + e].z]);
+      for (uint32_t e = 0; e < (r0.z & 0xFFFFu); ++e) d = std::max(d, depth[t.entry[r0.x + e].z]);
       depth[s] = 1 + d;
     }
     return true;
@@ -202,12 +215,12 @@ void nibble_spread(uint32_t m, uint32_t* out) {
   }
 }
 
-bool build_expand(const std::vector<uint32_t>& golay, std::vector<uint32_t>& out, std::string& why) {
+bool build_expand(const std::vector<uint32_t>& words, std::vector<uint32_t>& out, std::string& why) {
   out.assign((size_t)kNumGolay * kTabExpandWords, 0);
   uint32_t seed = 12345u;
   for (int gi = 0; gi < kNumGolay; ++gi) {
     uint32_t* e = out.data() + (size_t)gi * kTabExpandWords;
-    const uint32_t w = golay[gi];
+    const uint32_t w = words[gi];
     uint32_t mva[5], mvb[5], ma[3], mb[3], m0[3];
     expand_masks(w, mva);
     expand_masks(~w & kFull24, mvb);
@@ -260,29 +273,53 @@ bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
     return false;
   };
   const size_t n = cb.cls.size();
-  t.cls.resize(n);
-  std::vector<int> jobs(n, 0);
+  std::vector<uint2> parts(n);
   for (size_t k = 0; k < n; ++k) {
     const DevClass& c = cb.cls[k];
     if (c.nv0 + c.nv1 > kTabMaxVals) return bad("a class has more than 8 distinct magnitudes");
     int a[kTabMaxVals] = {0}, z[kTabMaxVals] = {0};
     if (c.parity) {
       for (int j = 0; j < c.nv0; ++j) a[j] = c.m0[j];
-      t.cls[k] = make_uint2(b.get(a), kTabEnd);
+      parts[k] = make_uint2(b.get(a), kTabEnd);
     } else {
       for (int j = 0; j < c.nv1; ++j) a[j] = c.m1[j];
       for (int j = 0; j < c.nv0; ++j) z[j] = c.m0[j];
-      t.cls[k] = make_uint2(c.even_weight > 0 ? b.get(a) : kTabEnd, c.even_weight < kDim ? b.get(z) : kTabEnd);
+      parts[k] = make_uint2(c.even_weight > 0 ? b.get(a) : kTabEnd, c.even_weight < kDim ? b.get(z) : kTabEnd);
     }
   }
   if (!b.run()) return bad(b.why);
+  t.crec.assign(4 * n, uint4{0, 0, 0, 0});
   for (size_t k = 0; k < n; ++k) {
-    const uint2 s = t.cls[k];
-    jobs[k] = (s.x != kTabEnd ? b.depth[s.x] : 0) + (s.y != kTabEnd ? b.depth[s.y] : 0);
-    t.max_jobs = std::max(t.max_jobs, jobs[k]);
+    const DevClass& c = cb.cls[k];
+    const uint2 st = parts[k];
+    t.max_jobs = std::max(t.max_jobs, (st.x != kTabEnd ? b.depth[st.x] : 0) + (st.y != kTabEnd ? b.depth[st.y] : 0));
+    uint64_t vals = 0;
+    int d0 = 0;
+    if (c.parity) {
+      for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
+    } else {
+      d0 = c.nv0;
+      for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
+      for (int j = 0; j < c.nv1; ++j) vals |= (uint64_t)(uint8_t)c.v1[j] << (8 * (d0 + j));
+    }
+    const uint64_t start = (uint64_t)c.start, perm = c.perm_count;
+    const uint64_t mp = ~0ull / perm, mf = ~0ull / c.f1_perm;
+    const uint32_t meta = (uint32_t)c.parity | ((uint32_t)c.even_weight << 1) | ((uint32_t)c.sign_shift << 6) |
+                          ((uint32_t)d0 << 11) | ((uint32_t)c.required << 15);
+    uint4* r = t.crec.data() + 4 * k;
+    r[0] = make_uint4((uint32_t)start, (uint32_t)(start >> 32), (uint32_t)perm, (uint32_t)(perm >> 32));
+    r[1] = make_uint4((uint32_t)mp, (uint32_t)(mp >> 32), (uint32_t)mf, (uint32_t)(mf >> 32));
+    r[2] = make_uint4((uint32_t)vals, (uint32_t)(vals >> 32), (uint32_t)c.f1_perm, meta);
+    r[3] = make_uint4((uint32_t)(c.parity ? 0 : cb.weight_start[c.even_weight]), st.x, st.y, 0);
+  }
+  t.bucket.assign(kBuckets + 1, 0);
+  for (int bk = 0; bk <= kBuckets; ++bk) {  // owner class of each bucket's lowest index
+    const uint64_t lo = bucket_low(bk);
+    t.bucket[bk] = (uint16_t)(lo >= (uint64_t)cb.total ? n - 1
+                                                        : find_class(cb.class_start.data(), (int)n, (int64_t)lo));
   }
   std::string why;
-  if (!build_expand(cb.golay, t.expand, why)) return bad(why);
+  if (!build_expand(cb.wlist_word, t.expand, why)) return bad(why);
   t.ok = true;
   return true;
 }
@@ -311,53 +348,36 @@ const uint8_t* host_deposit4() {
 
 }  // namespace
 
-// Host decode of one index with the tables (the same tab_* code the kernels
-// run); false and zeros outside the codebook or for a bad sign rank.
-bool decode_index_tables_host(const Codebook& cb, int64_t v, int32_t* out) {
+TabCtx host_tab_ctx(const Codebook& cb) {
   const TabHost& t = cb.tab;
+  TabCtx tc{};
+  tc.srec = t.state.data();
+  tc.crec = t.crec.data();
+  tc.starts = cb.class_start.data();
+  tc.bucket = t.bucket.data();
+  tc.entry = t.entry.data();
+  tc.guide = t.guide.data();
+  tc.tail = t.tail.data();
+  tc.expand = reinterpret_cast<const uint4*>(t.expand.data());
+  tc.words = cb.wlist_word.data();
+  tc.golay = cb.golay.data();
+  tc.deposit4 = host_deposit4();
+  tc.n_classes = (int)cb.cls.size();
+  tc.max_jobs = t.max_jobs;
+  tc.total = cb.total;
+  return tc;
+}
+
+// Host decode of one index with the tables (the same tab_* code the kernels
+// run); false and zeros outside the codebook.
+bool decode_index_tables_host(const Codebook& cb, int64_t v, int32_t* out) {
   for (int d = 0; d < kDim; ++d) out[d] = 0;
-  if (!t.ok || v < 0 || v >= cb.total) return false;
-  const int k = find_class(cb.class_start.data(), (int)cb.cls.size(), v);
-  const DevClass& c = cb.cls[k];
-  const uint64_t local = (uint64_t)(v - c.start);
-  const uint64_t prank = local % c.perm_count, cur = local / c.perm_count;
-  TabView tv{};
-  tv.state = t.state.data();
-  tv.entry = t.entry.data();
-  tv.guide = t.guide.data();
-  tv.tail = t.tail.data();
-  tv.cls = t.cls.data();
-  tv.expand = reinterpret_cast<const uint4*>(t.expand.data());
-  tv.max_jobs = t.max_jobs;
-  const uint2 st = t.cls[k];
-  uint64_t vals = 0;
-  uint32_t word;
-  int word_lex, d0;
-  uint64_t sign = 0, ra, rb;
-  if (c.parity) {
-    word = cb.golay[cur];
-    word_lex = kNumGolay - 1;
-    d0 = 0;
-    ra = prank;
-    rb = 0;
-    for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
-  } else {
-    sign = cur & (c.sign_count - 1);
-    const uint64_t g = cur >> c.sign_shift;
-    word_lex = cb.by_weight[cb.weight_start[c.even_weight] + (int)g];
-    word = cb.golay[word_lex];
-    d0 = c.nv0;
-    ra = prank % c.f1_perm;
-    rb = prank / c.f1_perm;
-    for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
-    for (int j = 0; j < c.nv1; ++j) vals |= (uint64_t)(uint8_t)c.v1[j] << (8 * (d0 + j));
-  }
-  uint32_t mag[6];
-  tab_magnitudes(tv, st.x, ra, st.y, rb, word_lex, d0, vals, mag);
+  if (!cb.tab.ok) return false;
+  const TabCtx tc = host_tab_ctx(cb);
   int y[kDim];
-  if (!tab_signs(mag, word, c.parity != 0, sign, c.required, host_deposit4(), y)) return false;
+  const bool ok = tab_decode<false>(tc, v, y);
   for (int d = 0; d < kDim; ++d) out[d] = y[d];
-  return true;
+  return ok;
 }
 
 }  // namespace llvq

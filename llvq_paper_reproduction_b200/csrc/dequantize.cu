@@ -8,6 +8,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "llvq_decode.cuh"
@@ -18,23 +19,24 @@ namespace llvq {
 
 constexpr int kDeqThreads = 256;
 // 5 CTAs per SM (<= 48 registers, a few bytes spilled): +6% on the Llama-3-8B
-// dequant workload; the decode is issue-bound and latency-bound in turn.
+// dequant workload with the arithmetic decoder; the decode is issue-bound and
+// latency-bound in turn.
 constexpr int kDeqMinBlocks = 5;
 
-template <int KIND, bool TAB>
-__global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(IndexSource index, int64_t n,
-                                                              DevBook book, void* __restrict__ out,
-                                                              const uint16_t* __restrict__ row_scale,
-                                                              int64_t blocks_per_row, uint64_t magic_bpr,
-                                                              int* error_count) {
-  __shared__ DecodeShared sh;
-  decode_setup(book, sh);
-  __syncthreads();
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  int y[kDim];
-  const bool ok = decode_any<TAB>(load_index(index, i), book, sh, y);
-  if (!ok && error_count) atomicAdd(error_count, 1);
+// Decoder modes of the kernels: the arithmetic unranking (no tables), the
+// table-driven decoder reading its class and state records from global
+// memory, or from a shared-memory copy (the usual case: a persistent grid
+// copies them once per CTA).
+enum { kModeArith = 0, kModeTabGlobal = 1, kModeTabShared = 2 };
+constexpr int kTabThreads = 512;   // persistent table-driven kernels: 2 CTAs of 512 threads per SM
+constexpr int kTabMinBlocks = 2;
+constexpr size_t kTabSmemBudget = 100 * 1024;
+
+// Output of one decoded block in every kind.
+template <int KIND>
+__device__ __forceinline__ void store_block(const int (&y)[kDim], int64_t i, void* __restrict__ out,
+                                            const uint16_t* __restrict__ row_scale, int64_t blocks_per_row,
+                                            uint64_t magic_bpr) {
   if constexpr (KIND == 0) {
     longlong2* o = reinterpret_cast<longlong2*>(static_cast<long long*>(out) + i * kDim);
 #pragma unroll
@@ -68,10 +70,62 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(Ind
   }
 }
 
+template <int KIND>
+__global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(IndexSource index, int64_t n,
+                                                              DevBook book, void* __restrict__ out,
+                                                              const uint16_t* __restrict__ row_scale,
+                                                              int64_t blocks_per_row, uint64_t magic_bpr,
+                                                              int* error_count) {
+  __shared__ DecodeShared sh;
+  decode_setup(book, sh);
+  __syncthreads();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int y[kDim];
+  const bool ok = decode_index(load_index(index, i), book, sh, y);
+  if (!ok && error_count) atomicAdd(error_count, 1);
+  store_block<KIND>(y, i, out, row_scale, blocks_per_row, magic_bpr);
+}
+
+// Table-driven dequantizer: a persistent grid; each CTA copies the class and
+// state records to shared memory once (MODE kModeTabShared) and then strides
+// over the indices.
+template <int KIND, int MODE>
+__global__ void __launch_bounds__(kTabThreads, kTabMinBlocks) dequant_tab_kernel(
+    IndexSource index, int64_t n, DevBook book, TabSmem L, void* __restrict__ out,
+    const uint16_t* __restrict__ row_scale, int64_t blocks_per_row, uint64_t magic_bpr, int* error_count) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  DecodeSharedBase& sh = *reinterpret_cast<DecodeSharedBase*>(dsm);
+  decode_setup_base(book, sh);
+  if constexpr (MODE == kModeTabShared) tab_smem_fill(book, dsm, L);
+  __syncthreads();
+  const TabCtx tc = tab_ctx<MODE == kModeTabShared>(book, sh, dsm, L);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int y[kDim];
+    const bool ok = tab_decode<MODE == kModeTabShared>(tc, load_index(index, i), y);
+    if (!ok && error_count) atomicAdd(error_count, 1);
+    store_block<KIND>(y, i, out, row_scale, blocks_per_row, magic_bpr);
+  }
+}
+
 // Weight staging for the large-batch GEMM: indices [rows, bpr] -> bf16
 // integer codewords [rows, ldw] (columns >= 24 * bpr zero), one thread per
 // (row, block) plus the padding.
-template <bool TAB>
+__device__ __forceinline__ void store_staged(const int (&y)[kDim], __nv_bfloat16* o, int b) {
+  uint4* dst = reinterpret_cast<uint4*>(o + b * kDim);
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+    uint32_t pk[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn((float)y[q * 8 + 2 * e], (float)y[q * 8 + 2 * e + 1]);
+      pk[e] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    dst[q] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+}
+
 __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(IndexSource index, int rows,
                                                                        int bpr, int ldw, DevBook book,
                                                                        __nv_bfloat16* __restrict__ out, uint64_t magic_per_row) {
@@ -86,35 +140,115 @@ __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(IndexSour
   __nv_bfloat16* o = out + (int64_t)r * ldw;
   if (b < bpr) {
     int y[kDim];
-    decode_any<TAB>(load_index(index, (int64_t)r * bpr + b), book, sh, y);
-    uint4* dst = reinterpret_cast<uint4*>(o + b * kDim);
-#pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      uint32_t pk[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat162 h = __floats2bfloat162_rn((float)y[q * 8 + 2 * e], (float)y[q * 8 + 2 * e + 1]);
-        pk[e] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-      dst[q] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
+    decode_index(load_index(index, (int64_t)r * bpr + b), book, sh, y);
+    store_staged(y, o, b);
   } else if (b == bpr) {
     for (int c = bpr * kDim; c < ldw; c += 8) *reinterpret_cast<uint4*>(o + c) = make_uint4(0, 0, 0, 0);
   }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kTabThreads, kTabMinBlocks) decode_rows_tab_kernel(
+    IndexSource index, int rows, int bpr, int ldw, DevBook book, TabSmem L, __nv_bfloat16* __restrict__ out,
+    uint64_t magic_per_row) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  DecodeSharedBase& sh = *reinterpret_cast<DecodeSharedBase*>(dsm);
+  decode_setup_base(book, sh);
+  if constexpr (MODE == kModeTabShared) tab_smem_fill(book, dsm, L);
+  __syncthreads();
+  const TabCtx tc = tab_ctx<MODE == kModeTabShared>(book, sh, dsm, L);
+  const int per_row = ldw / kDim + 1;
+  const int64_t total = (int64_t)rows * per_row, stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    uint64_t bq;
+    const int r = (int)div_magic((uint64_t)i, (uint64_t)per_row, magic_per_row, bq), b = (int)bq;
+    __nv_bfloat16* o = out + (int64_t)r * ldw;
+    if (b < bpr) {
+      int y[kDim];
+      tab_decode<MODE == kModeTabShared>(tc, load_index(index, (int64_t)r * bpr + b), y);
+      store_staged(y, o, b);
+    } else if (b == bpr) {
+      for (int c = bpr * kDim; c < ldw; c += 8) *reinterpret_cast<uint4*>(o + c) = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// Launch shape of the table-driven kernels for a codebook: the shared copy
+// when it fits, a persistent grid of at most `per_sm` CTAs per SM.
+struct TabLaunch {
+  int mode;
+  TabSmem L;
+  size_t smem;
+};
+
+TabLaunch tab_launch(const Codebook& cb) {
+  TabLaunch t;
+  t.L = tab_smem_layout((int)cb.cls.size(), cb.dev.tab.n_states, kTabSmemBudget);
+  t.mode = t.L.bytes ? kModeTabShared : kModeTabGlobal;
+  t.smem = t.L.bytes ? t.L.bytes : sizeof(DecodeSharedBase);
+  return t;
+}
+
+template <class K>
+static cudaError_t allow_smem(K kernel, size_t bytes) {
+  // above the 48 KB default: raise the kernel's limit (idempotent)
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTabSmemBudget);
+}
+
+static unsigned tab_grid(int64_t work) {
+  int sms = 0;
+  if (device_sms(&sms) != cudaSuccess || sms <= 0) sms = 148;
+  const int64_t blocks = (work + kTabThreads - 1) / kTabThreads;
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sms * kTabMinBlocks));
 }
 
 cudaError_t decode_rows_bf16_launch(const Codebook& cb, IndexSource index, int rows, int bpr, int ldw, void* out,
                                     cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const int64_t n = (int64_t)rows * (ldw / kDim + 1);
-  const unsigned grid = (unsigned)((n + kDeqThreads - 1) / kDeqThreads);
   const uint64_t magic = ~0ull / (uint64_t)(ldw / kDim + 1);
-  if (cb.dev.tab.state)
-    decode_rows_bf16_kernel<true><<<grid, kDeqThreads, 0, stream>>>(index, rows, bpr, ldw, cb.dev,
-                                                                     static_cast<__nv_bfloat16*>(out), magic);
-  else
-    decode_rows_bf16_kernel<false><<<grid, kDeqThreads, 0, stream>>>(index, rows, bpr, ldw, cb.dev,
-                                                                      static_cast<__nv_bfloat16*>(out), magic);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  if (cb.dev.tab.state) {
+    const TabLaunch t = tab_launch(cb);
+    const unsigned grid = tab_grid(n);
+    cudaError_t e;
+    if (t.mode == kModeTabShared) {
+      if ((e = allow_smem(decode_rows_tab_kernel<kModeTabShared>, t.smem)) != cudaSuccess) return e;
+      decode_rows_tab_kernel<kModeTabShared><<<grid, kTabThreads, t.smem, stream>>>(index, rows, bpr, ldw, cb.dev,
+                                                                                  t.L, o, magic);
+    } else {
+      decode_rows_tab_kernel<kModeTabGlobal><<<grid, kTabThreads, t.smem, stream>>>(index, rows, bpr, ldw, cb.dev,
+                                                                                  t.L, o, magic);
+    }
+  } else {
+    decode_rows_bf16_kernel<<<(unsigned)((n + kDeqThreads - 1) / kDeqThreads), kDeqThreads, 0, stream>>>(
+        index, rows, bpr, ldw, cb.dev, o, magic);
+  }
+  return cudaGetLastError();
+}
+
+template <int KIND>
+static cudaError_t dequantize_kind(const Codebook& cb, IndexSource index, int64_t n, void* out,
+                                   const uint16_t* row_scale, int64_t blocks_per_row, uint64_t magic_bpr,
+                                   int* error_count, cudaStream_t stream) {
+  if (cb.dev.tab.state) {
+    const TabLaunch t = tab_launch(cb);
+    const unsigned grid = tab_grid(n);
+    if (t.mode == kModeTabShared) {
+      const cudaError_t e = allow_smem(dequant_tab_kernel<KIND, kModeTabShared>, t.smem);
+      if (e != cudaSuccess) return e;
+      dequant_tab_kernel<KIND, kModeTabShared><<<grid, kTabThreads, t.smem, stream>>>(
+          index, n, cb.dev, t.L, out, row_scale, blocks_per_row, magic_bpr, error_count);
+    } else {
+      dequant_tab_kernel<KIND, kModeTabGlobal><<<grid, kTabThreads, t.smem, stream>>>(
+          index, n, cb.dev, t.L, out, row_scale, blocks_per_row, magic_bpr, error_count);
+    }
+  } else {
+    const unsigned blocks = (unsigned)((n + kDeqThreads - 1) / kDeqThreads);
+    dequant_kernel<KIND><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale, blocks_per_row,
+                                                             magic_bpr, error_count);
+  }
   return cudaGetLastError();
 }
 
@@ -122,23 +256,14 @@ cudaError_t dequantize_launch(const Codebook& cb, IndexSource index, int64_t n, 
                               const uint16_t* row_scale, int64_t blocks_per_row, int* error_count,
                               cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
-  const unsigned blocks = (unsigned)((n + kDeqThreads - 1) / kDeqThreads);
   const uint64_t magic_bpr = ~0ull / (uint64_t)(blocks_per_row > 0 ? blocks_per_row : 1);
-  const bool tab = cb.dev.tab.state != nullptr;
-#define LLVQ_DEQ(K)                                                                                            \
-  (tab ? dequant_kernel<K, true><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale,          \
-                                                                      blocks_per_row, magic_bpr, error_count)  \
-       : dequant_kernel<K, false><<<blocks, kDeqThreads, 0, stream>>>(index, n, cb.dev, out, row_scale,         \
-                                                                       blocks_per_row, magic_bpr, error_count))
   switch (kind) {
-    case 0: LLVQ_DEQ(0); break;
-    case 1: LLVQ_DEQ(1); break;
-    case 2: LLVQ_DEQ(2); break;
-    case 3: LLVQ_DEQ(3); break;
+    case 0: return dequantize_kind<0>(cb, index, n, out, row_scale, blocks_per_row, magic_bpr, error_count, stream);
+    case 1: return dequantize_kind<1>(cb, index, n, out, row_scale, blocks_per_row, magic_bpr, error_count, stream);
+    case 2: return dequantize_kind<2>(cb, index, n, out, row_scale, blocks_per_row, magic_bpr, error_count, stream);
+    case 3: return dequantize_kind<3>(cb, index, n, out, row_scale, blocks_per_row, magic_bpr, error_count, stream);
     default: return cudaErrorInvalidValue;
   }
-#undef LLVQ_DEQ
-  return cudaGetLastError();
 }
 
 // ------------------------------------------------------- packed indices

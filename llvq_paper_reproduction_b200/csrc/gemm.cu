@@ -287,6 +287,23 @@ cudaError_t gemm_staging_pool(cudaMemPool_t* pool) {
   return cudaSuccess;
 }
 
+// SM count of the current device, looked up once per device.
+cudaError_t device_sms(int* sms) {
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v <= 0) {
+    e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    cache[dev].store(v, std::memory_order_relaxed);
+  }
+  *sms = v;
+  return cudaSuccess;
+}
+
 int64_t gemm_staging_ldw(int64_t bpr) { return (24 * bpr + 63) / 64 * 64; }
 
 int64_t gemm_staging_bytes(int64_t n_out, int64_t bpr, int64_t budget) {

@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "llvq_decode.cuh"
@@ -23,6 +24,9 @@
 namespace llvq {
 
 constexpr int kGemvThreads = 256;  // 8 warps: 8 output rows per CTA
+
+constexpr int kGemvTabBlocks = 3;               // persistent table-driven grid: CTAs per SM
+constexpr size_t kGemvSmemBudget = 72 * 1024;  // shared copy of the records: 3 CTAs per SM
 
 // acc += dot(8 bf16 activations, w[0..7])
 __device__ __forceinline__ float dot8(uint4 v, const float* w, float acc) {
@@ -36,23 +40,20 @@ __device__ __forceinline__ float dot8(uint4 v, const float* w, float acc) {
   return acc;
 }
 
-template <int MB, bool TAB>
-__global__ void __launch_bounds__(kGemvThreads) gemv_decode_kernel(IndexSource index, int n_out, int bpr,
-                                                                    DevBook book, const uint16_t* __restrict__ rscale,
-                                                                    const __nv_bfloat16* __restrict__ a, int m, int k,
-                                                                    float* __restrict__ y) {
-  __shared__ DecodeShared sh;
-  decode_setup(book, sh);
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * (kGemvThreads / 32) + warp;
-  if (n >= n_out) return;  // whole warps only, after the block's one barrier
+// One output row n by one warp: lane l decodes blocks l, l + 32, ... of the
+// row (decode(v, w)), multiplies each by the matching activations of every
+// batch row in fp32, then a fixed shuffle tree adds the lanes.
+template <int MB, class Decode>
+__device__ __forceinline__ void gemv_row(IndexSource index, int n, int n_out, int bpr,
+                                         const uint16_t* __restrict__ rscale, const __nv_bfloat16* __restrict__ a,
+                                         int m, int k, float* __restrict__ y, Decode&& decode) {
+  const int lane = threadIdx.x & 31;
   float acc[MB];
 #pragma unroll
   for (int i = 0; i < MB; ++i) acc[i] = 0.f;
   for (int b = lane; b < bpr && 24 * b < k; b += 32) {
     int w[kDim];
-    decode_any<TAB>(load_index(index, (int64_t)n * bpr + b), book, sh, w);
+    decode(load_index(index, (int64_t)n * bpr + b), w);
     float wf[kDim];
 #pragma unroll
     for (int d = 0; d < kDim; ++d) wf[d] = (float)w[d];
@@ -82,26 +83,81 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_decode_kernel(IndexSource i
   }
 }
 
+// Arithmetic decoder (codebooks without tables): one warp per output row.
+template <int MB>
+__global__ void __launch_bounds__(kGemvThreads) gemv_decode_kernel(IndexSource index, int n_out, int bpr,
+                                                                    DevBook book, const uint16_t* __restrict__ rscale,
+                                                                    const __nv_bfloat16* __restrict__ a, int m, int k,
+                                                                    float* __restrict__ y) {
+  __shared__ DecodeShared sh;
+  decode_setup(book, sh);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  const int n = blockIdx.x * (kGemvThreads / 32) + warp;
+  if (n >= n_out) return;  // whole warps only, after the block's one barrier
+  gemv_row<MB>(index, n, n_out, bpr, rscale, a, m, k, y,
+               [&](int64_t v, int (&w)[kDim]) { decode_index(v, book, sh, w); });
+}
+
+// Table-driven decoder: a persistent grid; each CTA copies the class and
+// state records to shared memory once (MODE 2) and its warps then take
+// output rows in turn.
+template <int MB, int MODE>
+__global__ void __launch_bounds__(kGemvThreads) gemv_tab_kernel(IndexSource index, int n_out, int bpr, DevBook book,
+                                                                 TabSmem L, const uint16_t* __restrict__ rscale,
+                                                                 const __nv_bfloat16* __restrict__ a, int m, int k,
+                                                                 float* __restrict__ y) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  DecodeSharedBase& sh = *reinterpret_cast<DecodeSharedBase*>(dsm);
+  decode_setup_base(book, sh);
+  if constexpr (MODE == 2) tab_smem_fill(book, dsm, L);
+  __syncthreads();
+  const TabCtx tc = tab_ctx<MODE == 2>(book, sh, dsm, L);
+  const int warp = threadIdx.x >> 5, warps = kGemvThreads / 32;
+  for (int n = blockIdx.x * warps + warp; n < n_out; n += gridDim.x * warps)
+    gemv_row<MB>(index, n, n_out, bpr, rscale, a, m, k, y,
+                 [&](int64_t v, int (&w)[kDim]) { tab_decode<MODE == 2>(tc, v, w); });
+}
+
 cudaError_t gemv_decode_launch(const Codebook& cb, IndexSource idx, int64_t n_out, int64_t bpr,
                                const uint16_t* rscale, const void* a, int64_t m, int64_t k, float* y,
                                cudaStream_t stream) {
   if (m <= 0 || n_out <= 0) return cudaSuccess;
   if (m > kGemvMaxM) return cudaErrorInvalidValue;
-  const unsigned grid = (unsigned)((n_out + kGemvThreads / 32 - 1) / (kGemvThreads / 32));
+  const unsigned rows_grid = (unsigned)((n_out + kGemvThreads / 32 - 1) / (kGemvThreads / 32));
   const auto* ab = static_cast<const __nv_bfloat16*>(a);
   const int n = (int)n_out, b = (int)bpr, mm = (int)m, kk = (int)k;
-  const bool tab = cb.dev.tab.state != nullptr;
-#define LLVQ_GEMV(MB)                                                                                      \
-  (tab ? gemv_decode_kernel<MB, true><<<grid, kGemvThreads, 0, stream>>>(idx, n, b, cb.dev, rscale, ab, mm, \
-                                                                          kk, y)                           \
-       : gemv_decode_kernel<MB, false><<<grid, kGemvThreads, 0, stream>>>(idx, n, b, cb.dev, rscale, ab, mm, \
-                                                                           kk, y))
-  if (m == 1)
-    LLVQ_GEMV(1);
-  else if (m == 2)
-    LLVQ_GEMV(2);
-  else
-    LLVQ_GEMV(4);
+  if (!cb.dev.tab.state) {
+#define LLVQ_GEMV(MB) gemv_decode_kernel<MB><<<rows_grid, kGemvThreads, 0, stream>>>(idx, n, b, cb.dev, rscale, ab, mm, kk, y)
+    if (m == 1) LLVQ_GEMV(1);
+    else if (m == 2) LLVQ_GEMV(2);
+    else LLVQ_GEMV(4);
+#undef LLVQ_GEMV
+    return cudaGetLastError();
+  }
+  const TabSmem L = tab_smem_layout((int)cb.cls.size(), cb.dev.tab.n_states, kGemvSmemBudget);
+  const size_t smem = L.bytes ? L.bytes : sizeof(DecodeSharedBase);
+  int sms = 0;
+  cudaError_t e = device_sms(&sms);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = std::min<unsigned>(rows_grid, (unsigned)sms * kGemvTabBlocks);
+#define LLVQ_GEMV(MB, MODE)                                                                              \
+  do {                                                                                                   \
+    if (smem > 48 * 1024 &&                                                                              \
+        (e = cudaFuncSetAttribute(gemv_tab_kernel<MB, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                  (int)kGemvSmemBudget)) != cudaSuccess)                                 \
+      return e;                                                                                          \
+    gemv_tab_kernel<MB, MODE><<<grid, kGemvThreads, smem, stream>>>(idx, n, b, cb.dev, L, rscale, ab, mm, kk, y); \
+  } while (0)
+  if (L.bytes) {
+    if (m == 1) LLVQ_GEMV(1, 2);
+    else if (m == 2) LLVQ_GEMV(2, 2);
+    else LLVQ_GEMV(4, 2);
+  } else {
+    if (m == 1) LLVQ_GEMV(1, 1);
+    else if (m == 2) LLVQ_GEMV(2, 1);
+    else LLVQ_GEMV(4, 1);
+  }
 #undef LLVQ_GEMV
   return cudaGetLastError();
 }

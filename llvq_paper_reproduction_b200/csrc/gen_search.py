@@ -23,13 +23,22 @@ stay in registers.  The script also emits the window constants the kernel
 needs for its error bound and a signature the host matches against a runtime
 class list.
 
-Usage:  python gen_search.py OUT.cuh NAME:MIN_SHELL:MAX_SHELL [...]
+Angular specs (NAME:MIN:MAX:a) score the multi-shell shape of shape-gain
+quantization instead: the correlation per unit norm, proj / sqrt(shell)
+(no shell offset), so every coefficient of a shell is divided by
+sqrt(shell) (rounded to fp32) and the chains start at zero.  All classes of
+one shell share the factor, so the per-shell tries stay as they are.
+
+Usage:  python gen_search.py OUT.cuh NAME:MIN_SHELL:MAX_SHELL[:a] [...]
 """
 from __future__ import annotations
 
+import math
 import sys
 from collections import Counter
 from pathlib import Path
+
+import numpy as np
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent))
@@ -108,27 +117,44 @@ def term_bound(term):
     return 1 if arr.startswith("P") else idx
 
 
-def window_constants(classes, chains):
+def shell_scale(shell, angular):
+    """The factor an angular spec multiplies a shell's coefficients by
+    (1/sqrt(shell), rounded to fp32), or 1."""
+    return float(np.float32(1.0 / math.sqrt(shell))) if angular else 1.0
+
+
+def scaled(coef, shell, angular):
+    return float(np.float32(coef * shell_scale(shell, angular))) if angular else float(coef)
+
+
+def window_constants(classes, chains, angular=False):
     """L1max, MG = max m*(G+2), AM = max sum_j sum_{i<=j} |c_i|*bound_i over
-    the FFMA chain each class issues (in emitted order)."""
+    the FFMA chain each class issues (in emitted order).  Angular specs have
+    no shell offset (MG = 0) and round every coefficient once more, so AM
+    also takes sum_i |c_i|*bound_i (bounds in units of 2^Q; the kernel
+    multiplies AM by 2^-24 * 2^Q)."""
     l1max = mg = am = 0
     for c, chain in zip(classes, chains):
         l1max = max(l1max, sum(c.leader))
         acc = total = 0
         for t in chain:
-            acc += abs(t[1]) * term_bound(t)
+            acc += abs(scaled(t[1], c.shell, angular)) * term_bound(t)
             total += acc
-        mg = max(mg, c.shell * (len(chain) + 2))
+        if angular:
+            total += acc  # coefficient rounding: sum_i |c_i| bound_i
+        else:
+            mg = max(mg, c.shell * (len(chain) + 2))
         am = max(am, total)
-    return l1max, mg, am
+    return l1max, mg, int(math.ceil(am))
 
 
 class _Emitter:
     """DFS over the prefix trie of FFMA chains, with 3-input max folding."""
 
-    def __init__(self, min_shell, cands):
+    def __init__(self, min_shell, cands, angular=False):
         self.min_shell = min_shell
         self.cands = cands
+        self.angular = angular
         self.lines = []
         self.tmp = 0
         self.pending = False
@@ -152,21 +178,22 @@ class _Emitter:
                 node = node["kids"].setdefault(t, {"kids": {}, "ends": []})
             node["ends"].append(k)
 
-        def visit(node, parent, indent):
+        def visit(node, parent, indent, shell):
             for term, child in node["kids"].items():
                 arr, coef, idx = term
                 self.tmp += 1
                 name = f"t{self.tmp}"
                 operand = arr if arr.startswith("P") else f"{arr}[{idx}]"
-                self.lines.append(f"{indent}{{ const float {name} = fmaf({float(coef)!r}f, {operand}, {parent});")
+                c = scaled(coef, shell, self.angular)
+                self.lines.append(f"{indent}{{ const float {name} = fmaf({c!r}f, {operand}, {parent});")
                 for k in child["ends"]:
                     self.leaf(k, name, indent + "  ")
-                visit(child, name, indent + "  ")
+                visit(child, name, indent + "  ", shell)
                 self.lines.append(f"{indent}}}")
 
         for shell, root in trie.items():
             assert not root["ends"]
-            visit(root, f"nmk[{shell - self.min_shell}]", "    ")
+            visit(root, "0.0f" if self.angular else f"nmk[{shell - self.min_shell}]", "    ", shell)
         if not self.cands and self.pending:
             self.lines.append("    b = fmaxf(b, pend);")
             self.pending = False
@@ -209,7 +236,7 @@ def ffma_per_word(classes, chains):
     return total / sum(WORDS_BY_WEIGHT.values())
 
 
-def emit_spec(name, classes):
+def emit_spec(name, classes, angular=False):
     min_shell = min(c.shell for c in classes)
     max_shell = max(c.shell for c in classes)
     chains = ordered_chains(classes)
@@ -218,7 +245,7 @@ def emit_spec(name, classes):
         (256, 3) if fpw <= LARGE_CODE_FFMA_PER_WORD else (512, 1)
     lines = []
     L = lines.append
-    l1max, mg, am = window_constants(classes, chains)
+    l1max, mg, am = window_constants(classes, chains, angular)
     r0max = {w: 0 for w in WEIGHTS}
     has_w = {w: False for w in WEIGHTS}
     for c in classes:
@@ -235,6 +262,7 @@ def emit_spec(name, classes):
     L(f"  static constexpr int kWinMG = {mg};")
     L(f"  static constexpr int kWinAM = {am};")
     L(f"  static constexpr bool kHasOdd = {'true' if has_odd else 'false'};")
+    L(f"  static constexpr bool kAngular = {'true' if angular else 'false'};")
     L(f"  static constexpr int kCtaThreads = {threads};")
     L(f"  static constexpr int kCtaMinBlocks = {min_blocks};")
     L(f"  static constexpr bool kCtaRealign = {'true' if threads > 128 else 'false'};")
@@ -253,7 +281,7 @@ def emit_spec(name, classes):
         return out
 
     L("  __device__ __forceinline__ static float odd_max(const float (&R)[25], const float* nmk) {")
-    body = _Emitter(min_shell, False).run(items(1))
+    body = _Emitter(min_shell, False, angular).run(items(1))
     L("    float b = -INFINITY;" + (" float pend;" if body else ""))
     lines.extend(body)
     L("    (void)R; (void)nmk;")
@@ -261,13 +289,13 @@ def emit_spec(name, classes):
     L("  }")
     L("  template <class F>")
     L("  __device__ __forceinline__ static void odd_cands(const float (&R)[25], const float* nmk, float thr, F&& f) {")
-    lines.extend(_Emitter(min_shell, True).run(items(1)))
+    lines.extend(_Emitter(min_shell, True, angular).run(items(1)))
     L("    (void)R; (void)nmk; (void)thr; (void)f;")
     L("  }")
     for w in WEIGHTS:
         L(f"  __device__ __forceinline__ static float even_max_w{w}(const float (&R0)[25], const float (&R1)[25], "
           f"float P0, float P1, const float* nmk) {{")
-        body = _Emitter(min_shell, False).run(items(0, w))
+        body = _Emitter(min_shell, False, angular).run(items(0, w))
         L("    float b = -INFINITY;" + (" float pend;" if body else ""))
         lines.extend(body)
         L("    (void)R0; (void)R1; (void)P0; (void)P1; (void)nmk;")
@@ -276,7 +304,7 @@ def emit_spec(name, classes):
         L("  template <class F>")
         L(f"  __device__ __forceinline__ static void even_cands_w{w}(const float (&R0)[25], const float (&R1)[25], "
           f"float P0, float P1, const float* nmk, float thr, F&& f) {{")
-        lines.extend(_Emitter(min_shell, True).run(items(0, w)))
+        lines.extend(_Emitter(min_shell, True, angular).run(items(0, w)))
         L("    (void)R0; (void)R1; (void)P0; (void)P1; (void)nmk; (void)thr; (void)f;")
         L("  }")
     L("};")
@@ -291,14 +319,14 @@ def main(argv):
     out = Path(argv[1])
     specs = []
     for arg in argv[2:]:
-        name, lo, hi = arg.split(":")
-        specs.append((name, int(lo), int(hi)))
+        parts = arg.split(":")
+        specs.append((parts[0], int(parts[1]), int(parts[2]), len(parts) > 3 and parts[3] == "a"))
     lines = ["// Generated by gen_search.py from the codebook class lists -- do not edit.",
              "#pragma once", "#include <cmath>", "namespace llvq {", "namespace gen {"]
-    for name, lo, hi in specs:
-        lines += emit_spec(name, codebook_classes(hi, min_shell=lo))
+    for name, lo, hi, angular in specs:
+        lines += emit_spec(name, codebook_classes(hi, min_shell=lo), angular)
     lines += ["}  // namespace gen", "}  // namespace llvq", ""]
-    lines.append("#define LLVQ_FOR_EACH_SPEC(X) " + " ".join(f"X({name})" for name, _, _ in specs))
+    lines.append("#define LLVQ_FOR_EACH_SPEC(X) " + " ".join(f"X({name})" for name, _, _, _ in specs))
     text = "\n".join(lines) + "\n"
     if not out.exists() or out.read_text() != text:
         out.parent.mkdir(parents=True, exist_ok=True)

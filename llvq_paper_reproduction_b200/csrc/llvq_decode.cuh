@@ -53,17 +53,24 @@ constexpr int kMaxSmemClasses = 1024;
 constexpr int kDecodeThreads = 256;  // blocks up to this size get per-thread rows
 constexpr int kRowWords = 7;         // 24 magnitude bytes per thread; a 28-byte stride reads without bank conflicts
 
-struct DecodeShared {
+// What both decoders keep in shared memory: the class starts (binary
+// search) and the sign-deposit table.
+struct DecodeSharedBase {
   int64_t starts[kMaxSmemClasses];
+  uint8_t deposit4[256];  // [m * 16 + s]: the low popc(m) bits of s placed on the set bits of m, in order
+};
+
+// The arithmetic decoder's shared memory: the base plus division constants
+// and per-thread magnitude rows.
+struct DecodeShared : DecodeSharedBase {
   uint64_t inv[kDim + 1];   // inverse of the odd part of d modulo 2^64
   uint32_t shift[kDim + 1]; // trailing zeros of d
   uint2 div32[kDim + 1];    // {inverse of the odd part of d modulo 2^32, trailing zeros of d}
   uint32_t rows[kDecodeThreads * kRowWords];  // each thread's codeword magnitudes, by position
-  uint8_t deposit4[256];  // [m * 16 + s]: the low popc(m) bits of s placed on the set bits of m, in order
 };
 
-// Fill the shared tables (call with the whole block, then __syncthreads()).
-__device__ __forceinline__ void decode_setup(const DevBook& book, DecodeShared& sh) {
+// Fill the base tables (call with the whole block, then __syncthreads()).
+__device__ __forceinline__ void decode_setup_base(const DevBook& book, DecodeSharedBase& sh) {
   if (book.n_classes <= kMaxSmemClasses)
     for (int k = threadIdx.x; k < book.n_classes; k += blockDim.x) sh.starts[k] = book.class_start[k];
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
@@ -76,6 +83,11 @@ __device__ __forceinline__ void decode_setup(const DevBook& book, DecodeShared& 
       }
     sh.deposit4[i] = (uint8_t)dep;
   }
+}
+
+// Fill the shared tables (call with the whole block, then __syncthreads()).
+__device__ __forceinline__ void decode_setup(const DevBook& book, DecodeShared& sh) {
+  decode_setup_base(book, sh);
   if (threadIdx.x <= kDim && threadIdx.x > 0) {
     const uint32_t d = threadIdx.x, s = __ffs(d) - 1;
     sh.shift[d] = s;
@@ -531,64 +543,55 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
   return ok;
 }
 
-// Integer codeword of index v with the table-driven decoder (llvq_tables.cuh):
-// class, record and the class-local split as in decode_index, then a part's
-// sequence from at most three table lookups per part instead of one
-// unranking step per coordinate.  false and zeros outside the codebook.
-__device__ __forceinline__ bool decode_index_tab(int64_t v, const DevBook& book, const DecodeShared& sh,
-                                                 int (&y)[kDim]) {
-  if (!(v >= 0 && v < book.total)) {
-#pragma unroll
-    for (int d = 0; d < kDim; ++d) y[d] = 0;
-    return false;
-  }
-  const int k = find_class_bucketed(book, book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start, v);
-  const uint4* rp = reinterpret_cast<const uint4*>(book.dcls + k);
-  const uint4 w0 = __ldg(rp), w1 = __ldg(rp + 1), w2 = __ldg(rp + 2), w3 = __ldg(rp + 3), w4 = __ldg(rp + 4);
-  const uint2 st = __ldg(book.tab.cls + k);
-  auto u64 = [](uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; };
-  const uint64_t start = u64(w0.x, w0.y), perm = u64(w0.z, w0.w), magic_perm = u64(w1.x, w1.y);
-  const uint32_t f1p = w2.x, meta = w2.y, gbase = w2.z;
-  const uint64_t magic_f1 = u64(w3.x, w3.y), pv0 = u64(w3.z, w3.w), pv1 = u64(w4.z, w4.w);
-  const bool odd = meta & 1;
-  const int sshift = (meta >> 6) & 31;
-  uint64_t prank;
-  const uint64_t cur = div_magic((uint64_t)v - start, perm, magic_perm, prank);
-  uint32_t word;
-  int word_lex, d0;
-  uint64_t sign = 0, ra, rb = 0, vals;
-  if (odd) {
-    word = __ldg(book.golay + (int)cur);
-    word_lex = kNumGolay - 1;  // part A covers every position
-    d0 = 0;
-    ra = prank;
-    vals = pv0;
-  } else {
-    sign = cur & ((1ull << sshift) - 1);
-    word_lex = __ldg(book.by_weight + gbase + (int)(cur >> sshift));
-    word = __ldg(book.golay + word_lex);
-    uint64_t r1;
-    rb = div_magic(prank, f1p, magic_f1, r1);
-    ra = r1;
-    d0 = (int)((meta >> 11) & 15u);
-    vals = pv0 | (d0 < 8 ? pv1 << (8 * d0) : 0ull);
-  }
-  uint32_t mag[6];
-  tab_magnitudes(book.tab, st.x, ra, st.y, rb, word_lex, d0, vals, mag);
-  const bool ok = tab_signs(mag, word, odd, sign, (int)((meta >> 19) & 1u), sh.deposit4, y);
-  if (!ok) {
-#pragma unroll
-    for (int d = 0; d < kDim; ++d) y[d] = 0;
-  }
-  return ok;
+// Shared-memory copy of a codebook's small table-driven decoder tables:
+// class records (64 B each) and state records (32 B each), after the
+// DecodeSharedBase block (class starts and deposit table).  Offsets in bytes from the start of dynamic
+// shared memory; bytes == 0 when the copy would not fit (the decoder then
+// reads the records from global memory).
+struct TabSmem {
+  uint32_t crec, srec, bytes;
+};
+
+inline TabSmem tab_smem_layout(int n_classes, int n_states, size_t budget) {
+  TabSmem L{};
+  const size_t base = (sizeof(DecodeSharedBase) + 15) / 16 * 16;
+  const size_t crec = base, srec = crec + (size_t)n_classes * 64, end = srec + (size_t)n_states * 32;
+  if (n_classes > kMaxSmemClasses || end > budget) return L;
+  L.crec = (uint32_t)crec;
+  L.srec = (uint32_t)srec;
+  L.bytes = (uint32_t)end;
+  return L;
 }
 
-// The codebook's decoder: table-driven when its tables exist (TAB, decided
-// per launch), else the arithmetic unranking.
-template <bool TAB>
-__device__ __forceinline__ bool decode_any(int64_t v, const DevBook& book, DecodeShared& sh, int (&y)[kDim]) {
-  if constexpr (TAB) return decode_index_tab(v, book, sh, y);
-  else return decode_index(v, book, sh, y);
+// Fill the shared copy (whole block; call __syncthreads() afterwards).
+__device__ __forceinline__ void tab_smem_fill(const DevBook& book, uint8_t* smem, const TabSmem& L) {
+  uint4* crec = reinterpret_cast<uint4*>(smem + L.crec);
+  uint4* srec = reinterpret_cast<uint4*>(smem + L.srec);
+  for (int i = threadIdx.x; i < 4 * book.n_classes; i += blockDim.x) crec[i] = __ldg(book.tab.crec + i);
+  for (int i = threadIdx.x; i < 2 * book.tab.n_states; i += blockDim.x) srec[i] = __ldg(book.tab.state + i);
+}
+
+// The decoder's view of the tables: records from the shared copy (SMEM) or
+// from global memory; class starts and the deposit table from DecodeShared.
+template <bool SMEM>
+__device__ __forceinline__ TabCtx tab_ctx(const DevBook& book, const DecodeSharedBase& sh, const uint8_t* smem,
+                                          const TabSmem& L) {
+  TabCtx tc;
+  tc.srec = SMEM ? reinterpret_cast<const uint4*>(smem + L.srec) : book.tab.state;
+  tc.crec = SMEM ? reinterpret_cast<const uint4*>(smem + L.crec) : book.tab.crec;
+  tc.starts = book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start;
+  tc.bucket = book.bucket;
+  tc.entry = book.tab.entry;
+  tc.guide = book.tab.guide;
+  tc.tail = book.tab.tail;
+  tc.expand = book.tab.expand;
+  tc.words = book.wlist_word;
+  tc.golay = book.golay;
+  tc.deposit4 = sh.deposit4;
+  tc.n_classes = book.n_classes;
+  tc.max_jobs = book.tab.max_jobs;
+  tc.total = book.total;
+  return tc;
 }
 
 }  // namespace llvq

@@ -88,14 +88,16 @@ constexpr int kTailLen = 8;
 constexpr int kTailKeys = 9 * 9 * 9;
 constexpr int kTailSeqs = 1 << (2 * kTailLen);
 
-// Tables of the table-driven decoder (layout in llvq_tables.cuh).
+// Tables of the table-driven decoder in global memory (layout in
+// llvq_tables.cuh); state == nullptr when the codebook is not tabulated.
 struct TabView {
-  const uint4* state;
+  const uint4* state;      // 2 per state
+  const uint4* crec;       // 4 per class
   const uint4* entry;
   const uint16_t* guide;
   const unsigned long long* tail;
-  const uint2* cls;        // per class: {state of part A, state of part B}
-  const uint4* expand;     // per Golay word (lexicographic index): kTabExpandWords u32
+  const uint4* expand;     // per Golay word in weight order
+  int n_states;
   int max_jobs;            // lookups of the longest class (both parts)
 };
 

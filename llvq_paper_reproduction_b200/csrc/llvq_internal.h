@@ -37,6 +37,7 @@ struct SpecEntry {
   SearchLauncher launch;
   const char* name;
   float l1max, win_mg, win_am;
+  bool angular;  // scores proj / |y| (multi-shell shape of shape-gain) instead of the reference score
 };
 
 // Host copy of the table-driven decoder's tables (llvq_tables.cuh; built by
@@ -44,11 +45,13 @@ struct SpecEntry {
 // tabulate; the kernels then unrank arithmetically (llvq_decode.cuh).
 struct TabHost {
   bool ok = false;
-  std::vector<uint4> state, entry;
+  std::vector<uint4> state;            // 2 per state
+  std::vector<uint4> crec;             // 4 per class
+  std::vector<uint4> entry;
   std::vector<uint16_t> guide;
   std::vector<unsigned long long> tail;
-  std::vector<uint2> cls;
-  std::vector<uint32_t> expand;
+  std::vector<uint32_t> expand;        // per word in weight order
+  std::vector<uint16_t> bucket;        // index bucket -> class (host copy for the host decoder)
   int max_jobs = 0;
 };
 
@@ -70,6 +73,7 @@ struct Codebook {
   void* dev_alloc = nullptr;
   size_t dev_bytes = 0;
   const SpecEntry* spec = nullptr;     // generated search code for this class list, or null
+  const SpecEntry* spec_ang = nullptr; // generated angular (shape) search code for it, or null
   float rt_l1max = 0, rt_mg = 0, rt_am = 0;  // window constants of the table-driven chains
   TabHost tab;                         // table-driven decoder (host copy)
   std::string tab_why;                 // why the tables are off, when they are
@@ -83,7 +87,8 @@ bool decode_index_tables_host(const Codebook& cb, int64_t v, int32_t* out);
 const SpecEntry* spec_table(int* count);
 
 cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long long* index, long long* pair,
-                            float* score, cudaStream_t stream, bool force_runtime, const GainCode& gc = GainCode{});
+                            float* score, cudaStream_t stream, bool force_runtime, const GainCode& gc = GainCode{},
+                            bool angular = false);
 
 // Where a kernel reads its indices: int64 (bytes = 8) or packed little-endian
 // unsigned integers of 1..7 bytes, the all-ones value standing for an
@@ -128,6 +133,17 @@ constexpr int kGemvMaxM = 4;
 cudaError_t gemv_decode_launch(const Codebook& cb, IndexSource idx, int64_t n_out, int64_t bpr,
                                const uint16_t* rscale, const void* a, int64_t m, int64_t k, float* y,
                                cudaStream_t stream);
+
+// Fused dequant-GEMM (gemm_fused.cu) for 5 <= m <= 256 on codebooks with
+// decoder tables: weights decoded into shared memory, stream-K over (tile,
+// group) with a per-CTA partial-sum workspace of gemm_fused_workspace_bytes
+// and a fixup kernel (no device allocation inside).
+bool gemm_fused_ok(const Codebook& cb, int64_t m);
+int64_t gemm_fused_workspace_bytes(int64_t n_out, int64_t bpr, int64_t m, int sms);
+cudaError_t gemm_fused_launch(const Codebook& cb, IndexSource idx, int64_t n_out, int64_t bpr, const uint16_t* rscale,
+                              const void* a, int64_t m, int64_t k, float* y, int* error_flag, void* workspace,
+                              int64_t workspace_bytes, int sms, cudaStream_t stream);
+cudaError_t device_sms(int* sms);
 
 // Static staging for the no-allocation GEMM entry point: 16 MiB per device,
 // enough for one 128-row tile of rows up to 65536 columns.

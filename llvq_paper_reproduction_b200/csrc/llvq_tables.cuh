@@ -12,9 +12,10 @@
 //     in rank order, so the rest of the sequence is entry `rank`;
 //   * a search state lists the orderings of its next h positions (h at most
 //     kTabHead) in rank order, each with the rank of its first completion
-//     and the state it leaves; a guide table over rank / N, N the number of
-//     orderings of the state, finds the entry holding `rank` in one or two
-//     probes.
+//     and the state it leaves; a guide table over rank * G / N (N the number
+//     of orderings of the state, G a power of two, the slot computed exactly)
+//     names the entry holding the slot's first rank, and flags the slots that
+//     reach into a second entry (only those compare with the next entry).
 // A 24-position part is two searches and one tail; a 16-position part one
 // search and one tail; 12- and 8-position parts one tail.  Sequences are
 // nibble strings (value index j of the part in bits 4t..4t+3 for step t).
@@ -35,85 +36,130 @@ constexpr int kTabTail = 12;              // positions a tail state covers
 constexpr int kTabHead = 6;               // positions one search covers
 constexpr uint32_t kTabEnd = 0xFFFFFFFFu; // no state: the part is empty / finished
 constexpr int kTabExpandWords = 40;       // u32 per Golay word in the expand table
-
-// State record (uint4):
-//   tail:   x = first entry in `tail`, w = kTabTailBit | positions
-//   search: x = first entry in `entry`, y = first guide slot, z = fp32 bits of
-//           G / N (G guide slots, a power of two), w = entries | log2 G << 17
-//           | h << 22
-// Search entry (uint4): {start low, start high, next state, nibbles of the h
-// positions}.  Guide slot g: the entry holding rank ceil(g N / G).
 constexpr uint32_t kTabTailBit = 1u << 31;
+constexpr uint16_t kTabGuideAmbiguous = 0x8000;
+constexpr int kTabMaxStateEntries = 0x8000;  // entry numbers fit the guide's 15 bits
 
+// State record, two uint4:
+//   [0] tail:   x = first entry in `tail`, z = kTabTailBit | positions
+//       search: x = first entry in `entry`, y = first guide slot,
+//               z = entries | log2 G << 16 | h << 21
+//   [1] search: N (u64, x | y << 32), G / N as fp64 bits (z | w << 32)
+// Search entry (uint4): {start low, start high, next state, nibbles of the h
+// positions}.  Guide slot g (u16): the entry holding rank ceil(g N / G), with
+// kTabGuideAmbiguous set when ceil((g + 1) N / G) - 1 lies in a later entry.
+//
+// Class record, four uint4 (64 bytes):
+//   [0] start of the class (u64), permutation count (u64)
+//   [1] floor((2^64 - 1) / permutation count), floor((2^64 - 1) / f1 count)
+//   [2] values (u64: byte j = value j; even: the |v| = 0 mod 4 part's values,
+//       then the |v| = 2 mod 4 part's from byte d0 on), f1 count (u32), meta
+//   [3] first word of the class's weight group in weight order (u32), state of
+//       part A, state of part B, 0
+// meta: odd | word weight << 1 | sign shift << 6 | d0 << 11 | required << 15.
 // Part A is the odd class's only part or the even class's |v| = 2 (mod 4)
 // part on the word's positions; part B the even class's |v| = 0 (mod 4) part
 // on the other positions.
+//
+// Words are indexed in weight order (lexicographic inside a weight): an even
+// class's word is entry wbase + choice; every odd class uses entry 4095 (the
+// all-ones word: part A on every position) of the expand table.
 
 #if defined(__CUDA_ARCH__)
 template <class T>
-__device__ __forceinline__ T tab_ld(const T* p) { return __ldg(p); }
+__device__ __forceinline__ T tab_ldg(const T* p) { return __ldg(p); }
 __device__ __forceinline__ uint32_t tab_prmt(uint32_t a, uint32_t b, uint32_t s) { return __byte_perm(a, b, s); }
 __device__ __forceinline__ uint32_t tab_fshl(uint32_t lo, uint32_t hi, int s) { return __funnelshift_l(lo, hi, s); }
-__device__ __forceinline__ uint32_t tab_f2u(float f) { return __float2uint_rz(f); }
-__device__ __forceinline__ float tab_u2f(uint64_t v) { return __ull2float_rn(v); }
-__device__ __forceinline__ float tab_bits2f(uint32_t b) { return __uint_as_float(b); }
+__device__ __forceinline__ double tab_bits2d(uint32_t lo, uint32_t hi) {
+  return __hiloint2double((int)hi, (int)lo);
+}
+__device__ __forceinline__ uint64_t tab_mulhi(uint64_t a, uint64_t b) { return __umul64hi(a, b); }
+__device__ __forceinline__ int tab_popc(uint32_t v) { return __popc(v); }
+__device__ __forceinline__ int tab_msb(uint64_t u) { return 63 - __clzll((long long)u); }
 #else
 template <class T>
-inline T tab_ld(const T* p) { return *p; }
+inline T tab_ldg(const T* p) { return *p; }
 inline uint32_t tab_prmt(uint32_t a, uint32_t b, uint32_t s) {
   const uint64_t v = ((uint64_t)b << 32) | a;
   uint32_t out = 0;
   for (int i = 0; i < 4; ++i) out |= (uint32_t)((v >> (8 * ((s >> (4 * i)) & 7))) & 0xFF) << (8 * i);
   return out;
 }
-inline uint32_t tab_fshl(uint32_t lo, uint32_t hi, int s) {
-  return s ? (hi << s) | (lo >> (32 - s)) : hi;
+inline uint32_t tab_fshl(uint32_t lo, uint32_t hi, int s) { return s ? (hi << s) | (lo >> (32 - s)) : hi; }
+inline double tab_bits2d(uint32_t lo, uint32_t hi) {
+  const uint64_t b = ((uint64_t)hi << 32) | lo;
+  double d;
+  __builtin_memcpy(&d, &b, 8);
+  return d;
 }
-inline uint32_t tab_f2u(float f) { return (uint32_t)f; }
-inline float tab_u2f(uint64_t v) { return (float)v; }
-inline float tab_bits2f(uint32_t b) {
-  float f;
-  __builtin_memcpy(&f, &b, 4);
-  return f;
-}
+inline uint64_t tab_mulhi(uint64_t a, uint64_t b) { return (uint64_t)(((unsigned __int128)a * b) >> 64); }
+inline int tab_popc(uint32_t v) { return __builtin_popcount(v); }
+inline int tab_msb(uint64_t u) { return 63 - __builtin_clzll(u); }
 #endif
+
+LLVQ_HD uint64_t tab_u64(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+
+// Where the decoder reads its tables.  srec (state records) and crec (class
+// records) point to shared-memory copies (plain loads, SMEM) or to global
+// memory (read-only cache loads); starts and deposit4 are read with plain
+// loads (shared memory in the kernels); the rest is global memory.
+struct TabCtx {
+  const uint4* srec;          // 2 per state
+  const uint4* crec;          // 4 per class
+  const int64_t* starts;      // class starts (binary search)
+  const uint16_t* bucket;     // index bucket -> class (global)
+  const uint4* entry;
+  const uint16_t* guide;
+  const unsigned long long* tail;
+  const uint4* expand;        // kTabExpandWords u32 per word, weight order
+  const uint32_t* words;      // Golay words in weight order
+  const uint32_t* golay;      // Golay words in lexicographic order
+  const uint8_t* deposit4;    // [m * 16 + s]: the low popc(m) bits of s placed on the set bits of m
+  int n_classes;
+  int max_jobs;
+  int64_t total;
+};
+
+template <bool SMEM, class T>
+LLVQ_HD T tab_ldr(const T* p) {
+  if constexpr (SMEM) return *p;
+  else return tab_ldg(p);
+}
 
 // One lookup: from state s with rank r, the nibbles of the positions it
 // covers (`take` of them); s becomes the next state (kTabEnd after a tail).
-LLVQ_HD void tab_job(const TabView& tv, uint32_t& s, uint64_t& r, uint64_t& nib, int& take) {
-  const uint4 rec = tab_ld(tv.state + s);
-  if (rec.w & kTabTailBit) {
-    nib = tab_ld(tv.tail + rec.x + r);
-    take = (int)(rec.w & 31u);
+template <bool SMEM>
+LLVQ_HD void tab_job(const TabCtx& tc, uint32_t& s, uint64_t& r, uint64_t& nib, int& take) {
+  const uint4 r0 = tab_ldr<SMEM>(tc.srec + 2 * s);
+  if (r0.z & kTabTailBit) {
+    nib = tab_ldg(tc.tail + r0.x + r);
+    take = (int)(r0.z & 31u);
     s = kTabEnd;
     return;
   }
-  const uint32_t n = rec.w & 0x1FFFFu, lg = (rec.w >> 17) & 31u;
-  uint32_t g = tab_f2u(tab_u2f(r) * tab_bits2f(rec.z));
-  const uint32_t gmax = (1u << lg) - 1u;
-  g = g < gmax ? g : gmax;
-  const uint4* ent = tv.entry + rec.x;
-  uint32_t j = tab_ld(tv.guide + rec.y + g);
-  uint4 e = tab_ld(ent + j);
-  uint64_t st = ((uint64_t)e.y << 32) | e.x;
-  // the fp32 slot can be one too high: step back (entry 0 starts at 0)
-  while (st > r && j > 0) {
-    --j;
-    e = tab_ld(ent + j);
-    st = ((uint64_t)e.y << 32) | e.x;
+  const uint4 r1 = tab_ldr<SMEM>(tc.srec + 2 * s + 1);
+  const uint32_t n = r0.z & 0xFFFFu, lg = (r0.z >> 16) & 31u;
+  const uint64_t N = tab_u64(r1.x, r1.y), rg = r << lg;
+  // slot g = floor(r G / N): an fp64 estimate, corrected exactly (N (G + 1) < 2^64)
+  uint64_t g = (uint64_t)((double)r * tab_bits2d(r1.z, r1.w));
+  if ((g + 1) * N <= rg) ++g;
+  else if (g * N > rg) --g;
+  const uint32_t gv = tab_ldg(tc.guide + r0.y + (uint32_t)g);
+  const uint4* ent = tc.entry + r0.x;
+  uint32_t j = gv & 0x7FFFu;
+  uint4 e = tab_ldg(ent + j);
+  if (gv & kTabGuideAmbiguous) {
+    while (j + 1 < n) {
+      const uint2 nx = tab_ldg(reinterpret_cast<const uint2*>(ent + j + 1));
+      if (tab_u64(nx.x, nx.y) > r) break;
+      ++j;
+      e = tab_ldg(ent + j);
+    }
   }
-  while (j + 1 < n) {
-    const uint2 nx = tab_ld(reinterpret_cast<const uint2*>(ent + j + 1));
-    const uint64_t ns = ((uint64_t)nx.y << 32) | nx.x;
-    if (ns > r) break;
-    ++j;
-    e = tab_ld(ent + j);
-    st = ns;
-  }
-  r -= st;
+  r -= tab_u64(e.x, e.y);
   s = e.z;
   nib = e.w;
-  take = (int)((rec.w >> 22) & 15u);
+  take = (int)((r0.z >> 21) & 15u);
 }
 
 LLVQ_HD void tab_put(uint64_t& lo, uint64_t& hi, uint64_t nib, int t) {
@@ -140,12 +186,12 @@ LLVQ_HD void tab_shl96(const uint32_t (&x)[3], uint32_t (&t)[3]) {
   }
 }
 
-// Expand table layout, per Golay word (lexicographic index), kTabExpandWords
-// u32 as five 32-byte stages q = 0..4 (applied in that order; stage q moves
-// nibbles by 2^(4-q) positions): {A0, A1, A2, B0}, {B1, B2, M_q, 0}, where
-// A0..A2 / B0..B2 are the nibble-wide move masks of the expand by the word /
-// by its complement (three u32 covering positions 0-7, 8-15, 16-23) and
-// M_0..M_2 the word itself widened to nibbles.
+// Expand table layout, per Golay word (weight order), kTabExpandWords u32 as
+// five 32-byte stages q = 0..4 (applied in that order; stage q moves nibbles
+// by 2^(4-q) positions): {A0, A1, A2, B0}, {B1, B2, M_q, 0}, where A0..A2 /
+// B0..B2 are the nibble-wide move masks of the expand by the word / by its
+// complement (three u32 covering positions 0-7, 8-15, 16-23) and M_0..M_2
+// the word itself widened to nibbles.
 //
 // Nibble-wise expand of both parts at once: source nibble t of xa goes to
 // the t-th position of the word, source nibble t of xb to the t-th position
@@ -155,7 +201,7 @@ LLVQ_HD void tab_expand2(uint32_t (&xa)[3], uint32_t (&xb)[3], const uint4* e, u
   uint32_t t[3];
 #define LLVQ_EXPAND_STAGE(Q, S)                                                           \
   {                                                                                        \
-    const uint4 u = tab_ld(e + 2 * (Q)), v = tab_ld(e + 2 * (Q) + 1);                       \
+    const uint4 u = tab_ldg(e + 2 * (Q)), v = tab_ldg(e + 2 * (Q) + 1);                     \
     const uint32_t ma[3] = {u.x, u.y, u.z}, mb[3] = {u.w, v.x, v.y};                      \
     if ((Q) < 3) m[(Q) < 3 ? (Q) : 0] = v.z;                                               \
     tab_shl96<S>(xa, t);                                                                   \
@@ -171,24 +217,24 @@ LLVQ_HD void tab_expand2(uint32_t (&xa)[3], uint32_t (&xb)[3], const uint4* e, u
 #undef LLVQ_EXPAND_STAGE
 }
 
-// Magnitudes by position (mag[w], byte i = position 4 w + i) of a valid
-// class-local decomposition: part A rank ra from state sa, part B rank rb
-// from state sb, word = lexicographic index of the Golay word whose positions
-// part A takes (4095, all positions, for odd classes), d0 = number of part-B
-// values (their value indices come first in `vals`), vals = the part-B values
-// then the part-A values, one per byte.
-LLVQ_HD void tab_magnitudes(const TabView& tv, uint32_t sa, uint64_t ra, uint32_t sb, uint64_t rb, int word_lex,
-                            int d0, uint64_t vals, uint32_t (&mag)[6]) {
+// Magnitudes by position (mag[w], byte i = position 4 w + i) from the two
+// parts' states and ranks.  word_slot: the word's entry in the expand table
+// (weight order); spread: whether the parts need moving at all (false for
+// odd classes and words of weight 0 or 24, whose parts are in position
+// order already: their lanes skip the mask loads).
+template <bool SMEM>
+LLVQ_HD void tab_magnitudes(const TabCtx& tc, uint32_t sa, uint64_t ra, uint32_t sb, uint64_t rb, int word_slot,
+                            bool spread, int d0, uint64_t vals, uint32_t (&mag)[6]) {
   uint64_t a_lo = 0, a_hi = 0, b_lo = 0, b_hi = 0;
   bool in_b = sa == kTabEnd;
   uint32_t s = in_b ? sb : sa;
   uint64_t r = in_b ? rb : ra;
   int t = 0;
-  for (int job = 0; job < tv.max_jobs; ++job) {
+  for (int job = 0; job < tc.max_jobs; ++job) {
     if (s == kTabEnd) break;
     uint64_t nib;
     int take;
-    tab_job(tv, s, r, nib, take);
+    tab_job<SMEM>(tc, s, r, nib, take);
     if (in_b) tab_put(b_lo, b_hi, nib, t);
     else tab_put(a_lo, a_hi, nib, t);
     t += take;
@@ -208,7 +254,12 @@ LLVQ_HD void tab_magnitudes(const TabView& tv, uint32_t sa, uint64_t ra, uint32_
   uint32_t xa[3] = {(uint32_t)a_lo, (uint32_t)(a_lo >> 32), (uint32_t)a_hi};
   uint32_t xb[3] = {(uint32_t)b_lo, (uint32_t)(b_lo >> 32), (uint32_t)b_hi};
   uint32_t m[3];
-  tab_expand2(xa, xb, tv.expand + (size_t)word_lex * (kTabExpandWords / 4), m);
+  if (spread) {
+    tab_expand2(xa, xb, tc.expand + (size_t)word_slot * (kTabExpandWords / 4), m);
+  } else {  // part A (odd, or the weight-24 word) everywhere, or part B (weight 0) everywhere
+    const uint32_t all = word_slot ? 0xFFFFFFFFu : 0u;
+    m[0] = m[1] = m[2] = all;
+  }
   const uint32_t vlo = (uint32_t)vals, vhi = (uint32_t)(vals >> 32);
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
@@ -217,16 +268,6 @@ LLVQ_HD void tab_magnitudes(const TabView& tv, uint32_t sa, uint64_t ra, uint32_
     mag[2 * k + 1] = tab_prmt(vlo, vhi, x >> 16);
   }
 }
-
-}  // namespace llvq
-
-namespace llvq {
-
-#if defined(__CUDA_ARCH__)
-__device__ __forceinline__ int tab_popc(uint32_t v) { return __popc(v); }
-#else
-inline int tab_popc(uint32_t v) { return __builtin_popcount(v); }
-#endif
 
 // Signs of a codeword from its magnitudes by position (mag[w], byte i =
 // position 4 w + i) and y = the signed integer codeword; false (and y
@@ -238,7 +279,6 @@ inline int tab_popc(uint32_t v) { return __builtin_popcount(v); }
 //               order, with the bit at the first word coordinate inserted so
 //               that the negative word coordinates have the class's parity
 //               (rank_even_signs / apply_even_signs, :804-841).
-// deposit4[m * 16 + s]: the low popc(m) bits of s placed on the set bits of m.
 LLVQ_HD bool tab_signs(const uint32_t (&mag)[6], uint32_t word, bool odd, uint64_t sign, int parity_bit,
                        const uint8_t* deposit4, int (&y)[kDim]) {
   // per-position bits of the magnitudes, four bytes at a time (every
@@ -271,17 +311,91 @@ LLVQ_HD bool tab_signs(const uint32_t (&mag)[6], uint32_t word, bool odd, uint64
     neg = 0;
 #pragma unroll
     for (int k = 0; k < kDim / 4; ++k) {
-      const uint32_t m = (nzmask >> (4 * k)) & 15u;
-      neg |= (uint32_t)deposit4[m * 16 + (cmask & 15u)] << (4 * k);
-      cmask >>= tab_popc(m);
+      const uint32_t mm = (nzmask >> (4 * k)) & 15u;
+      neg |= (uint32_t)deposit4[mm * 16 + (cmask & 15u)] << (4 * k);
+      cmask >>= tab_popc(mm);
     }
     if (word && (tab_popc(neg & word) & 1) != parity_bit) neg ^= word & (0u - word);
   }
 #pragma unroll
   for (int d = 0; d < kDim; ++d) {
-    const int m = (int)((mag[d >> 2] >> (8 * (d & 3))) & 0xFFu);
-    y[d] = ((neg >> d) & 1u) ? -m : m;
+    const int mv = (int)((mag[d >> 2] >> (8 * (d & 3))) & 0xFFu);
+    y[d] = ((neg >> d) & 1u) ? -mv : mv;
   }
+  return ok;
+}
+
+// a / b for b >= 1 given magic = floor((2^64 - 1) / b): the high half of
+// a * magic is floor(a / b) or one less (division by an invariant integer by
+// multiplication, Granlund and Montgomery 1994), fixed by one comparison.
+LLVQ_HD uint64_t tab_divmod(uint64_t a, uint64_t b, uint64_t magic, uint64_t& rem) {
+  uint64_t q = tab_mulhi(a, magic);
+  uint64_t r = a - q * b;
+  if (r >= b) {
+    ++q;
+    r -= b;
+  }
+  rem = r;
+  return q;
+}
+
+// Class of a valid index: the bucket of its leading bit and next four bits
+// narrows the search to the classes between the owners of the bucket's lowest
+// index and of the next bucket's.
+LLVQ_HD int tab_find_class(const TabCtx& tc, int64_t v) {
+  const uint64_t u = (uint64_t)v;
+  int key = 0;
+  if (u) {
+    const int e = tab_msb(u);
+    key = 1 + e * 16 + (int)((e >= 4 ? u >> (e - 4) : u << (4 - e)) & 15u);
+  }
+  int lo = tab_ldg(tc.bucket + key), hi = tab_ldg(tc.bucket + key + 1) + 1;
+  while (lo + 1 < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (tc.starts[mid] <= v) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// Integer codeword of index v; false and zeros outside the codebook (or for
+// a sign rank out of range, which no valid index has).
+template <bool SMEM>
+LLVQ_HD bool tab_decode(const TabCtx& tc, int64_t v, int (&y)[kDim]) {
+  if (!(v >= 0 && v < tc.total)) {
+    for (int d = 0; d < kDim; ++d) y[d] = 0;
+    return false;
+  }
+  const int k = tab_find_class(tc, v);
+  const uint4* cp = tc.crec + 4 * k;
+  const uint4 c0 = tab_ldr<SMEM>(cp), c1 = tab_ldr<SMEM>(cp + 1), c2 = tab_ldr<SMEM>(cp + 2),
+              c3 = tab_ldr<SMEM>(cp + 3);
+  const uint64_t start = tab_u64(c0.x, c0.y), perm = tab_u64(c0.z, c0.w);
+  const uint64_t magic_perm = tab_u64(c1.x, c1.y), magic_f1 = tab_u64(c1.z, c1.w);
+  const uint64_t vals = tab_u64(c2.x, c2.y);
+  const uint32_t f1p = c2.z, meta = c2.w;
+  const bool odd = meta & 1u;
+  const int weight = (int)((meta >> 1) & 31u), sshift = (int)((meta >> 6) & 31u), d0 = (int)((meta >> 11) & 15u);
+  uint64_t prank;
+  const uint64_t cur = tab_divmod((uint64_t)v - start, perm, magic_perm, prank);
+  uint32_t word;
+  int slot;
+  uint64_t sign = 0, ra = prank, rb = 0;
+  if (odd) {
+    word = tab_ldg(tc.golay + (int)cur);
+    slot = kNumGolay - 1;
+  } else {
+    sign = cur & ((1ull << sshift) - 1);
+    slot = (int)c3.x + (int)(cur >> sshift);
+    word = tab_ldg(tc.words + slot);
+    uint64_t r1;
+    rb = tab_divmod(prank, f1p, magic_f1, r1);
+    ra = r1;
+  }
+  uint32_t mag[6];
+  tab_magnitudes<SMEM>(tc, c3.y, ra, c3.z, rb, slot, !odd && weight != 0 && weight != kDim, d0, vals, mag);
+  const bool ok = tab_signs(mag, word, odd, sign, (int)((meta >> 15) & 1u), tc.deposit4, y);
+  if (!ok)
+    for (int d = 0; d < kDim; ++d) y[d] = 0;
   return ok;
 }
 

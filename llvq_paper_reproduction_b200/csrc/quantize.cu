@@ -146,6 +146,15 @@ __device__ double reference_score(const float* x, const int* y, int shell) {
   return __dsub_rn(__dmul_rn(kLatticeScaleD, reference_projection(x, y)), (double)shell);
 }
 
+// The exact score a search maximises: the reference's (ANG false), or the
+// correlation per unit norm of the multi-shell shape search, proj / |y| =
+// proj / sqrt(16 shell) (ANG true; the angular specs of gen_search.py).
+template <bool ANG>
+__device__ __forceinline__ double exact_score(const float* x, const int* y, int shell) {
+  if constexpr (ANG) return __ddiv_rn(reference_projection(x, y), __dsqrt_rn(16.0 * (double)shell));
+  else return reference_score(x, y, shell);
+}
+
 // The reference's best codeword of class c for Golay word `word`
 // (solve_even_subclass / solve_odd_subclass).  apos: positions in ascending
 // (|x|, position) order.
@@ -203,6 +212,7 @@ struct Ops {
   static constexpr int kNumShells = S::kNumShells;
   static constexpr int kMinShellC = S::kMinShell;
   static constexpr bool kHasOdd = S::kHasOdd;
+  static constexpr bool kAngular = S::kAngular;
   template <int W>
   static constexpr bool has_even() {
     return W == 0 ? S::kHasEven_w0 : W == 8 ? S::kHasEven_w8 : W == 12 ? S::kHasEven_w12
@@ -262,6 +272,7 @@ struct Ops<RuntimeSpec> {
   static constexpr int kNumShells = kRuntimeShells;
   static constexpr int kMinShellC = -1;
   static constexpr bool kHasOdd = true;
+  static constexpr bool kAngular = false;
   template <int W>
   static constexpr bool has_even() { return true; }
   template <int W>
@@ -508,12 +519,13 @@ __device__ __forceinline__ void pair_max(const DevBook& b, const Row& sh, uint32
 // Exact-pass handler for one candidate pair: the reference's codeword and fp64
 // score, kept if it beats (score desc, loop order asc).  Not inlined: the
 // generated scoring code calls it from every class site.
+template <bool ANG>
 __device__ __noinline__ void consider_exact(const float* x, const int8_t* apos, const DevBook& book, uint32_t word,
                                             int lex, int k, double* best, long long* order) {
   int y[kDim];
   const DevClass& cls = book.cls[k];
   build_candidate(x, apos, cls, word, y);
-  const double s = reference_score(x, y, cls.shell);
+  const double s = exact_score<ANG>(x, y, cls.shell);
   const long long o = (long long)lex * book.n_classes + k;
   if (s > *best || (s == *best && o < *order)) {
     *best = s;
@@ -538,6 +550,7 @@ __device__ __forceinline__ int gain_code(const GainCode& gc, const float* x, con
 
 // Rebuild the winning codeword, its fp64 reference score and its index (and
 // its gain code).
+template <bool ANG>
 __device__ __noinline__ void write_winner(const float* x, const int8_t* apos, const DevBook& book, long long order,
                                           int64_t row, long long* index_out, long long* pair_out, float* score_out,
                                           GainCode gc) {
@@ -546,7 +559,7 @@ __device__ __noinline__ void write_winner(const float* x, const int8_t* apos, co
   const uint32_t word = book.golay[lex];
   int y[kDim];
   build_candidate(x, apos, c, word, y);
-  const double s = reference_score(x, y, c.shell);
+  const double s = exact_score<ANG>(x, y, c.shell);
   const int choice = c.parity ? lex : (int)book.golay_wrank[lex];
   long long idx = rank_codeword(c, y, word, choice);
   if (gc.thr) {
@@ -690,7 +703,9 @@ __global__ void __launch_bounds__(Ops<S>::kThreads, Ops<S>::kMinBlocks) search_k
         const uint32_t c = __ldg(book.wlist_word + j);
         const int lex = __ldg(book.wlist_lex + j);
         word_cands<S>(book, sh, c, nmk, thr,
-                      [&](int k, float) { consider_exact(sh.x, sh.apos, book, c, lex, k, &best, &order); });
+                      [&](int k, float) {
+                        consider_exact<Ops<S>::kAngular>(sh.x, sh.apos, book, c, lex, k, &best, &order);
+                      });
       }
       sh.xs_best[tid] = best;
       sh.xs_order[tid] = order;
@@ -789,9 +804,9 @@ __global__ void __launch_bounds__(128) finalize_kernel(const float* __restrict__
     int nc = 0;
     word_cands<S>(book, r, c, nmk, thr, [&](int k, float) {
       if (nc < kMaxCands) cand[nc++] = k;
-      else consider_exact(r.x, r.apos, book, c, lex, k, &best, &order);
+      else consider_exact<Ops<S>::kAngular>(r.x, r.apos, book, c, lex, k, &best, &order);
     });
-    for (int i = 0; i < nc; ++i) consider_exact(r.x, r.apos, book, c, lex, cand[i], &best, &order);
+    for (int i = 0; i < nc; ++i) consider_exact<Ops<S>::kAngular>(r.x, r.apos, book, c, lex, cand[i], &best, &order);
     if (order == LLONG_MAX) {  // cannot happen for a finite row
       index_out[row] = -1;
       pair_out[row] = -1;
@@ -800,7 +815,7 @@ __global__ void __launch_bounds__(128) finalize_kernel(const float* __restrict__
       return;
     }
   }
-  write_winner(r.x, r.apos, book, order, row, index_out, pair_out, score_out, gc);
+  write_winner<Ops<S>::kAngular>(r.x, r.apos, book, order, row, index_out, pair_out, score_out, gc);
 }
 
 // ------------------------------------------------------------- launchers
@@ -836,7 +851,7 @@ static cudaError_t launch_search(const float* x, int64_t n, const DevBook& book,
 
 #define LLVQ_SPEC_ENTRY(NAME)                                                                     \
   {gen::kSig_##NAME, &launch_search<gen::Spec_##NAME>, #NAME, (float)gen::Spec_##NAME::kL1Max, \
-   (float)gen::Spec_##NAME::kWinMG, (float)gen::Spec_##NAME::kWinAM},
+   (float)gen::Spec_##NAME::kWinMG, (float)gen::Spec_##NAME::kWinAM, gen::Spec_##NAME::kAngular},
 static const SpecEntry kSpecs[] = {LLVQ_FOR_EACH_SPEC(LLVQ_SPEC_ENTRY)};
 
 const SpecEntry* spec_table(int* count) {
@@ -845,11 +860,17 @@ const SpecEntry* spec_table(int* count) {
 }
 
 cudaError_t quantize_launch(const Codebook& cb, const float* x, int64_t n, long long* index, long long* pair,
-                            float* score, cudaStream_t stream, bool force_runtime, const GainCode& gc) {
+                            float* score, cudaStream_t stream, bool force_runtime, const GainCode& gc, bool angular) {
   if (n <= 0) return cudaSuccess;
   DevBook book = cb.dev;
   SearchLauncher launch;
-  if (cb.spec && !force_runtime) {
+  if (angular) {  // generated code only
+    if (!cb.spec_ang) return cudaErrorNotSupported;
+    launch = cb.spec_ang->launch;
+    book.l1max = cb.spec_ang->l1max;
+    book.win_mg = cb.spec_ang->win_mg;
+    book.win_am = cb.spec_ang->win_am;
+  } else if (cb.spec && !force_runtime) {
     launch = cb.spec->launch;
     book.l1max = cb.spec->l1max;
     book.win_mg = cb.spec->win_mg;

@@ -13,7 +13,9 @@ Shape-gain has no reference implementation (the reference README lists it
 but the package does not exist); it is defined here as:
   * shape: the nearest point of one shell m (the reference search restricted
     to shells m..m, i.e. the largest correlation <x, y>), direction
-    u = y / |y|;
+    u = y / |y|; or, multi-shell, the point of shells m_lo..m_hi with the
+    largest correlation per unit norm <x, y> / |y| (fp64, ties in the
+    reference's loop order; generated "angular" search code);
   * gain: g = <x, u> (the least-squares gain for that direction), coded with
     a b-bit Lloyd-Max quantizer designed for the chi(24) density scaled by
     sigma (the norm of a 24-D N(0, sigma^2 I) block);
@@ -147,14 +149,25 @@ def rate_split(bits_per_dim: float, min_gain_bits: int = 3, max_shape_bits: int 
     return best
 
 
-class ShapeGainQuantizer:
-    """Single-shell shape with a chi-matched scalar gain (no reference
-    counterpart; see the module docstring for the definition)."""
+# Multi-shell shape codebooks with generated angular search code, by rate:
+# (min shell, max shell, gain bits); shells 2..5 have 2^32.2 points (33 shape
+# bits), 2..10 have 2^43.6 (44 shape bits).
+MULTI_SHELL_SPLITS = {1.5: (2, 5, 3), 2.0: (2, 10, 4)}
 
-    def __init__(self, shell: int, gain_bits: int, sigma: float = 1.0, device="cuda", use_cache: bool = False):
-        self.shape = LeechLatticeVectorQuantizerGpu(max_shell=shell, min_shell=shell, device=device,
+
+class ShapeGainQuantizer:
+    """Shape from one shell (min_shell = shell, the default) or from shells
+    min_shell..shell by correlation per unit norm, with a chi-matched scalar
+    gain (no reference counterpart; see the module docstring)."""
+
+    def __init__(self, shell: int, gain_bits: int, sigma: float = 1.0, device="cuda", use_cache: bool = False,
+                 min_shell: int | None = None):
+        lo = shell if min_shell is None else min_shell
+        self.shape = LeechLatticeVectorQuantizerGpu(max_shell=shell, min_shell=lo, device=device,
                                                     use_cache=use_cache)
         self.shell = shell
+        self.min_shell = lo
+        self.multi_shell = lo < shell
         self.gain_bits = gain_bits
         self.sigma = sigma
         levels, thr = chi_lloyd_max(gain_bits)
@@ -163,7 +176,14 @@ class ShapeGainQuantizer:
         self.norm = math.sqrt(2.0 * shell)  # |y| / sqrt(8) for every point of the shell
 
     @classmethod
-    def for_rate(cls, bits_per_dim: float, sigma: float = 1.0, device="cuda") -> "ShapeGainQuantizer":
+    def for_rate(cls, bits_per_dim: float, sigma: float = 1.0, device="cuda",
+                 multi_shell: bool = False) -> "ShapeGainQuantizer":
+        if multi_shell:
+            if bits_per_dim not in MULTI_SHELL_SPLITS:
+                raise ValueError(f"no multi-shell split for {bits_per_dim} bits/dim "
+                                 f"(have {sorted(MULTI_SHELL_SPLITS)})")
+            lo, hi, gb = MULTI_SHELL_SPLITS[bits_per_dim]
+            return cls(hi, gb, sigma, device, min_shell=lo)
         split = rate_split(bits_per_dim)
         return cls(split.shell, split.gain_bits, sigma, device)
 
@@ -203,7 +223,8 @@ class ShapeGainQuantizer:
             self.shape._book().quantize_gain(
                 xs.data_ptr(), n, idx.data_ptr(), pair.data_ptr(), score.data_ptr(), self.thresholds.data_ptr(),
                 self.gain_bits, sig.data_ptr() if sig is not None else None, 1,
-                gain.data_ptr() if gain is not None else None, pack, torch.cuda.current_stream().cuda_stream)
+                gain.data_ptr() if gain is not None else None, pack, torch.cuda.current_stream().cuda_stream,
+                angular=self.multi_shell)
         return idx.reshape(shape), (gain.reshape(shape) if gain is not None else None)
 
     def dequantize_parts(self, sidx: torch.Tensor, gidx: torch.Tensor,
@@ -211,7 +232,10 @@ class ShapeGainQuantizer:
         g = self.levels[gidx.to(device=self.shape.device, dtype=torch.long)]
         if row_sigma is not None:
             g = g * row_sigma
-        return self.shape.dequantize(sidx.to(self.shape.device)) * (g / self.norm).unsqueeze(-1)
+        v = self.shape.dequantize(sidx.to(self.shape.device))
+        if self.multi_shell:  # |y| / sqrt(8) = sqrt(2 shell) varies with the shell
+            return v * (g / v.norm(dim=-1)).unsqueeze(-1)
+        return v * (g / self.norm).unsqueeze(-1)
 
     def quantize(self, x: torch.Tensor, row_sigma: torch.Tensor | None = None) -> torch.Tensor:
         """x [..., 24] -> combined int64 indices shape * 2^b + gain.  Rates

@@ -481,7 +481,13 @@ static void solve_odd(const ocls* c, uint32_t word, const word_orders* o, int* y
 
 /* quantize(): argmax over (Golay word lex order, shell asc, class asc) of
  * LATTICE_SCALE*proj - shell with strict '>'.  Returns the index, or -1 if no
- * candidate exists (all scores NaN). */
+ * candidate exists (all scores NaN).
+ * mode bit 0: hoist the per-word sorts (same result, faster).
+ * mode bit 1: angular search for the multi-shell shape of shape-gain
+ * quantization (no reference counterpart): the score is proj / |y| =
+ * proj / sqrt(16 shell) in fp64 instead, the same loop order and strict '>'.
+ * Within one class the best codeword of a word is the same for both scores
+ * (every codeword of a class has the same norm). */
 int64_t oracle_encode(const oracle_book* b, const int32_t* y);
 
 int64_t oracle_quantize(const oracle_book* b, const double* x, int mode, int32_t* best_golay, int32_t* best_class,
@@ -493,19 +499,21 @@ int64_t oracle_quantize(const oracle_book* b, const double* x, int mode, int32_t
     for (int g = 0; g < NGOLAY; ++g) {
         uint32_t word = b->golay[g];
         int wt = b->golay_weight[g];
-        if (mode == 1) compute_orders(x, word, &o, 1, 1);
+        const int hoist = mode & 1, angular = mode & 2;
+        if (hoist) compute_orders(x, word, &o, 1, 1);
         for (int k = 0; k < b->ncls; ++k) {
             const ocls* c = &b->cls[k];
             if (c->parity == 0) {
                 if (wt != c->even_weight) continue;
-                if (mode == 0) compute_orders(x, word, &o, 1, 0);
+                if (!hoist) compute_orders(x, word, &o, 1, 0);
                 solve_even(x, c, &o, y);
             } else {
-                if (mode == 0) compute_orders(x, word, &o, 0, 1);
+                if (!hoist) compute_orders(x, word, &o, 0, 1);
                 solve_odd(c, word, &o, y);
             }
             double proj = ref_projection(x, y);
-            double score = LATTICE_SCALE * proj - (double)c->shell;
+            double score = angular ? proj / sqrt(16.0 * (double)c->shell)
+                                   : LATTICE_SCALE * proj - (double)c->shell;
             if (score > best) {
                 best = score;
                 found = 1;

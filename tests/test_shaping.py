@@ -98,7 +98,8 @@ def expected_gain(book, sg, x, shape_idx, sigma=None):
     out = []
     for i, s in enumerate(shape_idx):
         y = np.asarray(book.codeword(int(s)), dtype=np.int32)
-        g = ref_projection(x[i].astype(np.float64), y) / np.sqrt(16.0 * sg.shell)
+        shell = int((y.astype(np.int64) ** 2).sum()) // 16
+        g = ref_projection(x[i].astype(np.float64), y) / np.sqrt(16.0 * shell)
         if sigma is not None:
             g = g / np.float64(np.float32(sigma[i]))
         out.append(int(np.searchsorted(thr, g, side="left")))
@@ -137,3 +138,29 @@ def test_gpu_shape_gain_every_rate_matches_oracle(rate):
     else:
         with pytest.raises(ValueError):
             sg.quantize(x.cuda())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("lo,hi,gain_bits,rows", [(2, 4, 3, 64), (2, 5, 3, 32), (2, 10, 4, 12)])
+def test_gpu_multi_shell_shape_matches_oracle(lo, hi, gain_bits, rows):
+    """Multi-shell shape search (largest <x, y> / |y| over shells lo..hi, fp64,
+    ties in loop order) against the oracle's angular search, with degenerate
+    rows (zeros, an integer row, a scaled lattice point); gain codes exactly."""
+    from llvq_paper_reproduction_b200.shaping import ShapeGainQuantizer
+    from oracle.oracle import OracleBook
+
+    sg = ShapeGainQuantizer(hi, gain_bits, min_shell=lo)
+    assert sg.multi_shell
+    book = OracleBook(hi, min_shell=lo)
+    x = torch.randn((rows, 24), generator=torch.Generator().manual_seed(lo * 100 + hi)).float()
+    x[0] = 0.0
+    x[1] = torch.tensor([4, 7, 2, 8, 6, 1, 6, 5, 7, 2, 4, 6, 5, 9, 2, 6, 3, 8, 5, 7, 4, 11, 2, 8], dtype=torch.float32)
+    x[2] = torch.tensor(book.codeword(7), dtype=torch.float32) * 0.35355339059327373
+    s2, g2 = sg.quantize_parts(x.cuda())
+    ref = book.quantize_batch(x.numpy(), mode=3, threads=8)[0]
+    np.testing.assert_array_equal(s2.cpu().numpy(), ref)
+    ok = ref >= 0
+    want = expected_gain(book, sg, x.numpy()[ok], ref[ok])
+    np.testing.assert_array_equal(g2.cpu().numpy()[ok], want)
+    recon = sg.dequantize_parts(s2[torch.from_numpy(ok).cuda()], g2[torch.from_numpy(ok).cuda()])
+    assert bool(torch.isfinite(recon).all())
