@@ -118,15 +118,21 @@ int llvq_dequantize_bf16(const llvq_codebook* cb, const int64_t* indices, int64_
  * (W columns at k and beyond meet zeros); y: fp32 [m, n_out].  For m <= 4
  * one kernel decodes each weight block in registers and multiplies it there
  * (a warp per output row, a fixed summation order; nothing is allocated).
+ * For 5 <= m <= 256 on a codebook with decoder tables (llvq_codebook_tables)
+ * one fused kernel decodes the weights straight into the shared-memory
+ * operand of tcgen05 MMAs (stream-K over tiles and K groups; the partial sums
+ * of tiles shared by two SMs go to a workspace of at most 39 MB from the
+ * library's pool and a second kernel adds them in a fixed order).
  * Otherwise the weights
  * are decoded into a bf16 staging buffer (at most 256 MiB, chunk by chunk
  * beyond that; stream-ordered on `stream` from a library-owned memory pool
  * that keeps its reservation between calls) that a pipelined
  * tcgen05 GEMM reads, accumulating in fp32; when the matrix has fewer
  * 128 x 256 output tiles than SMs the K range is split in two and y is
- * zeroed first (cudaMemsetAsync).  *error_flag (device int, may be NULL) is
- * set to 1 if a tensor-core wait timed out.  No reference counterpart (the
- * reference has no GEMM). */
+ * zeroed first (cudaMemsetAsync).  Every path gives each output one
+ * summation order (the same bits on every call).  *error_flag (device int,
+ * may be NULL) is set to 1 if a tensor-core wait timed out.  No reference
+ * counterpart (the reference has no GEMM). */
 int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, int64_t blocks_per_row,
               const uint16_t* row_scale_f16, const uint16_t* a_bf16, int64_t m, int64_t k, float* y,
               int32_t* error_flag, void* stream);
@@ -134,10 +140,11 @@ int llvq_gemm(const llvq_codebook* cb, const int64_t* indices, int64_t n_out, in
 /* llvq_gemm without device allocation.  No counterpart in the reference.
  * For callers that may not allocate device memory while they run (a serving
  * engine that reserved the GPU's memory for its own pool, a step that must not
- * fail on out-of-memory halfway): the decoded weights are staged in a fixed
- * LLVQ_GEMM_NOALLOC_STAGING_BYTES (16 MiB) array compiled into the library,
- * one per device, instead of a stream-ordered pool buffer, a chunk of rows at a
- * time (batches of m <= 4 are decoded in registers, as in llvq_gemm, and do
+ * fail on out-of-memory halfway): a fixed LLVQ_GEMM_NOALLOC_STAGING_BYTES
+ * (16 MiB) array compiled into the library, one per device, replaces the
+ * stream-ordered pool buffer: as the fused kernel's partial-sum workspace
+ * when that fits it, else as the bf16 staging, a chunk of rows at a time
+ * (batches of m <= 4 are decoded in registers, as in llvq_gemm, and do
  * not use the array).  Same arguments, results and error flag as llvq_gemm, plus,
  * for m > 4, the limit blocks_per_row <= LLVQ_GEMM_NOALLOC_MAX_BLOCKS_PER_ROW
  * (2730: one 128-row tile of rows up to 65536 columns fits the array); wider
@@ -194,6 +201,16 @@ int llvq_hadamard(const void* in, int32_t in_is_half, float* out, int64_t rows, 
 enum { LLVQ_DT_F32 = 0, LLVQ_DT_F16 = 1, LLVQ_DT_BF16 = 2 };
 int llvq_hadamard_ex(const void* in, int32_t in_type, void* out, int32_t out_type, int64_t rows, int64_t cols,
                      int32_t block, const int8_t* signs, int32_t inverse, void* stream);
+
+/* Weight preparation for quantization in one pass: each fp16 row of a
+ * [rows, cols] matrix is rotated forward as llvq_hadamard does (signs,
+ * segments of `block` columns), its RMS over the cols entries (a fixed-order
+ * fp32 reduction) is rounded to fp16 (at least 1e-8) into row_scale_out[row],
+ * and out[row] (fp32, ld >= cols columns) receives the rotated row divided by
+ * that scale, zero from column cols on.  cols * 4 bytes must fit 200 KiB of
+ * shared memory.  No reference counterpart. */
+int llvq_rotate_scale(const uint16_t* in_f16, int64_t rows, int64_t cols, int64_t ld, int32_t block,
+                      const int8_t* signs, float* out, uint16_t* row_scale_out, void* stream);
 
 /* Host-side scalar paths (no GPU needed).
  * llvq_codeword_host:  LeechLatticeVectorQuantizerGpu.codeword (_gpu.py:262-265)

@@ -39,7 +39,7 @@ EXPORTS = (
     "llvq_encode_host", "llvq_status_string", "llvq_last_error", "llvq_version", "llvq_gemm",
     "llvq_hadamard", "llvq_gemm_noalloc", "llvq_pack_indices", "llvq_unpack_indices", "llvq_dequantize_packed",
     "llvq_gemm_packed", "llvq_hadamard_ex", "llvq_codeword_batch_host", "llvq_codebook_tables",
-    "llvq_quantize_gain",
+    "llvq_quantize_gain", "llvq_rotate_scale",
 )
 
 _lib = None
@@ -73,6 +73,7 @@ def load() -> ctypes.CDLL:
             "llvq_gemm_noalloc": (ctypes.c_int, [vp, vp, i64, i64, vp, vp, i64, i64, vp, vp, vp]),
             "llvq_hadamard": (ctypes.c_int, [vp, i32, vp, i64, i64, i32, vp, i32, vp]),
             "llvq_hadamard_ex": (ctypes.c_int, [vp, i32, vp, i32, i64, i64, i32, vp, i32, vp]),
+            "llvq_rotate_scale": (ctypes.c_int, [vp, i64, i64, i64, i32, vp, vp, vp, vp]),
             "llvq_pack_indices": (ctypes.c_int, [vp, i64, i32, vp, vp, vp]),
             "llvq_unpack_indices": (ctypes.c_int, [vp, i64, i32, vp, vp]),
             "llvq_dequantize_packed": (ctypes.c_int, [vp, vp, i32, i64, vp, i32, vp, i64, vp, vp]),
@@ -238,6 +239,12 @@ def hadamard_ex(in_ptr: int, in_type: int, out_ptr: int, out_type: int, rows: in
                 signs_ptr: int, inverse: bool, stream: int) -> None:
     check(load().llvq_hadamard_ex(in_ptr, in_type, out_ptr, out_type, rows, cols, block, signs_ptr, int(inverse),
                                   stream), "llvq_hadamard_ex")
+
+
+def rotate_scale(in_ptr: int, rows: int, cols: int, ld: int, block: int, signs_ptr: int, out_ptr: int,
+                 scale_ptr: int, stream: int) -> None:
+    check(load().llvq_rotate_scale(in_ptr, rows, cols, ld, block, signs_ptr, out_ptr, scale_ptr, stream),
+          "llvq_rotate_scale")
 
 
 def hadamard(in_ptr: int, in_is_half: bool, out_ptr: int, rows: int, cols: int, block: int, signs_ptr: int,

@@ -812,6 +812,19 @@ int llvq_gemm_noalloc(const llvq_codebook* h, const int64_t* indices, int64_t n_
   });
 }
 
+int llvq_rotate_scale(const uint16_t* in_f16, int64_t rows, int64_t cols, int64_t ld, int32_t block,
+                      const int8_t* signs, float* out, uint16_t* row_scale_out, void* stream) {
+  if (rows < 0 || cols <= 0 || ld < cols || block < 2 || block > 4096 || (block & (block - 1)) || cols % block ||
+      cols * 4 > 200 * 1024)
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "rotate_scale: block a power of two <= 4096 dividing cols, ld >= cols, "
+                                           "cols <= 51200");
+  if (rows > 0 && (!in_f16 || !signs || !out || !row_scale_out))
+    return fail(LLVQ_ERR_INVALID_ARGUMENT, "rotate_scale: null pointer");
+  const cudaError_t e = llvq::rotate_scale_launch(in_f16, rows, cols, ld, block, signs, out, row_scale_out,
+                                                  (cudaStream_t)stream);
+  return e == cudaSuccess ? LLVQ_OK : cuda_fail(e, "rotate_scale launch");
+}
+
 int llvq_hadamard_ex(const void* in, int32_t in_type, void* out, int32_t out_type, int64_t rows, int64_t cols,
                      int32_t block, const int8_t* signs, int32_t inverse, void* stream) {
   if (rows < 0 || cols <= 0 || block < 1 || block > 4096 || (block & (block - 1)) || cols % block)

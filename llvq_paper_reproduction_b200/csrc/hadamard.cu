@@ -76,6 +76,81 @@ __global__ void __launch_bounds__(kHadThreads) hadamard_kernel(const void* __res
   }
 }
 
+// Rotation, row scale and padding of a weight matrix for quantization, one
+// CTA per row: the fp16 row with its signs into shared memory (fp32), the
+// butterflies of every segment of `block` columns, 1/sqrt(block); then the
+// row's RMS (a fixed-order reduction: each thread's strided partial sum, then
+// a tree over the threads), rounded to fp16 (at least 1e-8 before rounding)
+// as the row scale; the output row is the rotated row divided by that scale,
+// zero-padded from cols to ld columns (fp32).  Replaces rotate, RMS, divide
+// and pad as separate passes before the shape-gain quantizer.
+constexpr int kRotThreads = 512;
+
+__global__ void __launch_bounds__(kRotThreads) rotate_scale_kernel(const __half* __restrict__ in, int cols, int ld,
+                                                                    int block, int log2b,
+                                                                    const int8_t* __restrict__ signs,
+                                                                    float* __restrict__ out,
+                                                                    uint16_t* __restrict__ scale_out) {
+  extern __shared__ float row[];
+  __shared__ float red[kRotThreads / 32];
+  const int64_t r = blockIdx.x;
+  const __half* src = in + r * (int64_t)cols;
+  for (int i = threadIdx.x; i < cols; i += kRotThreads) {
+    const float v = __half2float(src[i]);
+    row[i] = signs[i] < 0 ? -v : v;
+  }
+  __syncthreads();
+  for (int st = 0; st < log2b; ++st) {
+    const int h = 1 << st;
+    for (int p = threadIdx.x; p < cols / 2; p += kRotThreads) {
+      // pair p of the whole row: segment p / (block / 2), butterfly inside it
+      const int i = ((p >> st) << (st + 1)) | (p & (h - 1));
+      const float a = row[i], b = row[i + h];
+      row[i] = a + b;
+      row[i + h] = a - b;
+    }
+    __syncthreads();
+  }
+  const float rs = rsqrtf((float)block);
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < cols; i += kRotThreads) {
+    const float v = row[i] * rs;
+    row[i] = v;
+    acc = fmaf(v, v, acc);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRotThreads / 32; ++w) total += red[w];
+  const __half hs = __float2half_rn(fmaxf(sqrtf(total / (float)cols), 1e-8f));
+  const float scale = __half2float(hs);
+  if (threadIdx.x == 0) scale_out[r] = __half_as_ushort(hs);
+  float* dst = out + r * (int64_t)ld;
+  for (int i = threadIdx.x; i < ld; i += kRotThreads) dst[i] = i < cols ? __fdiv_rn(row[i], scale) : 0.f;
+}
+
+cudaError_t rotate_scale_launch(const void* in, int64_t rows, int64_t cols, int64_t ld, int block,
+                                const int8_t* signs, float* out, uint16_t* scale_out, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  if (block < 2 || (block & (block - 1)) || cols % block || ld < cols || rows > 0x7FFFFFFFLL)
+    return cudaErrorInvalidValue;
+  int log2b = 0;
+  while ((1 << log2b) < block) ++log2b;
+  const size_t smem = (size_t)cols * sizeof(float);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(rotate_scale_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+  }
+  rotate_scale_kernel<<<(unsigned)rows, kRotThreads, smem, stream>>>(static_cast<const __half*>(in), (int)cols,
+                                                                      (int)ld, block, log2b, signs, out, scale_out);
+  return cudaGetLastError();
+}
+
 cudaError_t hadamard_launch(const void* in, int in_type, void* out, int out_type, int64_t rows, int64_t cols,
                             int block, const int8_t* signs, int inverse, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;

@@ -151,6 +151,11 @@ constexpr int64_t kNoAllocStagingBytes = 16ll << 20;
 cudaError_t noalloc_staging(void** ptr);
 cudaError_t gemm_configure_device();
 
+// Rotation (fp16 in), fp16 RMS row scale and zero padding to ld columns in
+// one pass (hadamard.cu).
+cudaError_t rotate_scale_launch(const void* in, int64_t rows, int64_t cols, int64_t ld, int block,
+                                const int8_t* signs, float* out, uint16_t* scale_out, cudaStream_t stream);
+
 // Element types 0 fp32, 1 fp16, 2 bf16 (out: 0 or 2).
 cudaError_t hadamard_launch(const void* in, int in_type, void* out, int out_type, int64_t rows, int64_t cols,
                             int block, const int8_t* signs, int inverse, cudaStream_t stream);

@@ -8,10 +8,11 @@ Per matrix:
   1. seeded random Hadamard rotation along the input dimension (+-1 signs
      times the normalised Walsh-Hadamard transform, in segments of the
      largest power of two dividing the row length: 4096 for 4096, 256 for
-     11008) -- the library's Hadamard kernel;
+     11008);
   2. per-row scale = RMS of the rotated row, stored as fp16;
-  3. rows padded with zeros to a multiple of 24 (4104, 11016) and split into
-     24-D blocks;
+  3. rows divided by their scale, padded with zeros to a multiple of 24
+     (4104, 11016) and split into 24-D blocks -- steps 1-3 are one library
+     kernel (llvq_rotate_scale);
   4. shape-gain quantization of every block (shaping.ShapeGainQuantizer,
      2 bits/dim by default: index = shape * 2^b + gain).
 Sharding: matrices are independent, so ranks own whole matrices (greedy
@@ -127,15 +128,19 @@ class MatrixQuantizer:
         self.device = torch.device(device)
 
     def quantize(self, spec: MatrixSpec, with_error: bool = False) -> dict:
+        from . import _native
+
         w = synth_weight(spec, self.seed, self.device)
         block = hadamard_block(spec.in_features)
         signs = hadamard_signs(spec.in_features, self.seed * 7919 + spec.in_features, self.device)
-        wr = rotate(w, signs, block)
-        scale = wr.pow(2).mean(1).sqrt().clamp_min(1e-8).to(torch.float16)
-        x = wr / scale.float()[:, None]
         bpr = spec.blocks_per_row
-        xp = torch.zeros((spec.out_features, bpr * DIM), dtype=torch.float32, device=self.device)
-        xp[:, : spec.in_features] = x
+        # rotation, fp16 RMS row scale, division and zero padding in one kernel
+        xp = torch.empty((spec.out_features, bpr * DIM), dtype=torch.float32, device=self.device)
+        scale = torch.empty(spec.out_features, dtype=torch.float16, device=self.device)
+        with torch.cuda.device(self.device):
+            _native.rotate_scale(w.data_ptr(), spec.out_features, spec.in_features, bpr * DIM, block,
+                                 signs.data_ptr(), xp.data_ptr(), scale.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream)
         idx = self.sg.quantize(xp.view(-1, DIM)).view(spec.out_features, bpr)
         out = {"indices": idx, "row_scale": scale}
         if with_error:

@@ -165,3 +165,27 @@ def test_gpu_matrix_quantization():
         assert r["indices"].shape == (spec.out_features, spec.blocks_per_row)
         assert int(r["indices"].min()) >= 0 and int(r["indices"].max()) < (1 << mq.sg.bits)
         assert r["rel_mse"] < 0.15  # ~2 bits/dim on a Gaussian source
+
+
+@pytest.mark.gpu
+def test_gpu_rotate_scale_matches_separate_passes():
+    """The fused rotation + RMS scale + pad kernel against the rotation kernel
+    followed by the same steps in torch: the rotated rows are identical; the
+    fp16 scale may differ by one fp16 step (the RMS reduction order differs)."""
+    from llvq_paper_reproduction_b200 import _native
+    from llvq_paper_reproduction_b200.model_quant import hadamard_signs, rotate
+
+    for rows, cols in ((64, 4096), (33, 11008)):
+        block = hadamard_block(cols)
+        ld = (cols + 23) // 24 * 24
+        w = (torch.randn((rows, cols), device="cuda") * 0.02).to(torch.float16)
+        signs = hadamard_signs(cols, 5, "cuda")
+        xp = torch.full((rows, ld), float("nan"), device="cuda")
+        sc = torch.empty(rows, dtype=torch.float16, device="cuda")
+        _native.rotate_scale(w.data_ptr(), rows, cols, ld, block, signs.data_ptr(), xp.data_ptr(), sc.data_ptr(),
+                             torch.cuda.current_stream().cuda_stream)
+        wr = rotate(w, signs, block)
+        want_sc = wr.pow(2).mean(1).sqrt().clamp_min(1e-8).to(torch.float16)
+        assert (sc.float() - want_sc.float()).abs().max() <= want_sc.float().max() * 2 ** -10
+        assert torch.equal(xp[:, :cols], wr / sc.float()[:, None])
+        assert not xp[:, cols:].any()
