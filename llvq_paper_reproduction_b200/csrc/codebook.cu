@@ -397,7 +397,7 @@ int upload(llvq::Codebook& cb, int device) {
   const size_t o_tstate = off; off = align256(off + tb.state.size() * sizeof(uint4));
   const size_t o_tcrec = off; off = align256(off + tb.crec.size() * sizeof(uint4));
   const size_t o_tentry = off; off = align256(off + tb.entry.size() * sizeof(uint4));
-  const size_t o_tguide = off; off = align256(off + tb.guide.size() * sizeof(uint16_t));
+  const size_t o_tslot = off; off = align256(off + tb.slot.size() * sizeof(uint4));
   const size_t o_ttail = off; off = align256(off + tb.tail.size() * sizeof(unsigned long long));
   const size_t o_texp = off; off = align256(off + tb.expand.size() * sizeof(uint32_t));
   std::vector<unsigned char> host(off, 0);
@@ -405,7 +405,7 @@ int upload(llvq::Codebook& cb, int device) {
     std::memcpy(host.data() + o_tstate, tb.state.data(), tb.state.size() * sizeof(uint4));
     std::memcpy(host.data() + o_tcrec, tb.crec.data(), tb.crec.size() * sizeof(uint4));
     std::memcpy(host.data() + o_tentry, tb.entry.data(), tb.entry.size() * sizeof(uint4));
-    std::memcpy(host.data() + o_tguide, tb.guide.data(), tb.guide.size() * sizeof(uint16_t));
+    std::memcpy(host.data() + o_tslot, tb.slot.data(), tb.slot.size() * sizeof(uint4));
     std::memcpy(host.data() + o_ttail, tb.tail.data(), tb.tail.size() * sizeof(unsigned long long));
     std::memcpy(host.data() + o_texp, tb.expand.data(), tb.expand.size() * sizeof(uint32_t));
   }
@@ -495,11 +495,11 @@ int upload(llvq::Codebook& cb, int device) {
     d.tab.state = reinterpret_cast<const uint4*>(base + o_tstate);
     d.tab.crec = reinterpret_cast<const uint4*>(base + o_tcrec);
     d.tab.entry = reinterpret_cast<const uint4*>(base + o_tentry);
-    d.tab.guide = reinterpret_cast<const uint16_t*>(base + o_tguide);
+    d.tab.slot = reinterpret_cast<const uint4*>(base + o_tslot);
     d.tab.tail = reinterpret_cast<const unsigned long long*>(base + o_ttail);
     d.tab.expand = reinterpret_cast<const uint4*>(base + o_texp);
     d.tab.n_states = (int)(tb.state.size() / 2);
-    d.tab.max_jobs = tb.max_jobs;
+    d.tab.max_searches = tb.max_searches;
   }
   std::copy(cb.weight_start, cb.weight_start + 25, d.weight_start);
   d.n_classes = (int32_t)n;
@@ -579,9 +579,9 @@ int llvq_codebook_tables(const llvq_codebook* h, int32_t* tabulated, int64_t* ta
   const llvq::TabHost& t = h->cb.tab;
   if (tabulated) *tabulated = t.ok ? 1 : 0;
   if (table_bytes)
-    *table_bytes = (int64_t)(t.state.size() * 16 + t.crec.size() * 16 + t.entry.size() * 16 + t.guide.size() * 2 +
+    *table_bytes = (int64_t)(t.state.size() * 16 + t.crec.size() * 16 + t.entry.size() * 16 + t.slot.size() * 16 +
                              t.tail.size() * 8 + t.expand.size() * 4);
-  if (max_lookups) *max_lookups = t.max_jobs;
+  if (max_lookups) *max_lookups = t.max_searches + 2;  // searches, then one tail per part
   return LLVQ_OK;
 }
 

@@ -9,7 +9,7 @@
 // becomes a tail (all its orderings, in rank order); a larger one a search
 // over its next h = min(kTabHead, positions - kTabTail) positions (every
 // h-prefix in rank order with the rank where its completions start and the
-// state it leaves), with a guide table.  States are keyed by their counts
+// state it leaves), with a slot table.  States are keyed by their counts
 // alone, so classes with equal part multisets share them.
 #include <cuda_runtime.h>
 
@@ -137,15 +137,17 @@ struct Builder {
         int lg = 0;
         while ((1u << lg) < 4 * pre.size()) ++lg;
         const uint32_t slots = 1u << lg;
-        if ((n * (u128)(slots + 1)) >> 63) return fail("guide slot arithmetic would overflow");
+        if ((n * (u128)(slots + 1)) >> 63) return fail("slot arithmetic would overflow");
+        if (t.slot.size() + slots > kTabMaxEntries) return fail("slot tables too large");
         r0.x = (uint32_t)t.entry.size();
-        r0.y = (uint32_t)t.guide.size();
-        r0.z = (uint32_t)pre.size() | ((uint32_t)lg << 16) | ((uint32_t)h << 21);
+        r0.y = (uint32_t)t.slot.size();
+        r0.z = (uint32_t)pre.size() | ((uint32_t)lg << 17) | ((uint32_t)h << 22);
         const uint64_t n64 = (uint64_t)n;
         const double gn = (double)slots / (double)n64;
         uint64_t gbits;
         std::memcpy(&gbits, &gn, 8);
         r1 = make_uint4((uint32_t)n64, (uint32_t)(n64 >> 32), (uint32_t)gbits, (uint32_t)(gbits >> 32));
+        const size_t e0 = t.entry.size();
         for (const Prefix& p : pre)
           t.entry.push_back({(uint32_t)(uint64_t)p.start, (uint32_t)((uint64_t)p.start >> 32), p.next, p.nib});
         // slot g holds the ranks ceil(g N / G) .. ceil((g + 1) N / G) - 1
@@ -162,7 +164,7 @@ struct Builder {
           const u128 next = ((u128)(g + 1) * n + slots - 1) / slots;
           const size_t j = entry_of(first < n ? first : n - 1);
           const bool ambiguous = next > first && entry_of(next - 1) != j;
-          t.guide.push_back((uint16_t)(j | (ambiguous ? kTabGuideAmbiguous : 0)));
+          t.slot.push_back(ambiguous ? make_uint4((uint32_t)j, kTabSlotAmbiguous, 0, 0) : t.entry[e0 + j]);
         }
       }
       t.state.push_back(r0);
@@ -175,7 +177,7 @@ struct Builder {
       const uint4& r0 = t.state[2 * s];
       if (r0.z & kTabTailBit) continue;
       int d = 0;
-      for (uint32_t e = 0; e < (r0.z & 0xFFFFu); ++e) d = std::max(d, depth[t.entry[r0.x + e].z]);
+      for (uint32_t e = 0; e < (r0.z & 0x1FFFFu); ++e) d = std::max(d, depth[t.entry[r0.x + e].z]);
       depth[s] = 1 + d;
     }
     return true;
@@ -292,7 +294,9 @@ bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
   for (size_t k = 0; k < n; ++k) {
     const DevClass& c = cb.cls[k];
     const uint2 st = parts[k];
-    t.max_jobs = std::max(t.max_jobs, (st.x != kTabEnd ? b.depth[st.x] : 0) + (st.y != kTabEnd ? b.depth[st.y] : 0));
+    // searches before each part's tail (depth counts the tail too)
+    t.max_searches = std::max(t.max_searches, (st.x != kTabEnd ? b.depth[st.x] - 1 : 0) +
+                                                  (st.y != kTabEnd ? b.depth[st.y] - 1 : 0));
     uint64_t vals = 0;
     int d0 = 0;
     if (c.parity) {
@@ -353,17 +357,17 @@ TabCtx host_tab_ctx(const Codebook& cb) {
   TabCtx tc{};
   tc.srec = t.state.data();
   tc.crec = t.crec.data();
-  tc.starts = cb.class_start.data();
   tc.bucket = t.bucket.data();
-  tc.entry = t.entry.data();
-  tc.guide = t.guide.data();
-  tc.tail = t.tail.data();
-  tc.expand = reinterpret_cast<const uint4*>(t.expand.data());
   tc.words = cb.wlist_word.data();
   tc.golay = cb.golay.data();
+  tc.starts = cb.class_start.data();
   tc.deposit4 = host_deposit4();
+  tc.entry = t.entry.data();
+  tc.slot = t.slot.data();
+  tc.tail = t.tail.data();
+  tc.expand = reinterpret_cast<const uint4*>(t.expand.data());
   tc.n_classes = (int)cb.cls.size();
-  tc.max_jobs = t.max_jobs;
+  tc.max_searches = t.max_searches;
   tc.total = cb.total;
   return tc;
 }

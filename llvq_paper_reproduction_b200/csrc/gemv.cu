@@ -25,8 +25,9 @@ namespace llvq {
 
 constexpr int kGemvThreads = 256;  // 8 warps: 8 output rows per CTA
 
-constexpr int kGemvTabBlocks = 3;               // persistent table-driven grid: CTAs per SM
-constexpr size_t kGemvSmemBudget = 72 * 1024;  // shared copy of the records: 3 CTAs per SM
+constexpr int kGemvTabThreads = 512;            // persistent table-driven grid: 2 CTAs of 16 warps per SM
+constexpr int kGemvTabBlocks = 2;
+constexpr size_t kGemvSmemBudget = 100 * 1024;  // shared copy of the small decoder tables
 
 // acc += dot(8 bf16 activations, w[0..7])
 __device__ __forceinline__ float dot8(uint4 v, const float* w, float acc) {
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_decode_kernel(IndexSource i
 // state records to shared memory once (MODE 2) and its warps then take
 // output rows in turn.
 template <int MB, int MODE>
-__global__ void __launch_bounds__(kGemvThreads) gemv_tab_kernel(IndexSource index, int n_out, int bpr, DevBook book,
+__global__ void __launch_bounds__(kGemvTabThreads, kGemvTabBlocks) gemv_tab_kernel(IndexSource index, int n_out, int bpr, DevBook book,
                                                                  TabSmem L, const uint16_t* __restrict__ rscale,
                                                                  const __nv_bfloat16* __restrict__ a, int m, int k,
                                                                  float* __restrict__ y) {
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_tab_kernel(IndexSource inde
   if constexpr (MODE == 2) tab_smem_fill(book, dsm, L);
   __syncthreads();
   const TabCtx tc = tab_ctx<MODE == 2>(book, sh, dsm, L);
-  const int warp = threadIdx.x >> 5, warps = kGemvThreads / 32;
+  const int warp = threadIdx.x >> 5, warps = kGemvTabThreads / 32;
   for (int n = blockIdx.x * warps + warp; n < n_out; n += gridDim.x * warps)
     gemv_row<MB>(index, n, n_out, bpr, rscale, a, m, k, y,
                  [&](int64_t v, int (&w)[kDim]) { tab_decode<MODE == 2>(tc, v, w); });
@@ -140,14 +141,15 @@ cudaError_t gemv_decode_launch(const Codebook& cb, IndexSource idx, int64_t n_ou
   int sms = 0;
   cudaError_t e = device_sms(&sms);
   if (e != cudaSuccess) return e;
-  const unsigned grid = std::min<unsigned>(rows_grid, (unsigned)sms * kGemvTabBlocks);
+  const unsigned grid = std::min<unsigned>((unsigned)((n_out + kGemvTabThreads / 32 - 1) / (kGemvTabThreads / 32)),
+                                          (unsigned)sms * kGemvTabBlocks);
 #define LLVQ_GEMV(MB, MODE)                                                                              \
   do {                                                                                                   \
     if (smem > 48 * 1024 &&                                                                              \
         (e = cudaFuncSetAttribute(gemv_tab_kernel<MB, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                   (int)kGemvSmemBudget)) != cudaSuccess)                                 \
       return e;                                                                                          \
-    gemv_tab_kernel<MB, MODE><<<grid, kGemvThreads, smem, stream>>>(idx, n, b, cb.dev, L, rscale, ab, mm, kk, y); \
+    gemv_tab_kernel<MB, MODE><<<grid, kGemvTabThreads, smem, stream>>>(idx, n, b, cb.dev, L, rscale, ab, mm, kk, y); \
   } while (0)
   if (L.bytes) {
     if (m == 1) LLVQ_GEMV(1, 2);

@@ -94,11 +94,11 @@ struct TabView {
   const uint4* state;      // 2 per state
   const uint4* crec;       // 4 per class
   const uint4* entry;
-  const uint16_t* guide;
+  const uint4* slot;
   const unsigned long long* tail;
   const uint4* expand;     // per Golay word in weight order
   int n_states;
-  int max_jobs;            // lookups of the longest class (both parts)
+  int max_searches;        // searches of the longest class (both parts)
 };
 
 // Everything a kernel needs about one codebook (plain pointers, passed by value).

@@ -48,11 +48,11 @@ struct TabHost {
   std::vector<uint4> state;            // 2 per state
   std::vector<uint4> crec;             // 4 per class
   std::vector<uint4> entry;
-  std::vector<uint16_t> guide;
+  std::vector<uint4> slot;
   std::vector<unsigned long long> tail;
   std::vector<uint32_t> expand;        // per word in weight order
   std::vector<uint16_t> bucket;        // index bucket -> class (host copy for the host decoder)
-  int max_jobs = 0;
+  int max_searches = 0;
 };
 
 struct Codebook {

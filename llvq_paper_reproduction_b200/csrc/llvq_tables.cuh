@@ -12,12 +12,15 @@
 //     in rank order, so the rest of the sequence is entry `rank`;
 //   * a search state lists the orderings of its next h positions (h at most
 //     kTabHead) in rank order, each with the rank of its first completion
-//     and the state it leaves; a guide table over rank * G / N (N the number
+//     and the state it leaves; a slot table over rank * G / N (N the number
 //     of orderings of the state, G a power of two, the slot computed exactly)
-//     names the entry holding the slot's first rank, and flags the slots that
-//     reach into a second entry (only those compare with the next entry).
+//     holds, for a slot inside one entry, that entry itself (one gather), and
+//     for a slot that reaches into a second entry the number of the entry
+//     holding its first rank (then compared with the following entries).
 // A 24-position part is two searches and one tail; a 16-position part one
-// search and one tail; 12- and 8-position parts one tail.  Sequences are
+// search and one tail; 12- and 8-position parts one tail.  Every lane runs
+// its searches first (part A's, then part B's; at most tc.max_searches) and
+// then its tails, so the lanes of a warp run the same lookup code together.  Sequences are
 // nibble strings (value index j of the part in bits 4t..4t+3 for step t).
 // The two parts of an even class are then moved onto their positions (the
 // word's coordinates and the others) by a nibble-wise bit expand (the
@@ -37,17 +40,18 @@ constexpr int kTabHead = 6;               // positions one search covers
 constexpr uint32_t kTabEnd = 0xFFFFFFFFu; // no state: the part is empty / finished
 constexpr int kTabExpandWords = 40;       // u32 per Golay word in the expand table
 constexpr uint32_t kTabTailBit = 1u << 31;
-constexpr uint16_t kTabGuideAmbiguous = 0x8000;
-constexpr int kTabMaxStateEntries = 0x8000;  // entry numbers fit the guide's 15 bits
+constexpr uint32_t kTabSlotAmbiguous = 1u << 31;
+constexpr int kTabMaxStateEntries = 0x10000;
 
 // State record, two uint4:
 //   [0] tail:   x = first entry in `tail`, z = kTabTailBit | positions
-//       search: x = first entry in `entry`, y = first guide slot,
+//       search: x = first entry in `entry`, y = first slot,
 //               z = entries | log2 G << 16 | h << 21
 //   [1] search: N (u64, x | y << 32), G / N as fp64 bits (z | w << 32)
 // Search entry (uint4): {start low, start high, next state, nibbles of the h
-// positions}.  Guide slot g (u16): the entry holding rank ceil(g N / G), with
-// kTabGuideAmbiguous set when ceil((g + 1) N / G) - 1 lies in a later entry.
+// positions}; starts stay below 2^46.  Slot g (uint4) covers the ranks
+// ceil(g N / G) .. ceil((g + 1) N / G) - 1: the entry holding all of them, or
+// {number of the entry holding the first, kTabSlotAmbiguous, 0, 0}.
 //
 // Class record, four uint4 (64 bytes):
 //   [0] start of the class (u64), permutation count (u64)
@@ -99,24 +103,24 @@ inline int tab_msb(uint64_t u) { return 63 - __builtin_clzll(u); }
 
 LLVQ_HD uint64_t tab_u64(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
 
-// Where the decoder reads its tables.  srec (state records) and crec (class
-// records) point to shared-memory copies (plain loads, SMEM) or to global
-// memory (read-only cache loads); starts and deposit4 are read with plain
-// loads (shared memory in the kernels); the rest is global memory.
+// Where the decoder reads its tables.  The small ones marked SMEM point to
+// shared-memory copies (plain loads) or to global memory (read-only cache
+// loads); starts and deposit4 are read with plain loads (shared memory in
+// the kernels); the rest is global memory.
 struct TabCtx {
-  const uint4* srec;          // 2 per state
-  const uint4* crec;          // 4 per class
-  const int64_t* starts;      // class starts (binary search)
-  const uint16_t* bucket;     // index bucket -> class (global)
+  const uint4* srec;          // 2 per state                          (SMEM)
+  const uint4* crec;          // 4 per class                          (SMEM)
+  const uint16_t* bucket;     // index bucket -> class                (SMEM)
+  const uint32_t* words;      // Golay words in weight order          (SMEM)
+  const uint32_t* golay;      // Golay words in lexicographic order   (SMEM)
+  const int64_t* starts;      // class starts (binary search)         (plain loads)
+  const uint8_t* deposit4;    // [m * 16 + s]: the low popc(m) bits of s placed on the set bits of m (plain)
   const uint4* entry;
-  const uint16_t* guide;
+  const uint4* slot;
   const unsigned long long* tail;
   const uint4* expand;        // kTabExpandWords u32 per word, weight order
-  const uint32_t* words;      // Golay words in weight order
-  const uint32_t* golay;      // Golay words in lexicographic order
-  const uint8_t* deposit4;    // [m * 16 + s]: the low popc(m) bits of s placed on the set bits of m
   int n_classes;
-  int max_jobs;
+  int max_searches;           // searches of the longest class (both parts)
   int64_t total;
 };
 
@@ -126,29 +130,22 @@ LLVQ_HD T tab_ldr(const T* p) {
   else return tab_ldg(p);
 }
 
-// One lookup: from state s with rank r, the nibbles of the positions it
-// covers (`take` of them); s becomes the next state (kTabEnd after a tail).
+// One search from search state s (record r0) with rank r: the nibbles of
+// the h positions it covers; s becomes the state left, r the rank within it.
 template <bool SMEM>
-LLVQ_HD void tab_job(const TabCtx& tc, uint32_t& s, uint64_t& r, uint64_t& nib, int& take) {
-  const uint4 r0 = tab_ldr<SMEM>(tc.srec + 2 * s);
-  if (r0.z & kTabTailBit) {
-    nib = tab_ldg(tc.tail + r0.x + r);
-    take = (int)(r0.z & 31u);
-    s = kTabEnd;
-    return;
-  }
+LLVQ_HD void tab_search(const TabCtx& tc, const uint4& r0, uint32_t& s, uint64_t& r, uint64_t& nib, int& take) {
   const uint4 r1 = tab_ldr<SMEM>(tc.srec + 2 * s + 1);
-  const uint32_t n = r0.z & 0xFFFFu, lg = (r0.z >> 16) & 31u;
+  const uint32_t n = r0.z & 0x1FFFFu, lg = (r0.z >> 17) & 31u;
   const uint64_t N = tab_u64(r1.x, r1.y), rg = r << lg;
   // slot g = floor(r G / N): an fp64 estimate, corrected exactly (N (G + 1) < 2^64)
   uint64_t g = (uint64_t)((double)r * tab_bits2d(r1.z, r1.w));
   if ((g + 1) * N <= rg) ++g;
   else if (g * N > rg) --g;
-  const uint32_t gv = tab_ldg(tc.guide + r0.y + (uint32_t)g);
-  const uint4* ent = tc.entry + r0.x;
-  uint32_t j = gv & 0x7FFFu;
-  uint4 e = tab_ldg(ent + j);
-  if (gv & kTabGuideAmbiguous) {
+  uint4 e = tab_ldg(tc.slot + r0.y + (uint32_t)g);
+  if (e.y & kTabSlotAmbiguous) {
+    const uint4* ent = tc.entry + r0.x;
+    uint32_t j = e.x;
+    e = tab_ldg(ent + j);
     while (j + 1 < n) {
       const uint2 nx = tab_ldg(reinterpret_cast<const uint2*>(ent + j + 1));
       if (tab_u64(nx.x, nx.y) > r) break;
@@ -159,7 +156,7 @@ LLVQ_HD void tab_job(const TabCtx& tc, uint32_t& s, uint64_t& r, uint64_t& nib, 
   r -= tab_u64(e.x, e.y);
   s = e.z;
   nib = e.w;
-  take = (int)((r0.z >> 21) & 15u);
+  take = (int)((r0.z >> 22) & 15u);
 }
 
 LLVQ_HD void tab_put(uint64_t& lo, uint64_t& hi, uint64_t nib, int t) {
@@ -226,24 +223,42 @@ template <bool SMEM>
 LLVQ_HD void tab_magnitudes(const TabCtx& tc, uint32_t sa, uint64_t ra, uint32_t sb, uint64_t rb, int word_slot,
                             bool spread, int d0, uint64_t vals, uint32_t (&mag)[6]) {
   uint64_t a_lo = 0, a_hi = 0, b_lo = 0, b_hi = 0;
-  bool in_b = sa == kTabEnd;
-  uint32_t s = in_b ? sb : sa;
-  uint64_t r = in_b ? rb : ra;
-  int t = 0;
-  for (int job = 0; job < tc.max_jobs; ++job) {
-    if (s == kTabEnd) break;
-    uint64_t nib;
-    int take;
-    tab_job<SMEM>(tc, s, r, nib, take);
-    if (in_b) tab_put(b_lo, b_hi, nib, t);
-    else tab_put(a_lo, a_hi, nib, t);
-    t += take;
-    if (s == kTabEnd && !in_b) {
+  int ta = 0, tb = 0;
+  // searches: part A's, then part B's, one per iteration
+  for (int it = 0; it < tc.max_searches; ++it) {
+    uint4 r0 = make_uint4(0, 0, kTabTailBit, 0);
+    bool in_b = false;
+    if (sa != kTabEnd) r0 = tab_ldr<SMEM>(tc.srec + 2 * sa);
+    if (r0.z & kTabTailBit) {
       in_b = true;
-      s = sb;
-      r = rb;
-      t = 0;
+      r0 = make_uint4(0, 0, kTabTailBit, 0);
+      if (sb != kTabEnd) r0 = tab_ldr<SMEM>(tc.srec + 2 * sb);
     }
+    if (r0.z & kTabTailBit) continue;  // both parts are at their tails
+    uint32_t s = in_b ? sb : sa;
+    uint64_t r = in_b ? rb : ra, nib;
+    int take;
+    tab_search<SMEM>(tc, r0, s, r, nib, take);
+    if (in_b) {
+      tab_put(b_lo, b_hi, nib, tb);
+      tb += take;
+      sb = s;
+      rb = r;
+    } else {
+      tab_put(a_lo, a_hi, nib, ta);
+      ta += take;
+      sa = s;
+      ra = r;
+    }
+  }
+  // tails: the rest of each part is one entry
+  if (sa != kTabEnd) {
+    const uint4 r0 = tab_ldr<SMEM>(tc.srec + 2 * sa);
+    tab_put(a_lo, a_hi, tab_ldg(tc.tail + r0.x + ra), ta);
+  }
+  if (sb != kTabEnd) {
+    const uint4 r0 = tab_ldr<SMEM>(tc.srec + 2 * sb);
+    tab_put(b_lo, b_hi, tab_ldg(tc.tail + r0.x + rb), tb);
   }
   // part A value indices follow the d0 part-B values (no nibble overflows:
   // indices stay below 8, and the nibbles past the part's end are dropped by
@@ -342,6 +357,7 @@ LLVQ_HD uint64_t tab_divmod(uint64_t a, uint64_t b, uint64_t magic, uint64_t& re
 // Class of a valid index: the bucket of its leading bit and next four bits
 // narrows the search to the classes between the owners of the bucket's lowest
 // index and of the next bucket's.
+template <bool SMEM>
 LLVQ_HD int tab_find_class(const TabCtx& tc, int64_t v) {
   const uint64_t u = (uint64_t)v;
   int key = 0;
@@ -349,7 +365,7 @@ LLVQ_HD int tab_find_class(const TabCtx& tc, int64_t v) {
     const int e = tab_msb(u);
     key = 1 + e * 16 + (int)((e >= 4 ? u >> (e - 4) : u << (4 - e)) & 15u);
   }
-  int lo = tab_ldg(tc.bucket + key), hi = tab_ldg(tc.bucket + key + 1) + 1;
+  int lo = tab_ldr<SMEM>(tc.bucket + key), hi = tab_ldr<SMEM>(tc.bucket + key + 1) + 1;
   while (lo + 1 < hi) {
     const int mid = (lo + hi) >> 1;
     if (tc.starts[mid] <= v) lo = mid; else hi = mid;
@@ -365,7 +381,7 @@ LLVQ_HD bool tab_decode(const TabCtx& tc, int64_t v, int (&y)[kDim]) {
     for (int d = 0; d < kDim; ++d) y[d] = 0;
     return false;
   }
-  const int k = tab_find_class(tc, v);
+  const int k = tab_find_class<SMEM>(tc, v);
   const uint4* cp = tc.crec + 4 * k;
   const uint4 c0 = tab_ldr<SMEM>(cp), c1 = tab_ldr<SMEM>(cp + 1), c2 = tab_ldr<SMEM>(cp + 2),
               c3 = tab_ldr<SMEM>(cp + 3);
@@ -381,12 +397,12 @@ LLVQ_HD bool tab_decode(const TabCtx& tc, int64_t v, int (&y)[kDim]) {
   int slot;
   uint64_t sign = 0, ra = prank, rb = 0;
   if (odd) {
-    word = tab_ldg(tc.golay + (int)cur);
+    word = tab_ldr<SMEM>(tc.golay + (int)cur);
     slot = kNumGolay - 1;
   } else {
     sign = cur & ((1ull << sshift) - 1);
     slot = (int)c3.x + (int)(cur >> sshift);
-    word = tab_ldg(tc.words + slot);
+    word = tab_ldr<SMEM>(tc.words + slot);
     uint64_t r1;
     rb = tab_divmod(prank, f1p, magic_f1, r1);
     ra = r1;
