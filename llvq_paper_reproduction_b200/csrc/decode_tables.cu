@@ -134,37 +134,57 @@ struct Builder {
         if (cursor != n) return fail("prefix counts do not add up");
         if (pre.size() >= (size_t)kTabMaxStateEntries) return fail("a search state has too many prefixes");
         if (t.entry.size() + pre.size() > kTabMaxEntries) return fail("search tables too large");
-        int lg = 0;
-        while ((1u << lg) < 4 * pre.size()) ++lg;
-        const uint32_t slots = 1u << lg;
-        if ((n * (u128)(slots + 1)) >> 63) return fail("slot arithmetic would overflow");
-        if (t.slot.size() + slots > kTabMaxEntries) return fail("slot tables too large");
-        r0.x = (uint32_t)t.entry.size();
-        r0.y = (uint32_t)t.slot.size();
-        r0.z = (uint32_t)pre.size() | ((uint32_t)lg << 17) | ((uint32_t)h << 22);
+        // slot function g(r) = umulhi((u32)(r >> s), M): s makes r >> s fit
+        // 32 bits, M spreads the ranks over about kTabSlotsPerEntry slots per
+        // entry (M <= G 2^32 / (qmax + 1) keeps g below G)
         const uint64_t n64 = (uint64_t)n;
-        const double gn = (double)slots / (double)n64;
-        uint64_t gbits;
-        std::memcpy(&gbits, &gn, 8);
-        r1 = make_uint4((uint32_t)n64, (uint32_t)(n64 >> 32), (uint32_t)gbits, (uint32_t)(gbits >> 32));
+        int sh = 0;
+        while (((n64 - 1) >> sh) >> 32) ++sh;
+        const uint64_t qmax = (n64 - 1) >> sh;
+        uint64_t want = 1;
+        while (want < (uint64_t)kTabSlotsPerEntry * pre.size()) want <<= 1;
+        const u128 mw = ((u128)want << 32) / (u128)(qmax + 1);
+        const uint32_t M = mw > 0xFFFFFFFFu ? 0xFFFFFFFFu : (mw ? (uint32_t)mw : 1u);
+        auto gof = [&](uint64_t r) { return (uint32_t)(((uint64_t)(uint32_t)(r >> sh) * M) >> 32); };
+        const uint32_t slots = gof(n64 - 1) + 1;
+        if (t.slot.size() / 2 + slots > kTabMaxEntries) return fail("slot tables too large");
+        r0.x = (uint32_t)(t.slot.size() / 2);
+        r0.y = M;
+        r0.z = (uint32_t)sh | ((uint32_t)h << 8);
+        r0.w = (uint32_t)t.entry.size();
+        r1 = make_uint4((uint32_t)n64, (uint32_t)(n64 >> 32), (uint32_t)pre.size(), 0);
         const size_t e0 = t.entry.size();
         for (const Prefix& p : pre)
           t.entry.push_back({(uint32_t)(uint64_t)p.start, (uint32_t)((uint64_t)p.start >> 32), p.next, p.nib});
-        // slot g holds the ranks ceil(g N / G) .. ceil((g + 1) N / G) - 1
-        auto entry_of = [&](u128 rank) {
+        auto entry_of = [&](uint64_t rank) {
           size_t lo = 0, hi = pre.size();
           while (lo + 1 < hi) {
             const size_t mid = (lo + hi) / 2;
-            if (pre[mid].start <= rank) lo = mid; else hi = mid;
+            if ((uint64_t)pre[mid].start <= rank) lo = mid; else hi = mid;
           }
           return lo;
         };
+        // first rank of slot g: the smallest q with umulhi(q, M) >= g, shifted back
+        auto first_rank = [&](uint32_t g) -> uint64_t {
+          const uint64_t q = (uint64_t)((((u128)g << 32) + M - 1) / M);
+          return q << sh;
+        };
         for (uint32_t g = 0; g < slots; ++g) {
-          const u128 first = ((u128)g * n + slots - 1) / slots;
-          const u128 next = ((u128)(g + 1) * n + slots - 1) / slots;
-          const size_t j = entry_of(first < n ? first : n - 1);
-          const bool ambiguous = next > first && entry_of(next - 1) != j;
-          t.slot.push_back(ambiguous ? make_uint4((uint32_t)j, kTabSlotAmbiguous, 0, 0) : t.entry[e0 + j]);
+          const uint64_t lo = first_rank(g);
+          const uint64_t hi = g + 1 < slots ? first_rank(g + 1) : n64;
+          if (lo >= hi || gof(lo) != g || (lo && gof(lo - 1) >= g)) return fail("slot function is not monotone");
+          const size_t j = entry_of(lo);
+          size_t inside = 0;
+          for (size_t e = j + 1; e < pre.size() && (uint64_t)pre[e].start < hi; ++e) ++inside;
+          t.slot.push_back(t.entry[e0 + j]);
+          if (inside == 0) {
+            t.slot.push_back(make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0));
+          } else if (inside == 1) {
+            t.slot.push_back(t.entry[e0 + j + 1]);
+          } else {
+            const uint4& nx = t.entry[e0 + j + 1];
+            t.slot.push_back(make_uint4(nx.x, nx.y, kTabSlotMulti, (uint32_t)(j + 1)));
+          }
         }
       }
       t.state.push_back(r0);
@@ -177,7 +197,7 @@ struct Builder {
       const uint4& r0 = t.state[2 * s];
       if (r0.z & kTabTailBit) continue;
       int d = 0;
-      for (uint32_t e = 0; e < (r0.z & 0x1FFFFu); ++e) d = std::max(d, depth[t.entry[r0.x + e].z]);
+      for (uint32_t e = 0; e < t.state[2 * s + 1].z; ++e) d = std::max(d, depth[t.entry[r0.w + e].z]);
       depth[s] = 1 + d;
     }
     return true;
@@ -290,7 +310,9 @@ bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
     }
   }
   if (!b.run()) return bad(b.why);
-  t.crec.assign(4 * n, uint4{0, 0, 0, 0});
+  if ((uint64_t)cb.total >> 48) return bad("the codebook has 2^48 or more codewords");
+  if (b.keys.size() >= 0xFFFFu) return bad("more than 65534 decoder states");
+  t.crec.assign(kTabClassRecords * n, uint4{0, 0, 0, 0});
   for (size_t k = 0; k < n; ++k) {
     const DevClass& c = cb.cls[k];
     const uint2 st = parts[k];
@@ -306,15 +328,25 @@ bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
       for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
       for (int j = 0; j < c.nv1; ++j) vals |= (uint64_t)(uint8_t)c.v1[j] << (8 * (d0 + j));
     }
+    int shape = kShapeOdd24;
+    if (!c.parity)
+      shape = c.even_weight == 0 || c.even_weight == kDim ? kShapeEven24
+              : c.even_weight == 12                        ? kShapeEven12
+                                                           : kShapeEven16;
+    // the part that is searched (P1) and the tail-only part (P2)
+    const bool p1a = shape == kShapeOdd24 || shape == kShapeEven12 || c.even_weight >= 16;
+    const uint32_t s1 = p1a ? st.x : st.y, s2 = shape >= kShapeEven16 ? (p1a ? st.y : st.x) : 0xFFFFu;
     const uint64_t start = (uint64_t)c.start, perm = c.perm_count;
     const uint64_t mp = ~0ull / perm, mf = ~0ull / c.f1_perm;
-    const uint32_t meta = (uint32_t)c.parity | ((uint32_t)c.even_weight << 1) | ((uint32_t)c.sign_shift << 6) |
-                          ((uint32_t)d0 << 11) | ((uint32_t)c.required << 15);
-    uint4* r = t.crec.data() + 4 * k;
-    r[0] = make_uint4((uint32_t)start, (uint32_t)(start >> 32), (uint32_t)perm, (uint32_t)(perm >> 32));
-    r[1] = make_uint4((uint32_t)mp, (uint32_t)(mp >> 32), (uint32_t)mf, (uint32_t)(mf >> 32));
-    r[2] = make_uint4((uint32_t)vals, (uint32_t)(vals >> 32), (uint32_t)c.f1_perm, meta);
-    r[3] = make_uint4((uint32_t)(c.parity ? 0 : cb.weight_start[c.even_weight]), st.x, st.y, 0);
+    const uint32_t meta = (uint32_t)shape | ((uint32_t)c.sign_shift << 2) | ((uint32_t)c.required << 7) |
+                          ((uint32_t)(c.even_weight == kDim) << 8) | ((uint32_t)p1a << 9);
+    uint4* r = t.crec.data() + kTabClassRecords * k;
+    r[0] = make_uint4((uint32_t)start, (uint32_t)(start >> 32) | (meta << 16), (uint32_t)perm,
+                      (uint32_t)(perm >> 32) | (s1 << 16));
+    r[1] = make_uint4((uint32_t)mp, (uint32_t)(mp >> 32), (uint32_t)vals, (uint32_t)(vals >> 32));
+    const uint32_t wbase = c.parity ? 0u : (uint32_t)cb.weight_start[c.even_weight];
+    r[2] = make_uint4((uint32_t)mf, (uint32_t)(mf >> 32), (uint32_t)c.f1_perm,
+                      (s2 & 0xFFFFu) | (wbase << 16) | ((uint32_t)d0 << 28));
   }
   t.bucket.assign(kBuckets + 1, 0);
   for (int bk = 0; bk <= kBuckets; ++bk) {  // owner class of each bucket's lowest index
@@ -367,6 +399,7 @@ TabCtx host_tab_ctx(const Codebook& cb) {
   tc.tail = t.tail.data();
   tc.expand = reinterpret_cast<const uint4*>(t.expand.data());
   tc.n_classes = (int)cb.cls.size();
+  tc.n_states = (int)(t.state.size() / 2);
   tc.max_searches = t.max_searches;
   tc.total = cb.total;
   return tc;

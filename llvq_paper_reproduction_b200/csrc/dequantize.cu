@@ -3,7 +3,9 @@
 // Reference: LeechLatticeVectorQuantizerGpu.dequantize / dequantize_lattice
 // (impl/leech_lattice_vector_quantizer_gpu.py:267-298) and its NVRTC kernel
 // (impl/llvq_cuda_dequantize.py:78-181).  One thread decodes one index in
-// registers (llvq_decode.cuh) and writes it with 16-byte vector stores.
+// registers -- with the table-driven decoder (llvq_tables.cuh) when the
+// codebook has tables, else by arithmetic unranking (llvq_decode.cuh) -- and
+// writes it with 16-byte vector stores.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -28,11 +30,14 @@ constexpr int kDeqMinBlocks = 5;
 // memory, or from a shared-memory copy (the usual case: a persistent grid
 // copies them once per CTA).
 enum { kModeArith = 0, kModeTabGlobal = 1, kModeTabShared = 2 };
-constexpr int kTabThreads = 512;   // persistent table-driven kernels: 2 CTAs of 512 threads per SM
+// Persistent table-driven kernels: 2 CTAs of 512 threads per SM (64
+// registers, no spills; 768-thread CTAs at 40 registers spill and ran 7%
+// slower on the Llama-3-8B dequant workload).
+constexpr int kTabThreads = 512;
 constexpr int kTabMinBlocks = 2;
 constexpr size_t kTabSmemBudget = 100 * 1024;
 
-// Output of one decoded block in every kind.
+// Output of one decoded block in every kind (arithmetic decoder).
 template <int KIND>
 __device__ __forceinline__ void store_block(const int (&y)[kDim], int64_t i, void* __restrict__ out,
                                             const uint16_t* __restrict__ row_scale, int64_t blocks_per_row,
@@ -87,9 +92,109 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(Ind
   store_block<KIND>(y, i, out, row_scale, blocks_per_row, magic_bpr);
 }
 
-// Table-driven dequantizer: a persistent grid; each CTA copies the class and
-// state records to shared memory once (MODE kModeTabShared) and then strides
-// over the indices.
+// ------------------------------------------------- table-driven decoder
+//
+// The decoded form is the 24 magnitudes by position (mag[w], byte j =
+// position 4w + j) and the mask of negative coordinates; the stores build
+// every output kind from it without forming the signed integers.
+
+// 2^23 + m as fp32 bits for the magnitude in byte j of w (m < 256).
+__device__ __forceinline__ float mag_float_2p23(uint32_t w, int j) {
+  return __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)j));
+}
+// fp32(fp32(1/sqrt 8) * m) in one rounding: (2^23 + m) * c - 2^23 * c.
+__device__ __forceinline__ float mag_scaled(uint32_t w, int j) {
+  return fmaf(mag_float_2p23(w, j), kLatticeScaleF, -8388608.0f * kLatticeScaleF);
+}
+// Sign bits of positions 2p and 2p + 1 of neg, as the sign bits of a bf16 pair.
+__device__ __forceinline__ uint32_t bf16_pair_signs(uint32_t neg, int p) {
+  return (((neg >> (2 * p)) & 3u) * 0x40008000u) & 0x80008000u;
+}
+__device__ __forceinline__ uint32_t bf16_pair(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Output of one decoded index in every kind (streaming stores).  The sign
+// is applied last (an exact negation of the rounded magnitude product,
+// since round-to-nearest is symmetric).
+template <int KIND>
+__device__ __forceinline__ void store_mn(const uint32_t (&mag)[6], uint32_t neg, int64_t i, void* __restrict__ out,
+                                         const uint16_t* __restrict__ row_scale, int64_t blocks_per_row,
+                                         uint64_t magic_bpr) {
+  if constexpr (KIND == 0) {
+    longlong2* o = reinterpret_cast<longlong2*>(static_cast<long long*>(out) + i * kDim);
+#pragma unroll
+    for (int d = 0; d < kDim; d += 2) {
+      const long long a = (mag[d >> 2] >> (8 * (d & 3))) & 0xFFu, b = (mag[d >> 2] >> (8 * ((d + 1) & 3))) & 0xFFu;
+      __stcs(o + d / 2, make_longlong2(((neg >> d) & 1u) ? -a : a, ((neg >> (d + 1)) & 1u) ? -b : b));
+    }
+  } else if constexpr (KIND == 1) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + i * kDim);
+#pragma unroll
+    for (int d = 0; d < kDim; d += 4) {
+      float f[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        f[e] = __int_as_float(__float_as_int(mag_scaled(mag[d >> 2], e)) ^ (int)(((neg >> (d + e)) & 1u) << 31));
+      __stcs(o + d / 4, make_float4(f[0], f[1], f[2], f[3]));
+    }
+  } else if constexpr (KIND == 2) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + i * kDim);
+#pragma unroll
+    for (int d = 0; d < kDim; d += 4) {
+      float f[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int m = (int)((mag[d >> 2] >> (8 * e)) & 0xFFu);
+        f[e] = (float)(kLatticeScaleD * (double)(((neg >> (d + e)) & 1u) ? -m : m));
+      }
+      __stcs(o + d / 4, make_float4(f[0], f[1], f[2], f[3]));
+    }
+  } else {
+    uint64_t col;  // row = i / blocks_per_row by multiply-high with an exact correction
+    const uint64_t row = div_magic((uint64_t)i, (uint64_t)blocks_per_row, magic_bpr, col);
+    const float s = __half2float(__ushort_as_half(__ldg(row_scale + row)));
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + i * kDim);
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int p = 4 * q + e;  // bf16 pair p: positions 2p, 2p + 1
+        const uint32_t mw = mag[p >> 1];
+        const int j = 2 * (p & 1);
+        w[e] = bf16_pair(__fmul_rn(mag_scaled(mw, j), s), __fmul_rn(mag_scaled(mw, j + 1), s)) ^
+               bf16_pair_signs(neg, p);
+      }
+      __stcs(o + q, make_uint4(w[0], w[1], w[2], w[3]));
+    }
+  }
+}
+
+__device__ __forceinline__ int64_t load_index_stream(IndexSource src, int64_t i) {
+  if (src.bytes == 8) return __ldcs(static_cast<const long long*>(src.ptr) + i);
+  return load_index(src, i);
+}
+
+// Decode of a valid or invalid index into (mag, neg); false (and zeros)
+// outside the codebook.
+template <bool SMEM>
+__device__ __forceinline__ bool tab_decode_any(const TabCtx& tc, int64_t v, uint32_t (&mag)[6], uint32_t& neg) {
+  bool ok = v >= 0 && v < tc.total;
+  neg = 0;
+  if (ok) ok = tab_decode_mn<SMEM>(tc, v, tab_find_class<SMEM>(tc, v), mag, neg);
+  if (!ok) {
+#pragma unroll
+    for (int w = 0; w < 6; ++w) mag[w] = 0;
+    neg = 0;
+  }
+  return ok;
+}
+
+// Table-driven dequantizer: a persistent grid; each CTA copies the small
+// tables to shared memory once (MODE kModeTabShared) and then strides over
+// the indices, loading the next index before decoding the current one.
 template <int KIND, int MODE>
 __global__ void __launch_bounds__(kTabThreads, kTabMinBlocks) dequant_tab_kernel(
     IndexSource index, int64_t n, DevBook book, TabSmem L, void* __restrict__ out,
@@ -101,11 +206,19 @@ __global__ void __launch_bounds__(kTabThreads, kTabMinBlocks) dequant_tab_kernel
   __syncthreads();
   const TabCtx tc = tab_ctx<MODE == kModeTabShared>(book, sh, dsm, L);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    int y[kDim];
-    const bool ok = tab_decode<MODE == kModeTabShared>(tc, load_index(index, i), y);
-    if (!ok && error_count) atomicAdd(error_count, 1);
-    store_block<KIND>(y, i, out, row_scale, blocks_per_row, magic_bpr);
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t v = i < n ? load_index_stream(index, i) : 0;
+  int errors = 0;
+  for (; i < n; i += stride) {
+    const int64_t vn = i + stride < n ? load_index_stream(index, i + stride) : 0;
+    uint32_t mag[6], neg;
+    if (!tab_decode_any<MODE == kModeTabShared>(tc, v, mag, neg)) ++errors;
+    store_mn<KIND>(mag, neg, i, out, row_scale, blocks_per_row, magic_bpr);
+    v = vn;
+  }
+  if (error_count) {
+    const int e = __reduce_add_sync(0xFFFFFFFFu, errors);
+    if ((threadIdx.x & 31) == 0 && e) atomicAdd(error_count, e);
   }
 }
 
@@ -147,34 +260,54 @@ __global__ void __launch_bounds__(kDeqThreads) decode_rows_bf16_kernel(IndexSour
   }
 }
 
+// Staging decode with the table-driven decoder: the indices [rows, bpr]
+// decode to bf16 integer codewords at out[r * ldw + 24 b]; columns 24 bpr ..
+// ldw - 1 of every row are zeroed.
 template <int MODE>
 __global__ void __launch_bounds__(kTabThreads, kTabMinBlocks) decode_rows_tab_kernel(
     IndexSource index, int rows, int bpr, int ldw, DevBook book, TabSmem L, __nv_bfloat16* __restrict__ out,
-    uint64_t magic_per_row) {
+    uint64_t magic_bpr) {
   extern __shared__ __align__(16) uint8_t dsm[];
   DecodeSharedBase& sh = *reinterpret_cast<DecodeSharedBase*>(dsm);
   decode_setup_base(book, sh);
   if constexpr (MODE == kModeTabShared) tab_smem_fill(book, dsm, L);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int pad = (ldw - bpr * kDim) / 8;  // 16-byte groups of zero padding per row
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)rows * pad; i += stride) {
+    const int64_t r = i / pad, c = i - r * pad;
+    *reinterpret_cast<uint4*>(out + r * ldw + bpr * kDim + c * 8) = make_uint4(0, 0, 0, 0);
+  }
   __syncthreads();
   const TabCtx tc = tab_ctx<MODE == kModeTabShared>(book, sh, dsm, L);
-  const int per_row = ldw / kDim + 1;
-  const int64_t total = (int64_t)rows * per_row, stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    uint64_t bq;
-    const int r = (int)div_magic((uint64_t)i, (uint64_t)per_row, magic_per_row, bq), b = (int)bq;
-    __nv_bfloat16* o = out + (int64_t)r * ldw;
-    if (b < bpr) {
-      int y[kDim];
-      tab_decode<MODE == kModeTabShared>(tc, load_index(index, (int64_t)r * bpr + b), y);
-      store_staged(y, o, b);
-    } else if (b == bpr) {
-      for (int c = bpr * kDim; c < ldw; c += 8) *reinterpret_cast<uint4*>(o + c) = make_uint4(0, 0, 0, 0);
+  const int64_t n = (int64_t)rows * bpr;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t v = i < n ? load_index_stream(index, i) : 0;
+  for (; i < n; i += stride) {
+    const int64_t vn = i + stride < n ? load_index_stream(index, i + stride) : 0;
+    uint32_t mag[6], neg;
+    tab_decode_any<MODE == kModeTabShared>(tc, v, mag, neg);
+    uint64_t b;
+    const uint64_t r = div_magic((uint64_t)i, (uint64_t)bpr, magic_bpr, b);
+    uint4* o = reinterpret_cast<uint4*>(out + r * ldw + b * kDim);
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int p = 4 * q + e;
+        const uint32_t mw = mag[p >> 1];
+        const int j = 2 * (p & 1);
+        w[e] = bf16_pair(mag_float_2p23(mw, j) - 8388608.0f, mag_float_2p23(mw, j + 1) - 8388608.0f) ^
+               bf16_pair_signs(neg, p);
+      }
+      o[q] = make_uint4(w[0], w[1], w[2], w[3]);
     }
+    v = vn;
   }
 }
 
 // Launch shape of the table-driven kernels for a codebook: the shared copy
-// when it fits, a persistent grid of at most `per_sm` CTAs per SM.
+// when it fits, a persistent grid of at most kTabMinBlocks CTAs per SM.
 struct TabLaunch {
   int mode;
   TabSmem L;
@@ -206,12 +339,11 @@ static unsigned tab_grid(int64_t work) {
 cudaError_t decode_rows_bf16_launch(const Codebook& cb, IndexSource index, int rows, int bpr, int ldw, void* out,
                                     cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  const int64_t n = (int64_t)rows * (ldw / kDim + 1);
-  const uint64_t magic = ~0ull / (uint64_t)(ldw / kDim + 1);
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (cb.dev.tab.state) {
     const TabLaunch t = tab_launch(cb);
-    const unsigned grid = tab_grid(n);
+    const unsigned grid = tab_grid((int64_t)rows * bpr);
+    const uint64_t magic = ~0ull / (uint64_t)bpr;
     cudaError_t e;
     if (t.mode == kModeTabShared) {
       if ((e = allow_smem(decode_rows_tab_kernel<kModeTabShared>, t.smem)) != cudaSuccess) return e;
@@ -222,8 +354,9 @@ cudaError_t decode_rows_bf16_launch(const Codebook& cb, IndexSource index, int r
                                                                                   t.L, o, magic);
     }
   } else {
+    const int64_t n = (int64_t)rows * (ldw / kDim + 1);
     decode_rows_bf16_kernel<<<(unsigned)((n + kDeqThreads - 1) / kDeqThreads), kDeqThreads, 0, stream>>>(
-        index, rows, bpr, ldw, cb.dev, o, magic);
+        index, rows, bpr, ldw, cb.dev, o, ~0ull / (uint64_t)(ldw / kDim + 1));
   }
   return cudaGetLastError();
 }

@@ -550,41 +550,48 @@ __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, Dec
 // in bytes from the start of dynamic shared memory; bytes == 0 when the copy
 // would not fit (the decoder then reads them from global memory).
 struct TabSmem {
-  uint32_t bucket, words, golay, crec, srec, bytes;
+  uint32_t bucket, words, golay, crec, srec, extra, bytes;
 };
 
-inline TabSmem tab_smem_layout(int n_classes, int n_states, size_t budget) {
+// `extra` bytes (16-byte aligned) after the tables for the kernel's own use.
+inline TabSmem tab_smem_layout(int n_classes, int n_states, size_t budget, size_t extra = 0) {
   TabSmem L{};
   size_t off = (sizeof(DecodeSharedBase) + 15) / 16 * 16;
-  const size_t bucket = off; off += ((size_t)(kBuckets + 1) * 2 + 15) / 16 * 16;
+  const size_t bucket = off; off += ((size_t)kBuckets * 4 + 15) / 16 * 16;
   const size_t words = off; off += (size_t)kNumGolay * 4;
   const size_t golay = off; off += (size_t)kNumGolay * 4;
-  const size_t crec = off; off += (size_t)n_classes * 64;
+  const size_t crec = off; off += (size_t)n_classes * 16 * kTabClassRecords;
   const size_t srec = off; off += (size_t)n_states * 32;
+  const size_t ext = off; off += (extra + 15) / 16 * 16;
   if (n_classes > kMaxSmemClasses || off > budget) return L;
   L.bucket = (uint32_t)bucket;
   L.words = (uint32_t)words;
   L.golay = (uint32_t)golay;
   L.crec = (uint32_t)crec;
   L.srec = (uint32_t)srec;
+  L.extra = (uint32_t)ext;
   L.bytes = (uint32_t)off;
   return L;
 }
 
 // Fill the shared copy (whole block; call __syncthreads() afterwards).
 __device__ __forceinline__ void tab_smem_fill(const DevBook& book, uint8_t* smem, const TabSmem& L) {
-  uint16_t* bucket = reinterpret_cast<uint16_t*>(smem + L.bucket);
+  uint32_t* bucket = reinterpret_cast<uint32_t*>(smem + L.bucket);
   uint32_t* words = reinterpret_cast<uint32_t*>(smem + L.words);
   uint32_t* golay = reinterpret_cast<uint32_t*>(smem + L.golay);
   uint4* crec = reinterpret_cast<uint4*>(smem + L.crec);
   uint4* srec = reinterpret_cast<uint4*>(smem + L.srec);
-  for (int i = threadIdx.x; i <= kBuckets; i += blockDim.x) bucket[i] = __ldg(book.bucket + i);
+  for (int i = threadIdx.x; i < kBuckets; i += blockDim.x)
+    bucket[i] = (uint32_t)__ldg(book.bucket + i) | ((uint32_t)__ldg(book.bucket + i + 1) << 16);
   for (int i = threadIdx.x; i < kNumGolay; i += blockDim.x) {
     words[i] = __ldg(book.wlist_word + i);
     golay[i] = __ldg(book.golay + i);
   }
-  for (int i = threadIdx.x; i < 4 * book.n_classes; i += blockDim.x) crec[i] = __ldg(book.tab.crec + i);
-  for (int i = threadIdx.x; i < 2 * book.tab.n_states; i += blockDim.x) srec[i] = __ldg(book.tab.state + i);
+  // field-major: record j of class k at j * n_classes + k (spreads a warp's random records over the banks)
+  for (int i = threadIdx.x; i < kTabClassRecords * book.n_classes; i += blockDim.x)
+    crec[(i % kTabClassRecords) * book.n_classes + i / kTabClassRecords] = __ldg(book.tab.crec + i);
+  for (int i = threadIdx.x; i < 2 * book.tab.n_states; i += blockDim.x)
+    srec[(i & 1) * book.tab.n_states + (i >> 1)] = __ldg(book.tab.state + i);
 }
 
 // The decoder's view of the tables: the small ones from the shared copy
@@ -596,7 +603,8 @@ __device__ __forceinline__ TabCtx tab_ctx(const DevBook& book, const DecodeShare
   TabCtx tc;
   tc.srec = SMEM ? reinterpret_cast<const uint4*>(smem + L.srec) : book.tab.state;
   tc.crec = SMEM ? reinterpret_cast<const uint4*>(smem + L.crec) : book.tab.crec;
-  tc.bucket = SMEM ? reinterpret_cast<const uint16_t*>(smem + L.bucket) : book.bucket;
+  tc.bucket = book.bucket;
+  tc.bucket2 = SMEM ? reinterpret_cast<const uint32_t*>(smem + L.bucket) : nullptr;
   tc.words = SMEM ? reinterpret_cast<const uint32_t*>(smem + L.words) : book.wlist_word;
   tc.golay = SMEM ? reinterpret_cast<const uint32_t*>(smem + L.golay) : book.golay;
   tc.starts = book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start;
@@ -606,6 +614,7 @@ __device__ __forceinline__ TabCtx tab_ctx(const DevBook& book, const DecodeShare
   tc.tail = book.tab.tail;
   tc.expand = book.tab.expand;
   tc.n_classes = book.n_classes;
+  tc.n_states = book.tab.n_states;
   tc.max_searches = book.tab.max_searches;
   tc.total = book.total;
   return tc;

@@ -92,7 +92,7 @@ constexpr int kTailSeqs = 1 << (2 * kTailLen);
 // llvq_tables.cuh); state == nullptr when the codebook is not tabulated.
 struct TabView {
   const uint4* state;      // 2 per state
-  const uint4* crec;       // 4 per class
+  const uint4* crec;       // 3 per class
   const uint4* entry;
   const uint4* slot;
   const unsigned long long* tail;

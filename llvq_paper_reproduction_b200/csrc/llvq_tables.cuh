@@ -8,25 +8,28 @@
 // Here a part's sequence comes from a few table lookups instead, keyed by the
 // multiset still to place (a "state": the counts of the part's values that
 // remain, shared by every class with the same counts):
-//   * a tail state (at most kTabTail positions left) lists all its orderings
-//     in rank order, so the rest of the sequence is entry `rank`;
-//   * a search state lists the orderings of its next h positions (h at most
-//     kTabHead) in rank order, each with the rank of its first completion
-//     and the state it leaves; a slot table over rank * G / N (N the number
-//     of orderings of the state, G a power of two, the slot computed exactly)
-//     holds, for a slot inside one entry, that entry itself (one gather), and
-//     for a slot that reaches into a second entry the number of the entry
-//     holding its first rank (then compared with the following entries).
-// A 24-position part is two searches and one tail; a 16-position part one
-// search and one tail; 12- and 8-position parts one tail.  Every lane runs
-// its searches first (part A's, then part B's; at most tc.max_searches) and
-// then its tails, so the lanes of a warp run the same lookup code together.  Sequences are
-// nibble strings (value index j of the part in bits 4t..4t+3 for step t).
-// The two parts of an even class are then moved onto their positions (the
-// word's coordinates and the others) by a nibble-wise bit expand (the
-// inverse of compress; H. S. Warren, Hacker's Delight, 2nd ed., section 7-5)
-// with move masks precomputed per Golay word, and a byte permute turns value
-// indices into magnitudes, four positions at a time.
+//   * a tail state (at most kTabTail = 12 positions left) lists all its
+//     orderings in rank order, so the rest of the sequence is entry `rank`;
+//   * a search state lists the orderings of its next h positions (h =
+//     min(kTabHead, positions - kTabTail)) in rank order, each with the rank
+//     of its first completion and the state it leaves.  A slot table over
+//     g(rank) = umulhi(rank >> s, M) (a monotone 32-bit map onto about four
+//     slots per entry) gives, per slot, the entry holding the slot's first
+//     rank and the entry after it when one boundary falls inside the slot,
+//     so a search is one 32-byte gather and one comparison; the few slots
+//     with two or more boundaries inside are marked and scanned.
+// Every class part has 0, 8, 12, 16 or 24 positions (Golay word weights), so
+// its lookups are fixed by its size: a 24-position part is two searches of 6
+// positions and a tail of 12, a 16-position part one search of 4 and a tail
+// of 12, 12- and 8-position parts one tail.  That gives four decode shapes
+// (kShape*), one per class; one code path covers them all, so lanes of a
+// warp holding different shapes run the same lookups.  Sequences are nibble
+// strings (value index j of the part in bits 4t..4t+3 for step t).  The two
+// parts of an even class are then moved onto their positions (the word's
+// coordinates and the others) by a nibble-wise bit expand (the inverse of
+// compress; H. S. Warren, Hacker's Delight, 2nd ed., section 7-5) with move
+// masks precomputed per Golay word, and a byte permute turns value indices
+// into magnitudes, four positions at a time.
 #pragma once
 
 #include <cstdint>
@@ -40,46 +43,65 @@ constexpr int kTabHead = 6;               // positions one search covers
 constexpr uint32_t kTabEnd = 0xFFFFFFFFu; // no state: the part is empty / finished
 constexpr int kTabExpandWords = 40;       // u32 per Golay word in the expand table
 constexpr uint32_t kTabTailBit = 1u << 31;
-constexpr uint32_t kTabSlotAmbiguous = 1u << 31;
+constexpr uint32_t kTabSlotMulti = 0xFFFFFFFEu;  // "next state" of a slot's second entry: scan the entries
+constexpr int kTabSlotsPerEntry = 4;
 constexpr int kTabMaxStateEntries = 0x10000;
+constexpr int kTabClassRecords = 3;       // uint4 per class record
+
+// Decode shapes (the lookups and the sign rule an index needs, from its class).
+enum : int {
+  kShapeOdd24 = 0,    // odd class: one 24-position part, odd signs
+  kShapeEven24 = 1,   // even class of word weight 0 or 24: one 24-position part, even signs
+  kShapeEven16 = 2,   // even, weight 8 or 16: a 16-position part and an 8-position part
+  kShapeEven12 = 3,   // even, weight 12: two 12-position parts
+  kShapeInvalid = 4,  // outside the codebook: a zero codeword
+  kShapes = 5
+};
 
 // State record, two uint4:
 //   [0] tail:   x = first entry in `tail`, z = kTabTailBit | positions
-//       search: x = first entry in `entry`, y = first slot,
-//               z = entries | log2 G << 16 | h << 21
-//   [1] search: N (u64, x | y << 32), G / N as fp64 bits (z | w << 32)
+//       search: x = first slot, y = M, z = s | h << 8, w = first entry in `entry`
+//   [1] N (u64, x | y << 32), z = number of entries (search)
 // Search entry (uint4): {start low, start high, next state, nibbles of the h
-// positions}; starts stay below 2^46.  Slot g (uint4) covers the ranks
-// ceil(g N / G) .. ceil((g + 1) N / G) - 1: the entry holding all of them, or
-// {number of the entry holding the first, kTabSlotAmbiguous, 0, 0}.
+// positions}; starts stay below 2^46.  Slot g (two uint4) covers the ranks r
+// with umulhi(r >> s, M) = g: {E0, E1}, E0 the entry holding the slot's first
+// rank, E1 the next entry if it starts inside the slot (else start = all
+// ones), or, when two or more entries start inside the slot, {start of the
+// next entry, kTabSlotMulti, its index, 0}.
 //
-// Class record, four uint4 (64 bytes):
-//   [0] start of the class (u64), permutation count (u64)
-//   [1] floor((2^64 - 1) / permutation count), floor((2^64 - 1) / f1 count)
-//   [2] values (u64: byte j = value j; even: the |v| = 0 mod 4 part's values,
-//       then the |v| = 2 mod 4 part's from byte d0 on), f1 count (u32), meta
-//   [3] first word of the class's weight group in weight order (u32), state of
-//       part A, state of part B, 0
-// meta: odd | word weight << 1 | sign shift << 6 | d0 << 11 | required << 15.
-// Part A is the odd class's only part or the even class's |v| = 2 (mod 4)
-// part on the word's positions; part B the even class's |v| = 0 (mod 4) part
-// on the other positions.
+// Class record, kTabClassRecords uint4 (48 bytes):
+//   [0] start (48 bits) | meta << 48, permutation count (48 bits) | P1 << 48
+//   [1] floor((2^64 - 1) / permutation count), values (u64: byte j = value
+//       j; even: the |v| = 0 mod 4 part's values, then the |v| = 2 mod 4
+//       part's from byte d0 on)
+//   [2] (even classes with two parts only) floor((2^64 - 1) / f1 count),
+//       f1 count, P2 | first word of the weight group (weight order) << 16 | d0 << 28
+// meta: shape | sign shift << 2 | required << 7 | (word weight 24) << 8 | (P1 is part A) << 9.
+// P1 is the part that is searched (odd: the only part; weight 0 or 24: the
+// non-empty part; weight 8 or 16: the 16-position part; weight 12: part A),
+// P2 the other part of a weight-8, 12 or 16 class.  Part A is the odd
+// class's only part or the even class's |v| = 2 (mod 4) part on the word's
+// positions; part B the even class's |v| = 0 (mod 4) part on the other
+// positions.
 //
 // Words are indexed in weight order (lexicographic inside a weight): an even
-// class's word is entry wbase + choice; every odd class uses entry 4095 (the
-// all-ones word: part A on every position) of the expand table.
+// class's word is entry wbase + choice.
 
 #if defined(__CUDA_ARCH__)
 template <class T>
 __device__ __forceinline__ T tab_ldg(const T* p) { return __ldg(p); }
 __device__ __forceinline__ uint32_t tab_prmt(uint32_t a, uint32_t b, uint32_t s) { return __byte_perm(a, b, s); }
 __device__ __forceinline__ uint32_t tab_fshl(uint32_t lo, uint32_t hi, int s) { return __funnelshift_l(lo, hi, s); }
-__device__ __forceinline__ double tab_bits2d(uint32_t lo, uint32_t hi) {
-  return __hiloint2double((int)hi, (int)lo);
-}
+__device__ __forceinline__ uint32_t tab_umulhi(uint32_t a, uint32_t b) { return __umulhi(a, b); }
 __device__ __forceinline__ uint64_t tab_mulhi(uint64_t a, uint64_t b) { return __umul64hi(a, b); }
 __device__ __forceinline__ int tab_popc(uint32_t v) { return __popc(v); }
 __device__ __forceinline__ int tab_msb(uint64_t u) { return 63 - __clzll((long long)u); }
+// One 32-byte read-only load (p 32-byte aligned): one gather instead of two.
+__device__ __forceinline__ void tab_ldg256(const uint4* p, uint4& a, uint4& b) {
+  asm("ld.global.nc.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+      : "l"(p));
+}
 #else
 template <class T>
 inline T tab_ldg(const T* p) { return *p; }
@@ -90,15 +112,14 @@ inline uint32_t tab_prmt(uint32_t a, uint32_t b, uint32_t s) {
   return out;
 }
 inline uint32_t tab_fshl(uint32_t lo, uint32_t hi, int s) { return s ? (hi << s) | (lo >> (32 - s)) : hi; }
-inline double tab_bits2d(uint32_t lo, uint32_t hi) {
-  const uint64_t b = ((uint64_t)hi << 32) | lo;
-  double d;
-  __builtin_memcpy(&d, &b, 8);
-  return d;
-}
+inline uint32_t tab_umulhi(uint32_t a, uint32_t b) { return (uint32_t)(((uint64_t)a * b) >> 32); }
 inline uint64_t tab_mulhi(uint64_t a, uint64_t b) { return (uint64_t)(((unsigned __int128)a * b) >> 64); }
 inline int tab_popc(uint32_t v) { return __builtin_popcount(v); }
 inline int tab_msb(uint64_t u) { return 63 - __builtin_clzll(u); }
+inline void tab_ldg256(const uint4* p, uint4& a, uint4& b) {
+  a = p[0];
+  b = p[1];
+}
 #endif
 
 LLVQ_HD uint64_t tab_u64(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
@@ -109,17 +130,22 @@ LLVQ_HD uint64_t tab_u64(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32)
 // the kernels); the rest is global memory.
 struct TabCtx {
   const uint4* srec;          // 2 per state                          (SMEM)
-  const uint4* crec;          // 4 per class                          (SMEM)
-  const uint16_t* bucket;     // index bucket -> class                (SMEM)
+  const uint4* crec;          // kTabClassRecords per class           (SMEM)
+  // (the shared copies of srec and crec are stored field-major, record j of
+  // state / class k at j * count + k, so that a warp's random records spread
+  // over all banks; the global ones record-major, at 2k + j / 3k + j)
+  const uint16_t* bucket;     // index bucket -> class                (global / host)
+  const uint32_t* bucket2;    // bucket b -> class of b | class of b + 1 << 16 (shared copy)
   const uint32_t* words;      // Golay words in weight order          (SMEM)
   const uint32_t* golay;      // Golay words in lexicographic order   (SMEM)
   const int64_t* starts;      // class starts (binary search)         (plain loads)
   const uint8_t* deposit4;    // [m * 16 + s]: the low popc(m) bits of s placed on the set bits of m (plain)
   const uint4* entry;
-  const uint4* slot;
+  const uint4* slot;          // 2 per slot
   const unsigned long long* tail;
   const uint4* expand;        // kTabExpandWords u32 per word, weight order
   int n_classes;
+  int n_states;
   int max_searches;           // searches of the longest class (both parts)
   int64_t total;
 };
@@ -130,43 +156,44 @@ LLVQ_HD T tab_ldr(const T* p) {
   else return tab_ldg(p);
 }
 
-// One search from search state s (record r0) with rank r: the nibbles of
-// the h positions it covers; s becomes the state left, r the rank within it.
+// Record j of class k / state s.
 template <bool SMEM>
-LLVQ_HD void tab_search(const TabCtx& tc, const uint4& r0, uint32_t& s, uint64_t& r, uint64_t& nib, int& take) {
-  const uint4 r1 = tab_ldr<SMEM>(tc.srec + 2 * s + 1);
-  const uint32_t n = r0.z & 0x1FFFFu, lg = (r0.z >> 17) & 31u;
-  const uint64_t N = tab_u64(r1.x, r1.y), rg = r << lg;
-  // slot g = floor(r G / N): an fp64 estimate, corrected exactly (N (G + 1) < 2^64)
-  uint64_t g = (uint64_t)((double)r * tab_bits2d(r1.z, r1.w));
-  if ((g + 1) * N <= rg) ++g;
-  else if (g * N > rg) --g;
-  uint4 e = tab_ldg(tc.slot + r0.y + (uint32_t)g);
-  if (e.y & kTabSlotAmbiguous) {
-    const uint4* ent = tc.entry + r0.x;
-    uint32_t j = e.x;
-    e = tab_ldg(ent + j);
+LLVQ_HD uint4 tab_crec(const TabCtx& tc, int k, int j) {
+  return tab_ldr<SMEM>(tc.crec + (SMEM ? j * tc.n_classes + k : kTabClassRecords * k + j));
+}
+template <bool SMEM>
+LLVQ_HD uint4 tab_srec(const TabCtx& tc, uint32_t s, int j) {
+  return tab_ldr<SMEM>(tc.srec + (SMEM ? (size_t)j * tc.n_states + s : 2 * (size_t)s + j));
+}
+
+// One search from search state s (record r0) with rank r: the nibbles of the
+// positions it covers; s becomes the state left, r the rank within it.
+template <bool SMEM>
+LLVQ_HD uint32_t tab_search(const TabCtx& tc, const uint4& r0, uint32_t& s, uint64_t& r) {
+  const uint32_t g = tab_umulhi((uint32_t)(r >> (r0.z & 63u)), r0.y);
+  uint4 e0, e1;
+  tab_ldg256(tc.slot + 2 * ((size_t)r0.x + g), e0, e1);
+  const uint64_t b = tab_u64(e1.x, e1.y);
+  const bool up = r >= b;
+  uint64_t start = up ? b : tab_u64(e0.x, e0.y);
+  uint32_t next = up ? e1.z : e0.z, nib = up ? e1.w : e0.w;
+  if (next == kTabSlotMulti) {  // several entries start inside the slot: scan from the second
+    const uint4* ent = tc.entry + r0.w;
+    const uint32_t n = tab_srec<SMEM>(tc, s, 1).z;
+    uint32_t j = nib;
     while (j + 1 < n) {
       const uint2 nx = tab_ldg(reinterpret_cast<const uint2*>(ent + j + 1));
       if (tab_u64(nx.x, nx.y) > r) break;
       ++j;
-      e = tab_ldg(ent + j);
     }
+    const uint4 e = tab_ldg(ent + j);
+    start = tab_u64(e.x, e.y);
+    next = e.z;
+    nib = e.w;
   }
-  r -= tab_u64(e.x, e.y);
-  s = e.z;
-  nib = e.w;
-  take = (int)((r0.z >> 22) & 15u);
-}
-
-LLVQ_HD void tab_put(uint64_t& lo, uint64_t& hi, uint64_t nib, int t) {
-  const int sh = 4 * t;
-  if (sh < 64) {
-    lo |= nib << sh;
-    if (sh) hi |= nib >> (64 - sh);
-  } else {
-    hi |= nib << (sh - 64);
-  }
+  r -= start;
+  s = next;
+  return nib;
 }
 
 // 96-bit (three u32) shift left by a constant number of bits.
@@ -198,7 +225,8 @@ LLVQ_HD void tab_expand2(uint32_t (&xa)[3], uint32_t (&xb)[3], const uint4* e, u
   uint32_t t[3];
 #define LLVQ_EXPAND_STAGE(Q, S)                                                           \
   {                                                                                        \
-    const uint4 u = tab_ldg(e + 2 * (Q)), v = tab_ldg(e + 2 * (Q) + 1);                     \
+    uint4 u, v;                                                                            \
+    tab_ldg256(e + 2 * (Q), u, v);                                                         \
     const uint32_t ma[3] = {u.x, u.y, u.z}, mb[3] = {u.w, v.x, v.y};                      \
     if ((Q) < 3) m[(Q) < 3 ? (Q) : 0] = v.z;                                               \
     tab_shl96<S>(xa, t);                                                                   \
@@ -214,129 +242,55 @@ LLVQ_HD void tab_expand2(uint32_t (&xa)[3], uint32_t (&xb)[3], const uint4* e, u
 #undef LLVQ_EXPAND_STAGE
 }
 
-// Magnitudes by position (mag[w], byte i = position 4 w + i) from the two
-// parts' states and ranks.  word_slot: the word's entry in the expand table
-// (weight order); spread: whether the parts need moving at all (false for
-// odd classes and words of weight 0 or 24, whose parts are in position
-// order already: their lanes skip the mask loads).
-template <bool SMEM>
-LLVQ_HD void tab_magnitudes(const TabCtx& tc, uint32_t sa, uint64_t ra, uint32_t sb, uint64_t rb, int word_slot,
-                            bool spread, int d0, uint64_t vals, uint32_t (&mag)[6]) {
-  uint64_t a_lo = 0, a_hi = 0, b_lo = 0, b_hi = 0;
-  int ta = 0, tb = 0;
-  // searches: part A's, then part B's, one per iteration
-  for (int it = 0; it < tc.max_searches; ++it) {
-    uint4 r0 = make_uint4(0, 0, kTabTailBit, 0);
-    bool in_b = false;
-    if (sa != kTabEnd) r0 = tab_ldr<SMEM>(tc.srec + 2 * sa);
-    if (r0.z & kTabTailBit) {
-      in_b = true;
-      r0 = make_uint4(0, 0, kTabTailBit, 0);
-      if (sb != kTabEnd) r0 = tab_ldr<SMEM>(tc.srec + 2 * sb);
-    }
-    if (r0.z & kTabTailBit) continue;  // both parts are at their tails
-    uint32_t s = in_b ? sb : sa;
-    uint64_t r = in_b ? rb : ra, nib;
-    int take;
-    tab_search<SMEM>(tc, r0, s, r, nib, take);
-    if (in_b) {
-      tab_put(b_lo, b_hi, nib, tb);
-      tb += take;
-      sb = s;
-      rb = r;
-    } else {
-      tab_put(a_lo, a_hi, nib, ta);
-      ta += take;
-      sa = s;
-      ra = r;
-    }
-  }
-  // tails: the rest of each part is one entry
-  if (sa != kTabEnd) {
-    const uint4 r0 = tab_ldr<SMEM>(tc.srec + 2 * sa);
-    tab_put(a_lo, a_hi, tab_ldg(tc.tail + r0.x + ra), ta);
-  }
-  if (sb != kTabEnd) {
-    const uint4 r0 = tab_ldr<SMEM>(tc.srec + 2 * sb);
-    tab_put(b_lo, b_hi, tab_ldg(tc.tail + r0.x + rb), tb);
-  }
-  // part A value indices follow the d0 part-B values (no nibble overflows:
-  // indices stay below 8, and the nibbles past the part's end are dropped by
-  // the merge below)
-  const uint64_t add = (uint64_t)d0 * 0x1111111111111111ull;
-  a_lo += add;
-  a_hi += add & 0xFFFFFFFFull;
-  uint32_t xa[3] = {(uint32_t)a_lo, (uint32_t)(a_lo >> 32), (uint32_t)a_hi};
-  uint32_t xb[3] = {(uint32_t)b_lo, (uint32_t)(b_lo >> 32), (uint32_t)b_hi};
-  uint32_t m[3];
-  if (spread) {
-    tab_expand2(xa, xb, tc.expand + (size_t)word_slot * (kTabExpandWords / 4), m);
-  } else {  // part A (odd, or the weight-24 word) everywhere, or part B (weight 0) everywhere
-    const uint32_t all = word_slot ? 0xFFFFFFFFu : 0u;
-    m[0] = m[1] = m[2] = all;
-  }
-  const uint32_t vlo = (uint32_t)vals, vhi = (uint32_t)(vals >> 32);
+// Per-position bit masks of magnitudes (mag[w], byte i = position 4w + i;
+// every magnitude is below 128): nonzero (byte + 0x7F carries into bit 7
+// exactly when the byte is nonzero) and bit 1; a multiply by 0x01020408
+// gathers bit 0 of four bytes into the top nibble.
+LLVQ_HD uint32_t tab_nonzero_mask(const uint32_t (&mag)[6]) {
+  uint32_t nz = 0;
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    const uint32_t x = (xa[k] & m[k]) | (xb[k] & ~m[k]);
-    mag[2 * k] = tab_prmt(vlo, vhi, x & 0xFFFFu);
-    mag[2 * k + 1] = tab_prmt(vlo, vhi, x >> 16);
-  }
+  for (int w = 0; w < 6; ++w)
+    nz |= (((((mag[w] + 0x7F7F7F7Fu) >> 7) & 0x01010101u) * 0x01020408u) >> 24) << (4 * w);
+  return nz;
 }
 
-// Signs of a codeword from its magnitudes by position (mag[w], byte i =
-// position 4 w + i) and y = the signed integer codeword; false (and y
-// undefined) if the even sign rank is out of range for the magnitudes.
-//   odd class:  y_d = m_d where m_d = 1 (mod 4) off the word or 3 (mod 4) on
-//               it, else -m_d (solve_odd_subclass's signed leader with the
-//               word's sign flips, impl/leech_lattice_vector_quantizer.py:649-681);
-//   even class: the sign rank's bits on the nonzero coordinates in position
-//               order, with the bit at the first word coordinate inserted so
-//               that the negative word coordinates have the class's parity
-//               (rank_even_signs / apply_even_signs, :804-841).
-LLVQ_HD bool tab_signs(const uint32_t (&mag)[6], uint32_t word, bool odd, uint64_t sign, int parity_bit,
-                       const uint8_t* deposit4, int (&y)[kDim]) {
-  // per-position bits of the magnitudes, four bytes at a time (every
-  // magnitude is below 128, so byte + 0x7F carries into bit 7 exactly when it
-  // is nonzero; a multiply by 0x01020408 gathers bit 0 of the four bytes into
-  // the top nibble)
-  uint32_t nzmask = 0, b1mask = 0;
+LLVQ_HD uint32_t tab_bit1_mask(const uint32_t (&mag)[6]) {
+  uint32_t b1 = 0;
 #pragma unroll
-  for (int w = 0; w < 6; ++w) {
-    const uint32_t t = mag[w];
-    nzmask |= (((((t + 0x7F7F7F7Fu) >> 7) & 0x01010101u) * 0x01020408u) >> 24) << (4 * w);
-    b1mask |= ((((t >> 1) & 0x01010101u) * 0x01020408u) >> 24) << (4 * w);
-  }
-  bool ok = true;
-  uint32_t neg;
-  if (odd) {
-    neg = b1mask ^ word;
+  for (int w = 0; w < 6; ++w) b1 |= ((((mag[w] >> 1) & 0x01010101u) * 0x01020408u) >> 24) << (4 * w);
+  return b1;
+}
+
+// Negative coordinates of an even codeword from its magnitudes and sign
+// rank: the rank's bits go to the nonzero coordinates in position order,
+// with the bit at the first word coordinate inserted so that the negative
+// word coordinates have the class's parity (rank_even_signs /
+// apply_even_signs, impl/leech_lattice_vector_quantizer.py:804-841).  False
+// when the rank is out of range for the magnitudes (no valid index).
+LLVQ_HD bool tab_even_neg(const uint32_t (&mag)[6], uint32_t word, uint64_t sign, int parity_bit,
+                          const uint8_t* deposit4, uint32_t& neg) {
+  const uint32_t nzmask = tab_nonzero_mask(mag);
+  const int nz = tab_popc(nzmask);
+  bool ok;
+  uint32_t cmask;
+  if (word) {
+    const int p = tab_popc(nzmask & ((word & (0u - word)) - 1u));
+    const uint32_t rr = (uint32_t)sign;
+    ok = (sign >> (nz - 1)) == 0;
+    cmask = ((rr >> p) << (p + 1)) | (rr & ((1u << p) - 1u));
   } else {
-    const int nz = tab_popc(nzmask);
-    uint32_t cmask;
-    if (word) {
-      const int p = tab_popc(nzmask & ((word & (0u - word)) - 1u));
-      const uint32_t rr = (uint32_t)sign;
-      ok = (sign >> (nz - 1)) == 0;
-      cmask = ((rr >> p) << (p + 1)) | (rr & ((1u << p) - 1u));
-    } else {
-      ok = nz >= 32 || (sign >> nz) == 0;
-      cmask = (uint32_t)sign;
-    }
-    neg = 0;
-#pragma unroll
-    for (int k = 0; k < kDim / 4; ++k) {
-      const uint32_t mm = (nzmask >> (4 * k)) & 15u;
-      neg |= (uint32_t)deposit4[mm * 16 + (cmask & 15u)] << (4 * k);
-      cmask >>= tab_popc(mm);
-    }
-    if (word && (tab_popc(neg & word) & 1) != parity_bit) neg ^= word & (0u - word);
+    ok = nz >= 32 || (sign >> nz) == 0;
+    cmask = (uint32_t)sign;
   }
+  uint32_t n = 0;
 #pragma unroll
-  for (int d = 0; d < kDim; ++d) {
-    const int mv = (int)((mag[d >> 2] >> (8 * (d & 3))) & 0xFFu);
-    y[d] = ((neg >> d) & 1u) ? -mv : mv;
+  for (int k = 0; k < kDim / 4; ++k) {
+    const uint32_t mm = (nzmask >> (4 * k)) & 15u;
+    n |= (uint32_t)deposit4[mm * 16 + (cmask & 15u)] << (4 * k);
+    cmask >>= tab_popc(mm);
   }
+  if (word && (tab_popc(n & word) & 1) != parity_bit) n ^= word & (0u - word);
+  neg = n;
   return ok;
 }
 
@@ -365,7 +319,15 @@ LLVQ_HD int tab_find_class(const TabCtx& tc, int64_t v) {
     const int e = tab_msb(u);
     key = 1 + e * 16 + (int)((e >= 4 ? u >> (e - 4) : u << (4 - e)) & 15u);
   }
-  int lo = tab_ldr<SMEM>(tc.bucket + key), hi = tab_ldr<SMEM>(tc.bucket + key + 1) + 1;
+  int lo, hi;
+  if constexpr (SMEM) {
+    const uint32_t bb = tc.bucket2[key];
+    lo = (int)(bb & 0xFFFFu);
+    hi = (int)(bb >> 16) + 1;
+  } else {
+    lo = tab_ldg(tc.bucket + key);
+    hi = tab_ldg(tc.bucket + key + 1) + 1;
+  }
   while (lo + 1 < hi) {
     const int mid = (lo + hi) >> 1;
     if (tc.starts[mid] <= v) lo = mid; else hi = mid;
@@ -373,45 +335,136 @@ LLVQ_HD int tab_find_class(const TabCtx& tc, int64_t v) {
   return lo;
 }
 
+// Class and decode shape of an index (kShapeInvalid outside the codebook).
+template <bool SMEM>
+LLVQ_HD int tab_classify(const TabCtx& tc, int64_t v, int& k) {
+  if (!(v >= 0 && v < tc.total)) {
+    k = 0;
+    return kShapeInvalid;
+  }
+  k = tab_find_class<SMEM>(tc, v);
+  return (int)((tab_crec<SMEM>(tc, k, 0).y >> 16) & 3u);
+}
+
+// 96-bit insert: nibble string t (its low `bits` bits valid, the rest zero)
+// at bit offset `at` (a multiple of 4, below 96) of x.
+LLVQ_HD void tab_put96(uint32_t (&x)[3], uint64_t t, int at) {
+  const int w = at >> 5, o = at & 31;
+  const uint32_t lo = (uint32_t)t, mid = (uint32_t)(t >> 32);
+  const uint32_t p0 = lo << o, p1 = tab_fshl(lo, mid, o), p2 = o ? mid >> (32 - o) : 0u;
+  // word w gets p0, w + 1 gets p1, w + 2 gets p2 (bits past 96 are dropped)
+  x[0] |= w == 0 ? p0 : 0u;
+  x[1] |= w == 0 ? p1 : w == 1 ? p0 : 0u;
+  x[2] |= w == 0 ? p2 : w == 1 ? p1 : p0;
+}
+
+// Magnitudes by position (mag[w], byte i = position 4w + i) and the mask of
+// negative coordinates of the valid index v of class k, on one path for every
+// decode shape (so the lanes of a warp that hold different shapes diverge
+// only around the even-class expand and sign deposit):
+//   part P1 (odd and weight 0/24: the 24-position part, two searches;
+//   weight 8/16: the 16-position part, one search; weight 12: part A, none)
+//   runs its searches and its tail; part P2 (weight 8/16: the 8-position
+//   part; weight 12: part B) is one tail.  False for a sign rank out of range
+//   (no valid index has one).
+template <bool SMEM>
+LLVQ_HD bool tab_decode_mn(const TabCtx& tc, int64_t v, int k, uint32_t (&mag)[6], uint32_t& neg) {
+  const uint4 c0 = tab_crec<SMEM>(tc, k, 0), c1 = tab_crec<SMEM>(tc, k, 1);
+  const uint32_t meta = c0.y >> 16;
+  const int shape = (int)(meta & 3u), sshift = (int)((meta >> 2) & 31u);
+  uint64_t prank;
+  const uint64_t cur = tab_divmod((uint64_t)v - tab_u64(c0.x, c0.y & 0xFFFFu), tab_u64(c0.z, c0.w & 0xFFFFu),
+                                  tab_u64(c1.x, c1.y), prank);
+  const bool split = shape >= kShapeEven16;
+  // primary part P1 and its searches, secondary tail part P2
+  uint32_t s1 = c0.w >> 16, s2 = kTabEnd, c2w = 0;
+  uint64_t r1 = prank, r2 = 0;
+  if (split) {
+    const uint4 c2 = tab_crec<SMEM>(tc, k, 2);
+    uint64_t ra;
+    const uint64_t rb = tab_divmod(prank, c2.z, tab_u64(c2.x, c2.y), ra);
+    const bool p1a = (meta >> 9) & 1u;
+    r1 = p1a ? ra : rb;
+    r2 = p1a ? rb : ra;
+    s2 = c2.w & 0xFFFFu;
+    c2w = c2.w;
+  }
+  const int nsearch = shape <= kShapeEven24 ? 2 : shape == kShapeEven16 ? 1 : 0;
+  uint32_t x1[3] = {0, 0, 0};
+  uint64_t t2 = 0;
+  if (split) t2 = tab_ldg(tc.tail + tab_srec<SMEM>(tc, s2, 0).x + r2);  // independent of P1
+  int at = 0;
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    if (it < nsearch) {
+      const uint4 r0 = tab_srec<SMEM>(tc, s1, 0);
+      const uint32_t nib = tab_search<SMEM>(tc, r0, s1, r1);
+      tab_put96(x1, nib, at);
+      at += 4 * (int)((r0.z >> 8) & 15u);
+    }
+  }
+  tab_put96(x1, tab_ldg(tc.tail + tab_srec<SMEM>(tc, s1, 0).x + r1), at);
+  uint32_t x[3], word;
+  if (shape == kShapeOdd24) {
+    word = tab_ldr<SMEM>(tc.golay + (int)cur);
+  } else if (shape == kShapeEven24) {
+    word = ((meta >> 8) & 1u) ? kFull24 : 0u;
+  } else {
+    const int slot = (int)((c2w >> 16) & 0xFFFu) + (int)(cur >> sshift);
+    word = tab_ldr<SMEM>(tc.words + slot);
+    // part A value indices follow the d0 part-B values (no nibble overflows:
+    // indices stay below 8, and the nibbles past the part's end are dropped
+    // by the merge below)
+    uint32_t xa[3], xb[3];
+    const bool p1a = (meta >> 9) & 1u;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint32_t y2 = (uint32_t)(t2 >> (32 * q));
+      xa[q] = p1a ? x1[q] : y2;
+      xb[q] = p1a ? y2 : x1[q];
+    }
+    xa[2] = p1a ? x1[2] : 0u;
+    xb[2] = p1a ? 0u : x1[2];
+    const uint32_t add = (c2w >> 28) * 0x11111111u;
+    xa[0] += add;
+    xa[1] += add;
+    uint32_t m[3];
+    tab_expand2(xa, xb, tc.expand + (size_t)slot * (kTabExpandWords / 4), m);
+#pragma unroll
+    for (int q = 0; q < 3; ++q) x1[q] = (xa[q] & m[q]) | (xb[q] & ~m[q]);
+  }
+#pragma unroll
+  for (int q = 0; q < 3; ++q) x[q] = x1[q];
+  const uint32_t vlo = c1.z, vhi = c1.w;
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+    mag[2 * q] = tab_prmt(vlo, vhi, x[q] & 0xFFFFu);
+    mag[2 * q + 1] = tab_prmt(vlo, vhi, x[q] >> 16);
+  }
+  if (shape == kShapeOdd24) {
+    // y = m where m = 1 mod 4 off the word or m = 3 mod 4 on it, else -m
+    // (solve_odd_subclass's signed leader with the word's sign flips,
+    // impl/leech_lattice_vector_quantizer.py:649-681)
+    neg = tab_bit1_mask(mag) ^ word;
+    return true;
+  }
+  return tab_even_neg(mag, word, cur & ((1ull << sshift) - 1), (int)((meta >> 7) & 1u), tc.deposit4, neg);
+}
+
 // Integer codeword of index v; false and zeros outside the codebook (or for
 // a sign rank out of range, which no valid index has).
 template <bool SMEM>
 LLVQ_HD bool tab_decode(const TabCtx& tc, int64_t v, int (&y)[kDim]) {
-  if (!(v >= 0 && v < tc.total)) {
-    for (int d = 0; d < kDim; ++d) y[d] = 0;
-    return false;
+  int k;
+  const int shape = tab_classify<SMEM>(tc, v, k);
+  uint32_t mag[6], neg = 0;
+  bool ok = shape != kShapeInvalid;
+  if (ok) ok = tab_decode_mn<SMEM>(tc, v, k, mag, neg);
+#pragma unroll
+  for (int d = 0; d < kDim; ++d) {
+    const int mv = ok ? (int)((mag[d >> 2] >> (8 * (d & 3))) & 0xFFu) : 0;
+    y[d] = ((neg >> d) & 1u) ? -mv : mv;
   }
-  const int k = tab_find_class<SMEM>(tc, v);
-  const uint4* cp = tc.crec + 4 * k;
-  const uint4 c0 = tab_ldr<SMEM>(cp), c1 = tab_ldr<SMEM>(cp + 1), c2 = tab_ldr<SMEM>(cp + 2),
-              c3 = tab_ldr<SMEM>(cp + 3);
-  const uint64_t start = tab_u64(c0.x, c0.y), perm = tab_u64(c0.z, c0.w);
-  const uint64_t magic_perm = tab_u64(c1.x, c1.y), magic_f1 = tab_u64(c1.z, c1.w);
-  const uint64_t vals = tab_u64(c2.x, c2.y);
-  const uint32_t f1p = c2.z, meta = c2.w;
-  const bool odd = meta & 1u;
-  const int weight = (int)((meta >> 1) & 31u), sshift = (int)((meta >> 6) & 31u), d0 = (int)((meta >> 11) & 15u);
-  uint64_t prank;
-  const uint64_t cur = tab_divmod((uint64_t)v - start, perm, magic_perm, prank);
-  uint32_t word;
-  int slot;
-  uint64_t sign = 0, ra = prank, rb = 0;
-  if (odd) {
-    word = tab_ldr<SMEM>(tc.golay + (int)cur);
-    slot = kNumGolay - 1;
-  } else {
-    sign = cur & ((1ull << sshift) - 1);
-    slot = (int)c3.x + (int)(cur >> sshift);
-    word = tab_ldr<SMEM>(tc.words + slot);
-    uint64_t r1;
-    rb = tab_divmod(prank, f1p, magic_f1, r1);
-    ra = r1;
-  }
-  uint32_t mag[6];
-  tab_magnitudes<SMEM>(tc, c3.y, ra, c3.z, rb, slot, !odd && weight != 0 && weight != kDim, d0, vals, mag);
-  const bool ok = tab_signs(mag, word, odd, sign, (int)((meta >> 15) & 1u), tc.deposit4, y);
-  if (!ok)
-    for (int d = 0; d < kDim; ++d) y[d] = 0;
   return ok;
 }
 
