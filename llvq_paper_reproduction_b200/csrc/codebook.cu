@@ -399,7 +399,8 @@ int upload(llvq::Codebook& cb, int device) {
   const size_t o_tentry = off; off = align256(off + tb.entry.size() * sizeof(uint4));
   const size_t o_tslot = off; off = align256(off + tb.slot.size() * sizeof(uint4));
   const size_t o_ttail = off; off = align256(off + tb.tail.size() * sizeof(unsigned long long));
-  const size_t o_texp = off; off = align256(off + tb.expand.size() * sizeof(uint32_t));
+  const size_t o_ttail2 = off; off = align256(off + tb.tail2.size() * sizeof(uint32_t));
+  const size_t o_texp2 = off; off = align256(off + tb.expand2.size() * sizeof(uint32_t));
   std::vector<unsigned char> host(off, 0);
   if (tb.ok) {
     std::memcpy(host.data() + o_tstate, tb.state.data(), tb.state.size() * sizeof(uint4));
@@ -407,7 +408,8 @@ int upload(llvq::Codebook& cb, int device) {
     std::memcpy(host.data() + o_tentry, tb.entry.data(), tb.entry.size() * sizeof(uint4));
     std::memcpy(host.data() + o_tslot, tb.slot.data(), tb.slot.size() * sizeof(uint4));
     std::memcpy(host.data() + o_ttail, tb.tail.data(), tb.tail.size() * sizeof(unsigned long long));
-    std::memcpy(host.data() + o_texp, tb.expand.data(), tb.expand.size() * sizeof(uint32_t));
+    std::memcpy(host.data() + o_ttail2, tb.tail2.data(), tb.tail2.size() * sizeof(uint32_t));
+    std::memcpy(host.data() + o_texp2, tb.expand2.data(), tb.expand2.size() * sizeof(uint32_t));
   }
   {
     std::vector<DecodeClass> dc(n);
@@ -497,7 +499,8 @@ int upload(llvq::Codebook& cb, int device) {
     d.tab.entry = reinterpret_cast<const uint4*>(base + o_tentry);
     d.tab.slot = reinterpret_cast<const uint4*>(base + o_tslot);
     d.tab.tail = reinterpret_cast<const unsigned long long*>(base + o_ttail);
-    d.tab.expand = reinterpret_cast<const uint4*>(base + o_texp);
+    d.tab.tail2 = reinterpret_cast<const uint32_t*>(base + o_ttail2);
+    d.tab.expand2 = reinterpret_cast<const uint4*>(base + o_texp2);
     d.tab.n_states = (int)(tb.state.size() / 2);
     d.tab.max_searches = tb.max_searches;
   }
@@ -580,7 +583,7 @@ int llvq_codebook_tables(const llvq_codebook* h, int32_t* tabulated, int64_t* ta
   if (tabulated) *tabulated = t.ok ? 1 : 0;
   if (table_bytes)
     *table_bytes = (int64_t)(t.state.size() * 16 + t.crec.size() * 16 + t.entry.size() * 16 + t.slot.size() * 16 +
-                             t.tail.size() * 8 + t.expand.size() * 4);
+                             t.tail.size() * 8 + t.tail2.size() * 4 + t.expand2.size() * 4);
   if (max_lookups) *max_lookups = t.max_searches + 2;  // searches, then one tail per part
   return LLVQ_OK;
 }

@@ -64,8 +64,11 @@ struct Builder {
 
   explicit Builder(TabHost& tab) : t(tab) {}
 
-  uint32_t get(const int* c) {
-    const uint64_t key = pack_counts(c);
+  // States are keyed by their counts and their entry format: value-index
+  // nibbles (the parts of odd and weight-0/24 classes) or two bit planes
+  // (the parts of weight-8/12/16 classes, at most four values).
+  uint32_t get(const int* c, bool planes) {
+    const uint64_t key = pack_counts(c) | (planes ? 1ull << 63 : 0ull);
     auto it = ids.find(key);
     if (it != ids.end()) return it->second;
     const uint32_t id = (uint32_t)keys.size();
@@ -75,8 +78,10 @@ struct Builder {
   }
 
   // Every ordering of the remaining counts, in rank order (value index
-  // ascending at each position), as nibble strings.
-  void tail_state(int* c, int rem, uint64_t prefix, int pos, std::vector<unsigned long long>& out) {
+  // ascending at each position): as nibble strings, or as bit planes (bit t
+  // of the low 12 bits = bit 0 of the value index at step t, bit 12 + t =
+  // its bit 1).
+  void tail_state(int* c, int rem, uint64_t prefix, int pos, bool planes, std::vector<uint64_t>& out) {
     if (pos == rem) {
       out.push_back(prefix);
       return;
@@ -84,7 +89,9 @@ struct Builder {
     for (int j = 0; j < kTabMaxVals; ++j) {
       if (!c[j]) continue;
       --c[j];
-      tail_state(c, rem, prefix | ((uint64_t)j << (4 * pos)), pos + 1, out);
+      const uint64_t add = planes ? (((uint64_t)(j & 1) << pos) | ((uint64_t)((j >> 1) & 1) << (kTabTail + pos)))
+                                  : (uint64_t)j << (4 * pos);
+      tail_state(c, rem, prefix | add, pos + 1, planes, out);
       ++c[j];
     }
   }
@@ -95,9 +102,11 @@ struct Builder {
     uint32_t nib;
   };
 
-  void search_state(int* c, int h, int pos, uint32_t nib, u128& cursor, std::vector<Prefix>& out) {
+  // Search prefixes: nibbles, or bit planes (bit t = bit 0 of step t, bit
+  // 8 + t = bit 1).
+  void search_state(int* c, int h, int pos, uint32_t nib, bool planes, u128& cursor, std::vector<Prefix>& out) {
     if (pos == h) {
-      const uint32_t nx = get(c);
+      const uint32_t nx = get(c, planes);
       out.push_back({cursor, nx, nib});
       cursor += multinomial_counts(c);
       return;
@@ -105,7 +114,9 @@ struct Builder {
     for (int j = 0; j < kTabMaxVals; ++j) {
       if (!c[j]) continue;
       --c[j];
-      search_state(c, h, pos + 1, nib | ((uint32_t)j << (4 * pos)), cursor, out);
+      const uint32_t add = planes ? (((uint32_t)(j & 1) << pos) | ((uint32_t)((j >> 1) & 1) << (8 + pos)))
+                                  : (uint32_t)j << (4 * pos);
+      search_state(c, h, pos + 1, nib | add, planes, cursor, out);
       ++c[j];
     }
   }
@@ -115,22 +126,33 @@ struct Builder {
     // their parent is processed, so the vector grows behind the cursor
     for (size_t s = 0; s < keys.size(); ++s) {
       int c[kTabMaxVals];
-      unpack_counts(keys[s], c);
+      const bool planes = keys[s] >> 63;
+      unpack_counts(keys[s] & ~(1ull << 63), c);
       int rem = 0;
       for (int j = 0; j < kTabMaxVals; ++j) rem += c[j];
       const u128 n = multinomial_counts(c);
       if (n >> 46) return fail("a part has 2^46 or more orderings");
       uint4 r0{0, 0, 0, 0}, r1{0, 0, 0, 0};
       if (rem <= kTabTail) {
-        if (t.tail.size() + (size_t)n > kTabMaxTail) return fail("tail tables too large");
-        r0.x = (uint32_t)t.tail.size();
+        if (planes) {
+          if (t.tail2.size() + (size_t)n > kTabMaxTail) return fail("tail tables too large");
+          r0.x = (uint32_t)t.tail2.size();
+          std::vector<uint64_t> seqs;
+          tail_state(c, rem, 0, 0, true, seqs);
+          for (uint64_t q : seqs) t.tail2.push_back((uint32_t)q);
+        } else {
+          if (t.tail.size() + (size_t)n > kTabMaxTail) return fail("tail tables too large");
+          r0.x = (uint32_t)t.tail.size();
+          std::vector<uint64_t> seqs;
+          tail_state(c, rem, 0, 0, false, seqs);
+          t.tail.insert(t.tail.end(), seqs.begin(), seqs.end());
+        }
         r0.z = kTabTailBit | (uint32_t)rem;
-        tail_state(c, rem, 0, 0, t.tail);
       } else {
         const int h = std::min(kTabHead, rem - kTabTail);
         std::vector<Prefix> pre;
         u128 cursor = 0;
-        search_state(c, h, 0, 0, cursor, pre);
+        search_state(c, h, 0, 0, planes, cursor, pre);
         if (cursor != n) return fail("prefix counts do not add up");
         if (pre.size() >= (size_t)kTabMaxStateEntries) return fail("a search state has too many prefixes");
         if (t.entry.size() + pre.size() > kTabMaxEntries) return fail("search tables too large");
@@ -227,63 +249,6 @@ void expand_masks(uint32_t m, uint32_t mv[5]) {
   }
 }
 
-// Each of the 24 mask bits widened to a nibble, as three u32.
-void nibble_spread(uint32_t m, uint32_t* out) {
-  for (int k = 0; k < 3; ++k) {
-    uint32_t v = 0;
-    for (int i = 0; i < 8; ++i)
-      if ((m >> (8 * k + i)) & 1u) v |= 0xFu << (4 * i);
-    out[k] = v;
-  }
-}
-
-bool build_expand(const std::vector<uint32_t>& words, std::vector<uint32_t>& out, std::string& why) {
-  out.assign((size_t)kNumGolay * kTabExpandWords, 0);
-  uint32_t seed = 12345u;
-  for (int gi = 0; gi < kNumGolay; ++gi) {
-    uint32_t* e = out.data() + (size_t)gi * kTabExpandWords;
-    const uint32_t w = words[gi];
-    uint32_t mva[5], mvb[5], ma[3], mb[3], m0[3];
-    expand_masks(w, mva);
-    expand_masks(~w & kFull24, mvb);
-    nibble_spread(w, m0);
-    for (int q = 0; q < 5; ++q) {  // stage q applies the shift by 2^(4-q) positions
-      nibble_spread(mva[4 - q], ma);
-      nibble_spread(mvb[4 - q], mb);
-      uint32_t* st = e + 8 * q;
-      st[0] = ma[0]; st[1] = ma[1]; st[2] = ma[2]; st[3] = mb[0];
-      st[4] = mb[1]; st[5] = mb[2]; st[6] = q < 3 ? m0[q] : 0u; st[7] = 0;
-    }
-    // self-check: random nibble strings (garbage beyond each part's length)
-    // land on the right positions
-    for (int trial = 0; trial < 4; ++trial) {
-      uint32_t xa[3], xb[3], want_a[24], want_b[24], m[3];
-      int ia = 0, ib = 0;
-      for (int k = 0; k < 3; ++k) {
-        seed = seed * 1664525u + 1013904223u;
-        xa[k] = seed;
-        seed = seed * 1664525u + 1013904223u;
-        xb[k] = seed;
-      }
-      auto nib = [](const uint32_t* x, int t) { return (x[t / 8] >> (4 * (t % 8))) & 15u; };
-      for (int d = 0; d < kDim; ++d) {
-        if ((w >> d) & 1u) want_a[d] = nib(xa, ia++);
-        else want_b[d] = nib(xb, ib++);
-      }
-      tab_expand2(xa, xb, reinterpret_cast<const uint4*>(e), m);
-      for (int d = 0; d < kDim; ++d) {
-        const bool on = (w >> d) & 1u;
-        const uint32_t got = on ? nib(xa, d) : nib(xb, d);
-        if (got != (on ? want_a[d] : want_b[d]) || nib(m, d) != (on ? 15u : 0u)) {
-          why = "expand self-check failed";
-          return false;
-        }
-      }
-    }
-  }
-  return true;
-}
-
 }  // namespace
 
 bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
@@ -302,11 +267,15 @@ bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
     int a[kTabMaxVals] = {0}, z[kTabMaxVals] = {0};
     if (c.parity) {
       for (int j = 0; j < c.nv0; ++j) a[j] = c.m0[j];
-      parts[k] = make_uint2(b.get(a), kTabEnd);
+      parts[k] = make_uint2(b.get(a, false), kTabEnd);
     } else {
       for (int j = 0; j < c.nv1; ++j) a[j] = c.m1[j];
       for (int j = 0; j < c.nv0; ++j) z[j] = c.m0[j];
-      parts[k] = make_uint2(c.even_weight > 0 ? b.get(a) : kTabEnd, c.even_weight < kDim ? b.get(z) : kTabEnd);
+      // two parts (weight 8, 12, 16): bit-plane entries, at most four values a part
+      const bool planes = c.even_weight > 0 && c.even_weight < kDim;
+      if (planes && (c.nv0 > 4 || c.nv1 > 4)) return bad("a two-part class has a part of more than four values");
+      parts[k] = make_uint2(c.even_weight > 0 ? b.get(a, planes) : kTabEnd,
+                            c.even_weight < kDim ? b.get(z, planes) : kTabEnd);
     }
   }
   if (!b.run()) return bad(b.why);
@@ -319,12 +288,14 @@ bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
     // searches before each part's tail (depth counts the tail too)
     t.max_searches = std::max(t.max_searches, (st.x != kTabEnd ? b.depth[st.x] - 1 : 0) +
                                                   (st.y != kTabEnd ? b.depth[st.y] - 1 : 0));
+    // values by selector: odd and weight 0/24: the one part's values from
+    // byte 0; weight 8/12/16: part B's values in bytes 0-3, part A's in 4-7
     uint64_t vals = 0;
     int d0 = 0;
     if (c.parity) {
       for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
     } else {
-      d0 = c.nv0;
+      d0 = c.even_weight > 0 && c.even_weight < kDim ? 4 : c.nv0;
       for (int j = 0; j < c.nv0; ++j) vals |= (uint64_t)(uint8_t)c.v0[j] << (8 * j);
       for (int j = 0; j < c.nv1; ++j) vals |= (uint64_t)(uint8_t)c.v1[j] << (8 * (d0 + j));
     }
@@ -354,8 +325,20 @@ bool build_decode_tables(const Codebook& cb, TabHost& t, std::string* why_out) {
     t.bucket[bk] = (uint16_t)(lo >= (uint64_t)cb.total ? n - 1
                                                         : find_class(cb.class_start.data(), (int)n, (int64_t)lo));
   }
-  std::string why;
-  if (!build_expand(cb.wlist_word, t.expand, why)) return bad(why);
+  // bit-plane deposit masks per word (weight order): stage i moves bits by
+  // 2^i; m[i] = stage i of the word's deposit | low byte of the complement's
+  // stage i << 24, m[5..7] the complement's upper 16 bits, two per word
+  t.expand2.assign((size_t)kNumGolay * kTabExpand2Words, 0);
+  for (int gi = 0; gi < kNumGolay; ++gi) {
+    uint32_t mva[5], mvb[5];
+    expand_masks(cb.wlist_word[gi], mva);
+    expand_masks(~cb.wlist_word[gi] & kFull24, mvb);
+    uint32_t* m = t.expand2.data() + (size_t)gi * kTabExpand2Words;
+    for (int i = 0; i < 5; ++i) m[i] = mva[i] | ((mvb[i] & 0xFFu) << 24);
+    m[5] = (mvb[0] >> 8) | ((mvb[1] >> 8) << 16);
+    m[6] = (mvb[2] >> 8) | ((mvb[3] >> 8) << 16);
+    m[7] = mvb[4] >> 8;
+  }
   t.ok = true;
   return true;
 }
@@ -397,7 +380,8 @@ TabCtx host_tab_ctx(const Codebook& cb) {
   tc.entry = t.entry.data();
   tc.slot = t.slot.data();
   tc.tail = t.tail.data();
-  tc.expand = reinterpret_cast<const uint4*>(t.expand.data());
+  tc.tail2 = t.tail2.data();
+  tc.expand2 = reinterpret_cast<const uint4*>(t.expand2.data());
   tc.n_classes = (int)cb.cls.size();
   tc.n_states = (int)(t.state.size() / 2);
   tc.max_searches = t.max_searches;

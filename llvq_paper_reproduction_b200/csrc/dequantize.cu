@@ -115,13 +115,13 @@ __device__ __forceinline__ uint32_t bf16_pair(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Output of one decoded index in every kind (streaming stores).  The sign
-// is applied last (an exact negation of the rounded magnitude product,
-// since round-to-nearest is symmetric).
+// Output of one decoded index in every kind (streaming stores); row is
+// i / blocks_per_row (kind 3 only).  The sign is applied last (an exact
+// negation of the rounded magnitude product, since round-to-nearest is
+// symmetric).
 template <int KIND>
 __device__ __forceinline__ void store_mn(const uint32_t (&mag)[6], uint32_t neg, int64_t i, void* __restrict__ out,
-                                         const uint16_t* __restrict__ row_scale, int64_t blocks_per_row,
-                                         uint64_t magic_bpr) {
+                                         const uint16_t* __restrict__ row_scale, int64_t row) {
   if constexpr (KIND == 0) {
     longlong2* o = reinterpret_cast<longlong2*>(static_cast<long long*>(out) + i * kDim);
 #pragma unroll
@@ -152,9 +152,10 @@ __device__ __forceinline__ void store_mn(const uint32_t (&mag)[6], uint32_t neg,
       __stcs(o + d / 4, make_float4(f[0], f[1], f[2], f[3]));
     }
   } else {
-    uint64_t col;  // row = i / blocks_per_row by multiply-high with an exact correction
-    const uint64_t row = div_magic((uint64_t)i, (uint64_t)blocks_per_row, magic_bpr, col);
     const float s = __half2float(__ushort_as_half(__ldg(row_scale + row)));
+    const float2 c = make_float2(kLatticeScaleF, kLatticeScaleF), d = make_float2(-8388608.0f * kLatticeScaleF,
+                                                                                  -8388608.0f * kLatticeScaleF);
+    const float2 s2 = make_float2(s, s);
     uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + i * kDim);
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
@@ -164,8 +165,9 @@ __device__ __forceinline__ void store_mn(const uint32_t (&mag)[6], uint32_t neg,
         const int p = 4 * q + e;  // bf16 pair p: positions 2p, 2p + 1
         const uint32_t mw = mag[p >> 1];
         const int j = 2 * (p & 1);
-        w[e] = bf16_pair(__fmul_rn(mag_scaled(mw, j), s), __fmul_rn(mag_scaled(mw, j + 1), s)) ^
-               bf16_pair_signs(neg, p);
+        // fp32(fp32(1/sqrt 8) * m) * s, two lanes per instruction
+        const float2 f = __fmul2_rn(__ffma2_rn(make_float2(mag_float_2p23(mw, j), mag_float_2p23(mw, j + 1)), c, d), s2);
+        w[e] = bf16_pair(f.x, f.y) ^ bf16_pair_signs(neg, p);
       }
       __stcs(o + q, make_uint4(w[0], w[1], w[2], w[3]));
     }
@@ -208,12 +210,27 @@ __global__ void __launch_bounds__(kTabThreads, kTabMinBlocks) dequant_tab_kernel
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t v = i < n ? load_index_stream(index, i) : 0;
+  // row of index i (kind 3), advanced with the stride instead of divided
+  uint64_t col, dcol;
+  int64_t row = 0, drow = 0;
+  if constexpr (KIND == 3) {
+    row = (int64_t)div_magic((uint64_t)i, (uint64_t)blocks_per_row, magic_bpr, col);
+    drow = (int64_t)div_magic((uint64_t)stride, (uint64_t)blocks_per_row, magic_bpr, dcol);
+  }
   int errors = 0;
   for (; i < n; i += stride) {
     const int64_t vn = i + stride < n ? load_index_stream(index, i + stride) : 0;
     uint32_t mag[6], neg;
     if (!tab_decode_any<MODE == kModeTabShared>(tc, v, mag, neg)) ++errors;
-    store_mn<KIND>(mag, neg, i, out, row_scale, blocks_per_row, magic_bpr);
+    store_mn<KIND>(mag, neg, i, out, row_scale, row);
+    if constexpr (KIND == 3) {
+      row += drow;
+      col += dcol;
+      if (col >= (uint64_t)blocks_per_row) {
+        col -= (uint64_t)blocks_per_row;
+        ++row;
+      }
+    }
     v = vn;
   }
   if (error_count) {

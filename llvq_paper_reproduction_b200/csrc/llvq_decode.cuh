@@ -612,7 +612,8 @@ __device__ __forceinline__ TabCtx tab_ctx(const DevBook& book, const DecodeShare
   tc.entry = book.tab.entry;
   tc.slot = book.tab.slot;
   tc.tail = book.tab.tail;
-  tc.expand = book.tab.expand;
+  tc.tail2 = book.tab.tail2;
+  tc.expand2 = book.tab.expand2;
   tc.n_classes = book.n_classes;
   tc.n_states = book.tab.n_states;
   tc.max_searches = book.tab.max_searches;

@@ -96,7 +96,8 @@ struct TabView {
   const uint4* entry;
   const uint4* slot;
   const unsigned long long* tail;
-  const uint4* expand;     // per Golay word in weight order
+  const uint32_t* tail2;   // bit-plane tails
+  const uint4* expand2;    // bit-plane deposit masks per Golay word in weight order
   int n_states;
   int max_searches;        // searches of the longest class (both parts)
 };

@@ -46,11 +46,12 @@ struct SpecEntry {
 struct TabHost {
   bool ok = false;
   std::vector<uint4> state;            // 2 per state
-  std::vector<uint4> crec;             // 4 per class
+  std::vector<uint4> crec;             // kTabClassRecords per class
   std::vector<uint4> entry;
   std::vector<uint4> slot;
-  std::vector<unsigned long long> tail;
-  std::vector<uint32_t> expand;        // per word in weight order
+  std::vector<unsigned long long> tail;  // nibble-string tails
+  std::vector<uint32_t> tail2;           // bit-plane tails (parts of two-part classes)
+  std::vector<uint32_t> expand2;         // kTabExpand2Words per word in weight order
   std::vector<uint16_t> bucket;        // index bucket -> class (host copy for the host decoder)
   int max_searches = 0;
 };

@@ -23,13 +23,16 @@
 // positions and a tail of 12, a 16-position part one search of 4 and a tail
 // of 12, 12- and 8-position parts one tail.  That gives four decode shapes
 // (kShape*), one per class; one code path covers them all, so lanes of a
-// warp holding different shapes run the same lookups.  Sequences are nibble
-// strings (value index j of the part in bits 4t..4t+3 for step t).  The two
-// parts of an even class are then moved onto their positions (the word's
-// coordinates and the others) by a nibble-wise bit expand (the inverse of
-// compress; H. S. Warren, Hacker's Delight, 2nd ed., section 7-5) with move
-// masks precomputed per Golay word, and a byte permute turns value indices
-// into magnitudes, four positions at a time.
+// warp holding different shapes run the same lookups.  The 24-position parts
+// (odd classes, word weight 0 or 24) store their sequences as nibble strings
+// (value index j of the part in bits 4t..4t+3 for step t), already in
+// position order.  The two parts of a weight-8/12/16 class (at most four
+// values each) store theirs as two bit planes (bit t = bit 0 / bit 1 of the
+// value index at step t); the planes are moved onto their positions (the
+// word's coordinates and the others) by a bit deposit (the expand of H. S.
+// Warren, Hacker's Delight, 2nd ed., section 7-5) with five move masks per
+// Golay word and part, one 32-byte load, and then widened to nibbles.  A byte
+// permute turns the nibbles into magnitudes, four positions at a time.
 #pragma once
 
 #include <cstdint>
@@ -41,12 +44,12 @@ namespace llvq {
 constexpr int kTabTail = 12;              // positions a tail state covers
 constexpr int kTabHead = 6;               // positions one search covers
 constexpr uint32_t kTabEnd = 0xFFFFFFFFu; // no state: the part is empty / finished
-constexpr int kTabExpandWords = 40;       // u32 per Golay word in the expand table
 constexpr uint32_t kTabTailBit = 1u << 31;
 constexpr uint32_t kTabSlotMulti = 0xFFFFFFFEu;  // "next state" of a slot's second entry: scan the entries
 constexpr int kTabSlotsPerEntry = 4;
 constexpr int kTabMaxStateEntries = 0x10000;
 constexpr int kTabClassRecords = 3;       // uint4 per class record
+constexpr int kTabExpand2Words = 8;       // u32 per Golay word in the bit-plane deposit table
 
 // Decode shapes (the lookups and the sign rule an index needs, from its class).
 enum : int {
@@ -142,8 +145,9 @@ struct TabCtx {
   const uint8_t* deposit4;    // [m * 16 + s]: the low popc(m) bits of s placed on the set bits of m (plain)
   const uint4* entry;
   const uint4* slot;          // 2 per slot
-  const unsigned long long* tail;
-  const uint4* expand;        // kTabExpandWords u32 per word, weight order
+  const unsigned long long* tail;  // nibble-string tails (odd and weight-0/24 parts)
+  const uint32_t* tail2;          // bit-plane tails (parts of weight-8/12/16 classes)
+  const uint4* expand2;       // kTabExpand2Words u32 per word, weight order
   int n_classes;
   int n_states;
   int max_searches;           // searches of the longest class (both parts)
@@ -196,80 +200,68 @@ LLVQ_HD uint32_t tab_search(const TabCtx& tc, const uint4& r0, uint32_t& s, uint
   return nib;
 }
 
-// 96-bit (three u32) shift left by a constant number of bits.
-template <int S>
-LLVQ_HD void tab_shl96(const uint32_t (&x)[3], uint32_t (&t)[3]) {
-  if constexpr (S == 64) {
-    t[2] = x[0]; t[1] = 0; t[0] = 0;
-  } else if constexpr (S == 32) {
-    t[2] = x[1]; t[1] = x[0]; t[0] = 0;
-  } else {
-    t[2] = tab_fshl(x[1], x[2], S);
-    t[1] = tab_fshl(x[0], x[1], S);
-    t[0] = x[0] << S;
-  }
+// Bit t (t < 8) of b to bit 4t: three shift-and-mask stages.
+LLVQ_HD uint32_t tab_spread8(uint32_t b) {
+  uint32_t x = (b & 0xFFu) | ((b & 0xFFu) << 12);
+  x &= 0x000F000Fu;
+  x = (x | (x << 6)) & 0x03030303u;
+  return (x | (x << 3)) & 0x11111111u;
 }
 
-// Expand table layout, per Golay word (weight order), kTabExpandWords u32 as
-// five 32-byte stages q = 0..4 (applied in that order; stage q moves nibbles
-// by 2^(4-q) positions): {A0, A1, A2, B0}, {B1, B2, M_q, 0}, where A0..A2 /
-// B0..B2 are the nibble-wide move masks of the expand by the word / by its
-// complement (three u32 covering positions 0-7, 8-15, 16-23) and M_0..M_2
-// the word itself widened to nibbles.
-//
-// Nibble-wise expand of both parts at once: source nibble t of xa goes to
-// the t-th position of the word, source nibble t of xb to the t-th position
-// outside it; m receives the word's nibble mask.  Positions outside each
-// part's mask hold garbage.
-LLVQ_HD void tab_expand2(uint32_t (&xa)[3], uint32_t (&xb)[3], const uint4* e, uint32_t (&m)[3]) {
-  uint32_t t[3];
-#define LLVQ_EXPAND_STAGE(Q, S)                                                           \
-  {                                                                                        \
-    uint4 u, v;                                                                            \
-    tab_ldg256(e + 2 * (Q), u, v);                                                         \
-    const uint32_t ma[3] = {u.x, u.y, u.z}, mb[3] = {u.w, v.x, v.y};                      \
-    if ((Q) < 3) m[(Q) < 3 ? (Q) : 0] = v.z;                                               \
-    tab_shl96<S>(xa, t);                                                                   \
-    for (int k = 0; k < 3; ++k) xa[k] = (xa[k] & ~ma[k]) | (t[k] & ma[k]);                  \
-    tab_shl96<S>(xb, t);                                                                   \
-    for (int k = 0; k < 3; ++k) xb[k] = (xb[k] & ~mb[k]) | (t[k] & mb[k]);                  \
+// Bit-plane deposit (the expand of Hacker's Delight, section 7-5, with the
+// move masks of one Golay word): bit t of a goes to the t-th set bit of the
+// word, bit t of b to the t-th clear bit, for both planes of each part; the
+// merged planes and the word give each position's byte-permute selector
+// (value index bits 0-1, bit 2 = on the word).  e: the word's kTabExpand2Words
+// masks (stage i of the word's deposit in m[i] bits 0-23, the complement's
+// stage i split over m[i] bits 24-31 and m[5..7]).
+LLVQ_HD void tab_deposit_planes(uint32_t a0, uint32_t a1, uint32_t b0, uint32_t b1, uint32_t word, const uint4* e,
+                                uint32_t (&x)[3]) {
+  uint4 u, v;
+  tab_ldg256(e, u, v);
+  const uint32_t ma[5] = {u.x, u.y, u.z, u.w, v.x};
+  const uint32_t mb[5] = {tab_prmt(u.x, v.y, 0x3543u), tab_prmt(u.y, v.y, 0x3763u), tab_prmt(u.z, v.z, 0x3543u),
+                          tab_prmt(u.w, v.z, 0x3763u), tab_prmt(v.x, v.w, 0x3543u)};
+#pragma unroll
+  for (int i = 4; i >= 0; --i) {
+    const int sh = 1 << i;
+    a0 = (a0 & ~ma[i]) | ((a0 << sh) & ma[i]);
+    a1 = (a1 & ~ma[i]) | ((a1 << sh) & ma[i]);
+    b0 = (b0 & ~mb[i]) | ((b0 << sh) & mb[i]);
+    b1 = (b1 & ~mb[i]) | ((b1 << sh) & mb[i]);
   }
-  LLVQ_EXPAND_STAGE(0, 64)
-  LLVQ_EXPAND_STAGE(1, 32)
-  LLVQ_EXPAND_STAGE(2, 16)
-  LLVQ_EXPAND_STAGE(3, 8)
-  LLVQ_EXPAND_STAGE(4, 4)
-#undef LLVQ_EXPAND_STAGE
+  const uint32_t p0 = (a0 & word) | (b0 & ~word), p1 = (a1 & word) | (b1 & ~word);
+#pragma unroll
+  for (int g = 0; g < 3; ++g)
+    x[g] = tab_spread8(p0 >> (8 * g)) + 2u * tab_spread8(p1 >> (8 * g)) + 4u * tab_spread8(word >> (8 * g));
 }
 
 // Per-position bit masks of magnitudes (mag[w], byte i = position 4w + i;
 // every magnitude is below 128): nonzero (byte + 0x7F carries into bit 7
-// exactly when the byte is nonzero) and bit 1; a multiply by 0x01020408
-// gathers bit 0 of four bytes into the top nibble.
-LLVQ_HD uint32_t tab_nonzero_mask(const uint32_t (&mag)[6]) {
-  uint32_t nz = 0;
+// exactly when the byte is nonzero) and bit 1, both gathered by one multiply
+// (0x01020408 moves bit 0 of four bytes into the top nibble; nonzero in bit
+// 0 and bit 1 in bit 4 of each byte give nonzero bits 24-27 and bit-1 bits
+// 28-31).
+LLVQ_HD void tab_magnitude_masks(const uint32_t (&mag)[6], uint32_t& nz, uint32_t& b1) {
+  nz = 0;
+  b1 = 0;
 #pragma unroll
-  for (int w = 0; w < 6; ++w)
-    nz |= (((((mag[w] + 0x7F7F7F7Fu) >> 7) & 0x01010101u) * 0x01020408u) >> 24) << (4 * w);
-  return nz;
+  for (int w = 0; w < 6; ++w) {
+    const uint32_t t = mag[w];
+    const uint32_t f = ((((t + 0x7F7F7F7Fu) >> 7) & 0x01010101u) | ((t << 3) & 0x10101010u)) * 0x01020408u;
+    nz |= ((f >> 24) & 15u) << (4 * w);
+    b1 |= (f >> 28) << (4 * w);
+  }
 }
 
-LLVQ_HD uint32_t tab_bit1_mask(const uint32_t (&mag)[6]) {
-  uint32_t b1 = 0;
-#pragma unroll
-  for (int w = 0; w < 6; ++w) b1 |= ((((mag[w] >> 1) & 0x01010101u) * 0x01020408u) >> 24) << (4 * w);
-  return b1;
-}
-
-// Negative coordinates of an even codeword from its magnitudes and sign
+// Negative coordinates of an even codeword from its nonzero mask and sign
 // rank: the rank's bits go to the nonzero coordinates in position order,
 // with the bit at the first word coordinate inserted so that the negative
 // word coordinates have the class's parity (rank_even_signs /
 // apply_even_signs, impl/leech_lattice_vector_quantizer.py:804-841).  False
 // when the rank is out of range for the magnitudes (no valid index).
-LLVQ_HD bool tab_even_neg(const uint32_t (&mag)[6], uint32_t word, uint64_t sign, int parity_bit,
-                          const uint8_t* deposit4, uint32_t& neg) {
-  const uint32_t nzmask = tab_nonzero_mask(mag);
+LLVQ_HD bool tab_even_neg(uint32_t nzmask, uint32_t word, uint64_t sign, int parity_bit, const uint8_t* deposit4,
+                          uint32_t& neg) {
   const int nz = tab_popc(nzmask);
   bool ok;
   uint32_t cmask;
@@ -346,18 +338,6 @@ LLVQ_HD int tab_classify(const TabCtx& tc, int64_t v, int& k) {
   return (int)((tab_crec<SMEM>(tc, k, 0).y >> 16) & 3u);
 }
 
-// 96-bit insert: nibble string t (its low `bits` bits valid, the rest zero)
-// at bit offset `at` (a multiple of 4, below 96) of x.
-LLVQ_HD void tab_put96(uint32_t (&x)[3], uint64_t t, int at) {
-  const int w = at >> 5, o = at & 31;
-  const uint32_t lo = (uint32_t)t, mid = (uint32_t)(t >> 32);
-  const uint32_t p0 = lo << o, p1 = tab_fshl(lo, mid, o), p2 = o ? mid >> (32 - o) : 0u;
-  // word w gets p0, w + 1 gets p1, w + 2 gets p2 (bits past 96 are dropped)
-  x[0] |= w == 0 ? p0 : 0u;
-  x[1] |= w == 0 ? p1 : w == 1 ? p0 : 0u;
-  x[2] |= w == 0 ? p2 : w == 1 ? p1 : p0;
-}
-
 // Magnitudes by position (mag[w], byte i = position 4w + i) and the mask of
 // negative coordinates of the valid index v of class k, on one path for every
 // decode shape (so the lanes of a warp that hold different shapes diverge
@@ -390,65 +370,53 @@ LLVQ_HD bool tab_decode_mn(const TabCtx& tc, int64_t v, int k, uint32_t (&mag)[6
     c2w = c2.w;
   }
   const int nsearch = shape <= kShapeEven24 ? 2 : shape == kShapeEven16 ? 1 : 0;
-  uint32_t x1[3] = {0, 0, 0};
-  uint64_t t2 = 0;
-  if (split) t2 = tab_ldg(tc.tail + tab_srec<SMEM>(tc, s2, 0).x + r2);  // independent of P1
-  int at = 0;
+  uint32_t t2 = 0;
+  if (split) t2 = tab_ldg(tc.tail2 + tab_srec<SMEM>(tc, s2, 0).x + r2);  // independent of P1
+  uint32_t nib[2] = {0, 0};
 #pragma unroll
-  for (int it = 0; it < 2; ++it) {
-    if (it < nsearch) {
-      const uint4 r0 = tab_srec<SMEM>(tc, s1, 0);
-      const uint32_t nib = tab_search<SMEM>(tc, r0, s1, r1);
-      tab_put96(x1, nib, at);
-      at += 4 * (int)((r0.z >> 8) & 15u);
-    }
-  }
-  tab_put96(x1, tab_ldg(tc.tail + tab_srec<SMEM>(tc, s1, 0).x + r1), at);
+  for (int it = 0; it < 2; ++it)
+    if (it < nsearch) nib[it] = tab_search<SMEM>(tc, tab_srec<SMEM>(tc, s1, 0), s1, r1);
+  const uint32_t tbase = tab_srec<SMEM>(tc, s1, 0).x;
   uint32_t x[3], word;
-  if (shape == kShapeOdd24) {
-    word = tab_ldr<SMEM>(tc.golay + (int)cur);
-  } else if (shape == kShapeEven24) {
-    word = ((meta >> 8) & 1u) ? kFull24 : 0u;
+  if (!split) {
+    // one 24-position part: two searches of 6 positions, a tail of 12
+    const uint64_t t = tab_ldg(tc.tail + tbase + r1);
+    x[0] = nib[0] | (nib[1] << 24);
+    x[1] = (nib[1] >> 8) | ((uint32_t)t << 16);
+    x[2] = (uint32_t)(t >> 16);
+    word = shape == kShapeOdd24 ? tab_ldr<SMEM>(tc.golay + (int)cur) : (((meta >> 8) & 1u) ? kFull24 : 0u);
   } else {
+    // two parts as bit planes: P1 (a search of 4 positions and a tail of 12,
+    // or a tail of 12) and P2 (a tail of 8 or 12)
+    const uint32_t t1 = tab_ldg(tc.tail2 + tbase + r1);
+    uint32_t q0 = t1 & 0xFFFu, q1 = t1 >> 12;
+    if (shape == kShapeEven16) {
+      q0 = (nib[0] & 0xFu) | (q0 << 4);
+      q1 = ((nib[0] >> 8) & 0xFu) | (q1 << 4);
+    }
+    const uint32_t u0 = t2 & 0xFFFu, u1 = t2 >> 12;
+    const bool p1a = (meta >> 9) & 1u;
     const int slot = (int)((c2w >> 16) & 0xFFFu) + (int)(cur >> sshift);
     word = tab_ldr<SMEM>(tc.words + slot);
-    // part A value indices follow the d0 part-B values (no nibble overflows:
-    // indices stay below 8, and the nibbles past the part's end are dropped
-    // by the merge below)
-    uint32_t xa[3], xb[3];
-    const bool p1a = (meta >> 9) & 1u;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const uint32_t y2 = (uint32_t)(t2 >> (32 * q));
-      xa[q] = p1a ? x1[q] : y2;
-      xb[q] = p1a ? y2 : x1[q];
-    }
-    xa[2] = p1a ? x1[2] : 0u;
-    xb[2] = p1a ? 0u : x1[2];
-    const uint32_t add = (c2w >> 28) * 0x11111111u;
-    xa[0] += add;
-    xa[1] += add;
-    uint32_t m[3];
-    tab_expand2(xa, xb, tc.expand + (size_t)slot * (kTabExpandWords / 4), m);
-#pragma unroll
-    for (int q = 0; q < 3; ++q) x1[q] = (xa[q] & m[q]) | (xb[q] & ~m[q]);
+    tab_deposit_planes(p1a ? q0 : u0, p1a ? q1 : u1, p1a ? u0 : q0, p1a ? u1 : q1, word,
+                       tc.expand2 + (size_t)slot * (kTabExpand2Words / 4), x);
   }
-#pragma unroll
-  for (int q = 0; q < 3; ++q) x[q] = x1[q];
   const uint32_t vlo = c1.z, vhi = c1.w;
 #pragma unroll
   for (int q = 0; q < 3; ++q) {
     mag[2 * q] = tab_prmt(vlo, vhi, x[q] & 0xFFFFu);
     mag[2 * q + 1] = tab_prmt(vlo, vhi, x[q] >> 16);
   }
+  uint32_t nzmask, b1mask;
+  tab_magnitude_masks(mag, nzmask, b1mask);
   if (shape == kShapeOdd24) {
     // y = m where m = 1 mod 4 off the word or m = 3 mod 4 on it, else -m
     // (solve_odd_subclass's signed leader with the word's sign flips,
     // impl/leech_lattice_vector_quantizer.py:649-681)
-    neg = tab_bit1_mask(mag) ^ word;
+    neg = b1mask ^ word;
     return true;
   }
-  return tab_even_neg(mag, word, cur & ((1ull << sshift) - 1), (int)((meta >> 7) & 1u), tc.deposit4, neg);
+  return tab_even_neg(nzmask, word, cur & ((1ull << sshift) - 1), (int)((meta >> 7) & 1u), tc.deposit4, neg);
 }
 
 // Integer codeword of index v; false and zeros outside the codebook (or for
