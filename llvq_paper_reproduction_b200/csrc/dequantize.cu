@@ -98,23 +98,6 @@ __global__ void __launch_bounds__(kDeqThreads, kDeqMinBlocks) dequant_kernel(Ind
 // position 4w + j) and the mask of negative coordinates; the stores build
 // every output kind from it without forming the signed integers.
 
-// 2^23 + m as fp32 bits for the magnitude in byte j of w (m < 256).
-__device__ __forceinline__ float mag_float_2p23(uint32_t w, int j) {
-  return __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)j));
-}
-// fp32(fp32(1/sqrt 8) * m) in one rounding: (2^23 + m) * c - 2^23 * c.
-__device__ __forceinline__ float mag_scaled(uint32_t w, int j) {
-  return fmaf(mag_float_2p23(w, j), kLatticeScaleF, -8388608.0f * kLatticeScaleF);
-}
-// Sign bits of positions 2p and 2p + 1 of neg, as the sign bits of a bf16 pair.
-__device__ __forceinline__ uint32_t bf16_pair_signs(uint32_t neg, int p) {
-  return (((neg >> (2 * p)) & 3u) * 0x40008000u) & 0x80008000u;
-}
-__device__ __forceinline__ uint32_t bf16_pair(float lo, float hi) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
 // Output of one decoded index in every kind (streaming stores); row is
 // i / blocks_per_row (kind 3 only).  The sign is applied last (an exact
 // negation of the rounded magnitude product, since round-to-nearest is
@@ -172,26 +155,6 @@ __device__ __forceinline__ void store_mn(const uint32_t (&mag)[6], uint32_t neg,
       __stcs(o + q, make_uint4(w[0], w[1], w[2], w[3]));
     }
   }
-}
-
-__device__ __forceinline__ int64_t load_index_stream(IndexSource src, int64_t i) {
-  if (src.bytes == 8) return __ldcs(static_cast<const long long*>(src.ptr) + i);
-  return load_index(src, i);
-}
-
-// Decode of a valid or invalid index into (mag, neg); false (and zeros)
-// outside the codebook.
-template <bool SMEM>
-__device__ __forceinline__ bool tab_decode_any(const TabCtx& tc, int64_t v, uint32_t (&mag)[6], uint32_t& neg) {
-  bool ok = v >= 0 && v < tc.total;
-  neg = 0;
-  if (ok) ok = tab_decode_mn<SMEM>(tc, v, tab_find_class<SMEM>(tc, v), mag, neg);
-  if (!ok) {
-#pragma unroll
-    for (int w = 0; w < 6; ++w) mag[w] = 0;
-    neg = 0;
-  }
-  return ok;
 }
 
 // Table-driven dequantizer: a persistent grid; each CTA copies the small
@@ -306,19 +269,10 @@ __global__ void __launch_bounds__(kTabThreads, kTabMinBlocks) decode_rows_tab_ke
     uint64_t b;
     const uint64_t r = div_magic((uint64_t)i, (uint64_t)bpr, magic_bpr, b);
     uint4* o = reinterpret_cast<uint4*>(out + r * ldw + b * kDim);
+    uint32_t w[12];
+    bf16_codeword(mag, neg, w);
 #pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      uint32_t w[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int p = 4 * q + e;
-        const uint32_t mw = mag[p >> 1];
-        const int j = 2 * (p & 1);
-        w[e] = bf16_pair(mag_float_2p23(mw, j) - 8388608.0f, mag_float_2p23(mw, j + 1) - 8388608.0f) ^
-               bf16_pair_signs(neg, p);
-      }
-      o[q] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
+    for (int q = 0; q < 3; ++q) o[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
     v = vn;
   }
 }

@@ -7,21 +7,22 @@
 // Work is the flattened list of (weight tile of 128 rows, group of 8 index
 // blocks = 192 columns); each persistent CTA takes one contiguous range of it
 // (stream-K: every CTA gets the same number of groups, a tile can be shared by
-// consecutive CTAs).  Per CTA (one per SM, 22 warps):
-//   warps 0-15  decode the group's 128 x 8 blocks (two per thread) with the
-//               table-driven decoder and store them as bf16 into one of two
+// consecutive CTAs).  Per CTA (one per SM, 30 warps):
+//   warps 0-23  decode the group's 128 x 8 blocks (one or two per thread)
+//               with the table-driven decoder (its small tables copied to
+//               shared memory) and store them as bf16 into one of two
 //               group slots: three 64-column K-major sub-tiles in the 128-byte
 //               swizzle the MMA descriptors read; then fence the writes to the
 //               async proxy and arrive on the slot's "full" barrier;
-//   warp 16     (one thread) loads the activation columns of each 64-column
+//   warp 24     (one thread) loads the activation columns of each 64-column
 //               chunk with 2-D TMA (no multicast; rows >= m and columns >= k
 //               read as zero) into a ring of chunk slots;
-//   warp 17     (one thread) issues 4 tcgen05 MMAs per chunk (M = 128 weight
+//   warp 25     (one thread) issues 4 tcgen05 MMAs per chunk (M = 128 weight
 //               rows, N = m rounded up to 16, K = 16) into one of two TMEM
 //               accumulators and commits them to the chunk's and the group's
 //               "empty" barriers, and to the accumulator's "full" barrier at
 //               the end of a tile segment;
-//   warps 18-21 read a finished accumulator (one TMEM lane quarter each) and
+//   warps 26-29 read a finished accumulator (one TMEM lane quarter each) and
 //               write Y, scaled by fp32(1/sqrt 8) * row_scale (a whole tile),
 //               or the unscaled partial sums into the CTA's workspace slot (a
 //               tile shared with a neighbouring CTA).
@@ -55,10 +56,10 @@ constexpr int kFGroupBlocks = 8;             // index blocks per group: 192 colu
 constexpr int kFChunks = 3;
 constexpr int kFSubTile = kFRows * 128;      // one 64-column chunk of the weight tile: 16 KB
 constexpr int kFGroupBytes = kFChunks * kFSubTile;
-constexpr int kFDecodeWarps = 16;
+constexpr int kFDecodeWarps = 24;
 constexpr int kFDecodeThreads = kFDecodeWarps * 32;
 constexpr int kFWarps = kFDecodeWarps + 6;
-constexpr int kFThreads = kFWarps * 32;      // 704
+constexpr int kFThreads = kFWarps * 32;      // 960: at most 64 registers
 constexpr int kFTmaWarp = kFDecodeWarps, kFMmaWarp = kFDecodeWarps + 1, kFEpiWarp0 = kFDecodeWarps + 2;
 constexpr uint32_t kFWaitLimit = 1u << 22;
 constexpr size_t kFSmemBudget = 227 * 1024;
@@ -67,18 +68,31 @@ struct FusedLayout {
   int n_mma;        // MMA N: m rounded up to 16 (<= 256)
   int a_bytes;      // one activation chunk: n_mma rows x 128 B
   int a_slots;      // activation chunk ring
-  size_t off_a, off_sh, off_bar, smem;
+  TabSmem T;        // the decoder's shared tables, at off_tab (DecodeSharedBase first)
+  size_t off_a, off_tab, off_bar, smem;
 };
 
-FusedLayout fused_layout(int m) {
-  FusedLayout L;
+// Weight slots, then the activation ring, the decoder's tables (with the
+// Golay word lists when three activation slots still fit, else without:
+// those are read through the cache) and the barriers.
+FusedLayout fused_layout(const Codebook& cb, int m) {
+  FusedLayout L{};
   L.n_mma = (m + 15) / 16 * 16;
   L.a_bytes = L.n_mma * 128;
-  const size_t fixed = 2 * (size_t)kFGroupBytes + sizeof(DecodeSharedBase) + 1024 + 256;
-  L.a_slots = (int)std::min<size_t>(6, (kFSmemBudget - fixed) / (size_t)L.a_bytes);
+  const int ncls = (int)cb.cls.size(), nst = cb.dev.tab.n_states;
+  for (int with_words = 1; with_words >= 0; --with_words) {
+    const TabSmem T = tab_smem_layout(ncls, nst, ~size_t(0) >> 1, 0, with_words != 0);
+    const size_t fixed = 2 * (size_t)kFGroupBytes + (T.bytes + 15) / 16 * 16 + 1024 + 256;
+    const int slots = fixed >= kFSmemBudget ? 0 : (int)std::min<size_t>(6, (kFSmemBudget - fixed) / (size_t)L.a_bytes);
+    if (slots >= (with_words ? 3 : 2)) {
+      L.a_slots = slots;
+      L.T = T;
+      break;
+    }
+  }
   L.off_a = 2 * (size_t)kFGroupBytes;
-  L.off_sh = L.off_a + (size_t)L.a_slots * L.a_bytes;
-  L.off_bar = (L.off_sh + sizeof(DecodeSharedBase) + 7) / 8 * 8;
+  L.off_tab = L.off_a + (size_t)L.a_slots * L.a_bytes;
+  L.off_bar = (L.off_tab + L.T.bytes + 15) / 16 * 16;
   L.smem = L.off_bar + 8 * (size_t)(4 + 2 * L.a_slots + 5) + 16 + 1024;  // + alignment slack
   return L;
 }
@@ -88,16 +102,11 @@ __host__ __device__ __forceinline__ int cta_of(int64_t L, int C, int64_t g) {
   return (int)(((g + 1) * C + L - 1) / L) - 1;
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(int a, int b) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn((float)a, (float)b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
 }  // namespace
 
 __global__ void __launch_bounds__(kFThreads, 1)
     gemm_fused_kernel(const __grid_constant__ CUtensorMap ta, IndexSource index, int n_out, int bpr,
-                      DevBook book, const uint16_t* __restrict__ rscale, int m_act, int n_mma, int a_bytes,
+                      DevBook book, TabSmem T, const uint16_t* __restrict__ rscale, int m_act, int n_mma, int a_bytes,
                       int a_slots, uint32_t off_a, uint32_t off_sh, uint32_t off_bar, int64_t total_groups,
                       int groups_per_tile, float* __restrict__ Y, float* __restrict__ ws, int* error_flag) {
   extern __shared__ uint8_t smem_raw[];
@@ -123,6 +132,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
   while (tmem_cols < (uint32_t)(2 * n_mma)) tmem_cols <<= 1;
 
   decode_setup_base(book, sh);
+  tab_smem_fill(book, base + off_sh, T);
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(wfull(s), kFDecodeWarps);
@@ -147,44 +157,50 @@ __global__ void __launch_bounds__(kFThreads, 1)
   bool failed = false;
 
   if (warp < kFDecodeWarps) {
-    // ---- decoders: two blocks per thread per group (class and state records
-    // through the read-only cache: shared memory is taken by the operands)
-    const TabCtx tcx = tab_ctx<false>(book, sh, nullptr, TabSmem{});
-    for (int64_t g = gb; g < ge && !failed; ++g) {
-      const int i = (int)(g - gb), slot = i & 1;
-      const uint32_t use = (uint32_t)i >> 1;
-      if (use > 0 && !tc::mbar_wait(wempty(slot), (use - 1) & 1u, kFWaitLimit)) {
-        failed = true;
-        break;
-      }
-      const int tile = (int)(g / G), gl = (int)(g % G);
-      uint8_t* wslot = base + slot * kFGroupBytes;
-#pragma unroll 1
-      for (int blk = tid; blk < kFRows * kFGroupBlocks; blk += kFDecodeThreads) {
-        const int r = blk >> 3, j = blk & 7;
-        const int n = tile * kFRows + r, b = gl * kFGroupBlocks + j;
-        int y[kDim];
-        if (n < n_out && b < bpr) {
-          tab_decode<false>(tcx, load_index(index, (int64_t)n * bpr + b), y);
-        } else {
-#pragma unroll
-          for (int d = 0; d < kDim; ++d) y[d] = 0;
-        }
-#pragma unroll
-        for (int e = 0; e < 3; ++e) {
-          const int c8 = 3 * j + e, st = c8 >> 3, q = c8 & 7;
-          uint4 v;
-          v.x = pack_bf16x2(y[8 * e + 0], y[8 * e + 1]);
-          v.y = pack_bf16x2(y[8 * e + 2], y[8 * e + 3]);
-          v.z = pack_bf16x2(y[8 * e + 4], y[8 * e + 5]);
-          v.w = pack_bf16x2(y[8 * e + 6], y[8 * e + 7]);
-          *reinterpret_cast<uint4*>(wslot + st * kFSubTile + r * 128 + ((q ^ (r & 7)) << 4)) = v;
-        }
-      }
+    // ---- decoders: the CTA's blocks in one sequence (1024 per group), thread
+    // t taking t, t + 768, ...: every warp meets every group at least once
+    // (its blocks are 768 apart) and arrives on a group's barrier when it
+    // moves past it, so the decode work is spread evenly over the warps
+    const TabCtx tcx = tab_ctx<true>(book, sh, base + off_sh, T);
+    constexpr int kItems = kFRows * kFGroupBlocks;
+    const int64_t nitems = (ge - gb) * kItems;
+    int64_t cur_g = -1;
+    uint8_t* wslot = base;
+    auto finish_group = [&](int64_t g) {
       tc::fence_proxy_async();  // the MMA reads these bytes through the async proxy
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(wfull(slot));
+      if (lane == 0) tc::mbar_arrive(wfull((int)((g - gb) & 1)));
+    };
+#pragma unroll 1
+    for (int64_t it = tid; it < nitems; it += kFDecodeThreads) {
+      const int64_t g = gb + it / kItems;
+      if (g != cur_g) {
+        if (cur_g >= 0) finish_group(cur_g);
+        cur_g = g;
+        const int i = (int)(g - gb);
+        const uint32_t use = (uint32_t)i >> 1;
+        if (use > 0 && !tc::mbar_wait(wempty(i & 1), (use - 1) & 1u, kFWaitLimit)) {
+          failed = true;
+          break;
+        }
+        wslot = base + (i & 1) * kFGroupBytes;
+      }
+      const int tile = (int)(g / G), gl = (int)(g % G);
+      const int blk = (int)(it % kItems);
+      const int r = blk >> 3, j = blk & 7;
+      const int n = tile * kFRows + r, b = gl * kFGroupBlocks + j;
+      uint32_t mag[6], neg;
+      tab_decode_any<true>(tcx, n < n_out && b < bpr ? load_index(index, (int64_t)n * bpr + b) : -1, mag, neg);
+      uint32_t w[12];
+      bf16_codeword(mag, neg, w);
+#pragma unroll
+      for (int e = 0; e < 3; ++e) {
+        const int c8 = 3 * j + e, st = c8 >> 3, q = c8 & 7;
+        *reinterpret_cast<uint4*>(wslot + st * kFSubTile + r * 128 + ((q ^ (r & 7)) << 4)) =
+            make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+      }
     }
+    if (cur_g >= 0 && !failed) finish_group(cur_g);
   } else if (warp == kFTmaWarp) {
     if (lane == 0) {  // ---- activation chunks
       uint32_t q = 0;
@@ -331,7 +347,9 @@ __global__ void __launch_bounds__(256) gemm_fused_fixup(int n_out, const uint16_
   }
 }
 
-bool gemm_fused_ok(const Codebook& cb, int64_t m) { return cb.dev.tab.state && m > kGemvMaxM && m <= 256; }
+bool gemm_fused_ok(const Codebook& cb, int64_t m) {
+  return cb.dev.tab.state && m > kGemvMaxM && m <= 256 && fused_layout(cb, (int)m).a_slots >= 2;
+}
 
 int64_t gemm_fused_workspace_bytes(int64_t n_out, int64_t bpr, int64_t m, int sms) {
   const int64_t total = ((n_out + kFRows - 1) / kFRows) * ((bpr + kFGroupBlocks - 1) / kFGroupBlocks);
@@ -344,7 +362,7 @@ cudaError_t gemm_fused_launch(const Codebook& cb, IndexSource idx, int64_t n_out
                               int64_t workspace_bytes, int sms, cudaStream_t stream) {
   if (m <= 0 || n_out <= 0) return cudaSuccess;
   if (!gemm_fused_ok(cb, m)) return cudaErrorInvalidValue;
-  const FusedLayout L = fused_layout((int)m);
+  const FusedLayout L = fused_layout(cb, (int)m);
   if (L.a_slots < 2) return cudaErrorInvalidValue;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -364,8 +382,8 @@ cudaError_t gemm_fused_launch(const Codebook& cb, IndexSource idx, int64_t n_out
   e = encode_bf16_map(&ta, a, (uint64_t)k, (uint64_t)m, (uint64_t)k, (uint32_t)L.n_mma);
   if (e != cudaSuccess) return e;
   gemm_fused_kernel<<<ctas, kFThreads, L.smem, stream>>>(
-      ta, idx, (int)n_out, (int)bpr, cb.dev, rscale, (int)m, L.n_mma, L.a_bytes, L.a_slots, (uint32_t)L.off_a,
-      (uint32_t)L.off_sh, (uint32_t)L.off_bar, total, (int)G, y, static_cast<float*>(workspace), error_flag);
+      ta, idx, (int)n_out, (int)bpr, cb.dev, L.T, rscale, (int)m, L.n_mma, L.a_bytes, L.a_slots, (uint32_t)L.off_a,
+      (uint32_t)L.off_tab, (uint32_t)L.off_bar, total, (int)G, y, static_cast<float*>(workspace), error_flag);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   gemm_fused_fixup<<<(unsigned)tiles, 256, 0, stream>>>((int)n_out, rscale, (int)m, L.n_mma, total, (int)G, ctas,

@@ -42,8 +42,9 @@ __device__ __forceinline__ float dot8(uint4 v, const float* w, float acc) {
 }
 
 // One output row n by one warp: lane l decodes blocks l, l + 32, ... of the
-// row (decode(v, w)), multiplies each by the matching activations of every
-// batch row in fp32, then a fixed shuffle tree adds the lanes.
+// row (decode(v, wf): the 24 integer codeword entries as fp32), multiplies
+// each by the matching activations of every batch row in fp32, then a fixed
+// shuffle tree adds the lanes.
 template <int MB, class Decode>
 __device__ __forceinline__ void gemv_row(IndexSource index, int n, int n_out, int bpr,
                                          const uint16_t* __restrict__ rscale, const __nv_bfloat16* __restrict__ a,
@@ -53,11 +54,8 @@ __device__ __forceinline__ void gemv_row(IndexSource index, int n, int n_out, in
 #pragma unroll
   for (int i = 0; i < MB; ++i) acc[i] = 0.f;
   for (int b = lane; b < bpr && 24 * b < k; b += 32) {
-    int w[kDim];
-    decode(load_index(index, (int64_t)n * bpr + b), w);
     float wf[kDim];
-#pragma unroll
-    for (int d = 0; d < kDim; ++d) wf[d] = (float)w[d];
+    decode(load_index(index, (int64_t)n * bpr + b), wf);
     const int c0 = 24 * b, valid = min(kDim, k - c0);  // 8, 16 or 24: k is a multiple of 8
 #pragma unroll
     for (int i = 0; i < MB; ++i) {
@@ -96,8 +94,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_decode_kernel(IndexSource i
   const int warp = threadIdx.x >> 5;
   const int n = blockIdx.x * (kGemvThreads / 32) + warp;
   if (n >= n_out) return;  // whole warps only, after the block's one barrier
-  gemv_row<MB>(index, n, n_out, bpr, rscale, a, m, k, y,
-               [&](int64_t v, int (&w)[kDim]) { decode_index(v, book, sh, w); });
+  gemv_row<MB>(index, n, n_out, bpr, rscale, a, m, k, y, [&](int64_t v, float (&wf)[kDim]) {
+    int w[kDim];
+    decode_index(v, book, sh, w);
+#pragma unroll
+    for (int d = 0; d < kDim; ++d) wf[d] = (float)w[d];
+  });
 }
 
 // Table-driven decoder: a persistent grid; each CTA copies the class and
@@ -116,8 +118,20 @@ __global__ void __launch_bounds__(kGemvTabThreads, kGemvTabBlocks) gemv_tab_kern
   const TabCtx tc = tab_ctx<MODE == 2>(book, sh, dsm, L);
   const int warp = threadIdx.x >> 5, warps = kGemvTabThreads / 32;
   for (int n = blockIdx.x * warps + warp; n < n_out; n += gridDim.x * warps)
-    gemv_row<MB>(index, n, n_out, bpr, rscale, a, m, k, y,
-                 [&](int64_t v, int (&w)[kDim]) { tab_decode<MODE == 2>(tc, v, w); });
+    gemv_row<MB>(index, n, n_out, bpr, rscale, a, m, k, y, [&](int64_t v, float (&wf)[kDim]) {
+      // magnitudes to fp32 (2^23 + m minus 2^23, exact), then the sign bit
+      uint32_t mag[6], neg;
+      tab_decode_any<MODE == 2>(tc, v, mag, neg);
+#pragma unroll
+      for (int p = 0; p < kDim / 2; ++p) {
+        const uint32_t mw = mag[p >> 1];
+        const int j = 2 * (p & 1);
+        const float2 f = __fadd2_rn(make_float2(mag_float_2p23(mw, j), mag_float_2p23(mw, j + 1)),
+                                    make_float2(-8388608.0f, -8388608.0f));
+        wf[2 * p] = __int_as_float(__float_as_int(f.x) ^ (int)(((neg >> (2 * p)) & 1u) << 31));
+        wf[2 * p + 1] = __int_as_float(__float_as_int(f.y) ^ (int)(((neg >> (2 * p + 1)) & 1u) << 31));
+      }
+    });
 }
 
 cudaError_t gemv_decode_launch(const Codebook& cb, IndexSource idx, int64_t n_out, int64_t bpr,

@@ -26,6 +26,8 @@
 // signs use the closed form of rank_even_signs (llvq_device.cuh).
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include <cstdint>
 
 #include "llvq_device.cuh"
@@ -554,12 +556,15 @@ struct TabSmem {
 };
 
 // `extra` bytes (16-byte aligned) after the tables for the kernel's own use.
-inline TabSmem tab_smem_layout(int n_classes, int n_states, size_t budget, size_t extra = 0) {
+// Without `with_words` the two Golay word lists stay in global memory
+// (words == golay == 0).
+inline TabSmem tab_smem_layout(int n_classes, int n_states, size_t budget, size_t extra = 0,
+                               bool with_words = true) {
   TabSmem L{};
   size_t off = (sizeof(DecodeSharedBase) + 15) / 16 * 16;
   const size_t bucket = off; off += ((size_t)kBuckets * 4 + 15) / 16 * 16;
-  const size_t words = off; off += (size_t)kNumGolay * 4;
-  const size_t golay = off; off += (size_t)kNumGolay * 4;
+  const size_t words = with_words ? off : 0; off += with_words ? (size_t)kNumGolay * 4 : 0;
+  const size_t golay = with_words ? off : 0; off += with_words ? (size_t)kNumGolay * 4 : 0;
   const size_t crec = off; off += (size_t)n_classes * 16 * kTabClassRecords;
   const size_t srec = off; off += (size_t)n_states * 32;
   const size_t ext = off; off += (extra + 15) / 16 * 16;
@@ -583,10 +588,11 @@ __device__ __forceinline__ void tab_smem_fill(const DevBook& book, uint8_t* smem
   uint4* srec = reinterpret_cast<uint4*>(smem + L.srec);
   for (int i = threadIdx.x; i < kBuckets; i += blockDim.x)
     bucket[i] = (uint32_t)__ldg(book.bucket + i) | ((uint32_t)__ldg(book.bucket + i + 1) << 16);
-  for (int i = threadIdx.x; i < kNumGolay; i += blockDim.x) {
-    words[i] = __ldg(book.wlist_word + i);
-    golay[i] = __ldg(book.golay + i);
-  }
+  if (L.words)
+    for (int i = threadIdx.x; i < kNumGolay; i += blockDim.x) {
+      words[i] = __ldg(book.wlist_word + i);
+      golay[i] = __ldg(book.golay + i);
+    }
   // field-major: record j of class k at j * n_classes + k (spreads a warp's random records over the banks)
   for (int i = threadIdx.x; i < kTabClassRecords * book.n_classes; i += blockDim.x)
     crec[(i % kTabClassRecords) * book.n_classes + i / kTabClassRecords] = __ldg(book.tab.crec + i);
@@ -605,8 +611,8 @@ __device__ __forceinline__ TabCtx tab_ctx(const DevBook& book, const DecodeShare
   tc.crec = SMEM ? reinterpret_cast<const uint4*>(smem + L.crec) : book.tab.crec;
   tc.bucket = book.bucket;
   tc.bucket2 = SMEM ? reinterpret_cast<const uint32_t*>(smem + L.bucket) : nullptr;
-  tc.words = SMEM ? reinterpret_cast<const uint32_t*>(smem + L.words) : book.wlist_word;
-  tc.golay = SMEM ? reinterpret_cast<const uint32_t*>(smem + L.golay) : book.golay;
+  tc.words = SMEM && L.words ? reinterpret_cast<const uint32_t*>(smem + L.words) : book.wlist_word;
+  tc.golay = SMEM && L.words ? reinterpret_cast<const uint32_t*>(smem + L.golay) : book.golay;
   tc.starts = book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start;
   tc.deposit4 = sh.deposit4;
   tc.entry = book.tab.entry;
@@ -619,6 +625,61 @@ __device__ __forceinline__ TabCtx tab_ctx(const DevBook& book, const DecodeShare
   tc.max_searches = book.tab.max_searches;
   tc.total = book.total;
   return tc;
+}
+
+// ------------------------------------------------ decoded-form helpers
+//
+// The table-driven decoder's output is the 24 magnitudes by position
+// (mag[w], byte j = position 4w + j) and the mask of negative coordinates.
+
+// 2^23 + m as fp32 bits for the magnitude in byte j of w (m < 256).
+__device__ __forceinline__ float mag_float_2p23(uint32_t w, int j) {
+  return __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)j));
+}
+// fp32(fp32(1/sqrt 8) * m) in one rounding: (2^23 + m) * c - 2^23 * c.
+__device__ __forceinline__ float mag_scaled(uint32_t w, int j) {
+  return fmaf(mag_float_2p23(w, j), kLatticeScaleF, -8388608.0f * kLatticeScaleF);
+}
+// Sign bits of positions 2p and 2p + 1 of neg, as the sign bits of a bf16 pair.
+__device__ __forceinline__ uint32_t bf16_pair_signs(uint32_t neg, int p) {
+  return (((neg >> (2 * p)) & 3u) * 0x40008000u) & 0x80008000u;
+}
+__device__ __forceinline__ uint32_t bf16_pair(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// The integer codeword as 12 bf16 pairs (exact: |k| <= 22), positions 2p
+// and 2p + 1 in w[p].
+__device__ __forceinline__ void bf16_codeword(const uint32_t (&mag)[6], uint32_t neg, uint32_t (&w)[12]) {
+#pragma unroll
+  for (int p = 0; p < 12; ++p) {
+    const uint32_t mw = mag[p >> 1];
+    const int j = 2 * (p & 1);
+    const float2 f = __fadd2_rn(make_float2(mag_float_2p23(mw, j), mag_float_2p23(mw, j + 1)),
+                                make_float2(-8388608.0f, -8388608.0f));
+    w[p] = bf16_pair(f.x, f.y) ^ bf16_pair_signs(neg, p);
+  }
+}
+
+__device__ __forceinline__ int64_t load_index_stream(IndexSource src, int64_t i) {
+  if (src.bytes == 8) return __ldcs(static_cast<const long long*>(src.ptr) + i);
+  return load_index(src, i);
+}
+
+// Decode of a valid or invalid index into (mag, neg); false (and zeros)
+// outside the codebook.
+template <bool SMEM>
+__device__ __forceinline__ bool tab_decode_any(const TabCtx& tc, int64_t v, uint32_t (&mag)[6], uint32_t& neg) {
+  bool ok = v >= 0 && v < tc.total;
+  neg = 0;
+  if (ok) ok = tab_decode_mn<SMEM>(tc, v, tab_find_class<SMEM>(tc, v), mag, neg);
+  if (!ok) {
+#pragma unroll
+    for (int w = 0; w < 6; ++w) mag[w] = 0;
+    neg = 0;
+  }
+  return ok;
 }
 
 }  // namespace llvq
