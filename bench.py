@@ -47,9 +47,10 @@ FP32_LANES = 128
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) measured with ncu
 # on smaller launches of the same kernels, per unit, for the roofline
 # `traffic` entry: the search kernel on 65,536 blocks (6,622,720 + 663,040 B)
-# and the bf16 dequant kernel on 9,797,632 indices (78,706,688 + 418,110,976 B).
+# and the table-driven bf16 dequant kernel on 9,797,632 indices
+# (131,759,104 + 414,060,544 B).
 SEARCH_DRAM_BYTES_PER_BLOCK = (6_622_720 + 663_040) / 65_536
-DEQUANT_DRAM_BYTES_PER_INDEX = (78_706_688 + 418_110_976) / 9_797_632
+DEQUANT_DRAM_BYTES_PER_INDEX = (131_759_104 + 414_060_544) / 9_797_632
 
 
 def log(*a):
@@ -556,8 +557,8 @@ def dequant_bench(q, device, stream, args) -> dict:
                          "traffic": DEQUANT_DRAM_BYTES_PER_INDEX * n_idx,
                          "traffic_unit": "bytes per step (ncu on 9,797,632 indices, scaled by indices)",
                          "note": "56 B per index (8 B int64 index + 48 B bf16) + 2 B per row; the kernel is "
-                                 "instruction-bound (about 2 k thread instructions per index under ncu, ALU "
-                                 "pipe above 60%), not HBM-bound; peak of "
+                                 "SM-bound (about 790 thread instructions per index under ncu, ALU pipe 65%, "
+                                 "L1/shared data pipe 61%), not HBM-bound; peak of "
                                  + ("fallback" if peaks.get("fallback") else "measured") + " copy bandwidth"}}
 
 
