@@ -31,7 +31,7 @@ typedef enum {
   LLVQ_OK = 0,
   LLVQ_ERR_INVALID_ARGUMENT = 1, /* the reference raises ValueError (bad device, dtype, shape) */
   LLVQ_ERR_CUDA = 2,             /* the reference raises RuntimeError(str(CUresult)) */
-  LLVQ_ERR_UNSUPPORTED = 3,      /* codebook the library cannot index in int64 */
+  LLVQ_ERR_UNSUPPORTED = 3,      /* codebook the library cannot index in 64 bits */
   LLVQ_ERR_OUT_OF_MEMORY = 4,
   LLVQ_ERR_INDEX_RANGE = 5,      /* the reference raises IndexError */
   LLVQ_ERR_NOT_A_CODEWORD = 6    /* the reference's encode_codeword raises ValueError */
@@ -54,11 +54,17 @@ enum { LLVQ_FLAG_TABLE_DRIVEN = 1 /* score with the table-driven chains even if 
  * tables, offsets and counts on the host and uploads them to `device`
  * (device < 0: host-only codebook, usable by the *_host functions).
  * Replaces the table construction of LeechLatticeVectorQuantizerGpu.__init__
- * and its two *_cuda_metadata caches (_gpu.py:154-212, :345-518). */
+ * and its two *_cuda_metadata caches (_gpu.py:154-212, :345-518).
+ * Indices are unsigned 64-bit: a codebook may hold up to 2^64 - 2 codewords
+ * (shells 2..32 hold 1.09e19, past the reference's int64 torch.long), and
+ * every int64 index argument or output carries the two's-complement image of
+ * its unsigned value (negative from 2^63 on); -1 (all ones) is never a
+ * codeword and stays the invalid index. */
 int llvq_codebook_create(int32_t n_classes, const int32_t* shell, const int32_t* parity, const int32_t* leader,
                          int device, llvq_codebook** out);
 void llvq_codebook_destroy(llvq_codebook* cb);
-/* total_count (= reference total_count), class count, shell range, and whether
+/* total_count (= reference total_count, as the int64 image of an unsigned
+ * value), class count, shell range, and whether
  * generated scoring code matches this class list (1) or the table-driven path runs (0). */
 int llvq_codebook_info(const llvq_codebook* cb, int64_t* total_count, int32_t* n_classes, int32_t* min_shell,
                        int32_t* max_shell, int32_t* specialized);

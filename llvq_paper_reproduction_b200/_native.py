@@ -94,6 +94,12 @@ def load() -> ctypes.CDLL:
         return lib
 
 
+def as_int64(index: int) -> int:
+    """The int64 image of an unsigned 64-bit index (negative from 2^63 on)."""
+    i = int(index) & ((1 << 64) - 1)
+    return i - (1 << 64) if i >> 63 else i
+
+
 def check(status: int, what: str) -> None:
     """Raise the exception type the reference raises for this failure."""
     if status == OK:
@@ -130,7 +136,7 @@ class NativeCodebook:
             ctypes.c_int32()
         check(lib.llvq_codebook_info(self.handle, ctypes.byref(total), ctypes.byref(ncls), ctypes.byref(lo),
                                      ctypes.byref(hi), ctypes.byref(spec)), "llvq_codebook_info")
-        self.total_count = total.value
+        self.total_count = total.value & ((1 << 64) - 1)  # unsigned: codebooks past 2^63 use the full range
         self.n_classes = ncls.value
         self.min_shell = lo.value
         self.max_shell = hi.value
@@ -145,10 +151,11 @@ class NativeCodebook:
                 pass
             self.handle = None
 
-    # ---- host paths
+    # ---- host paths (indices are unsigned 64-bit: Python ints in
+    # [0, total_count); the int64 arguments carry their two's-complement image)
     def codeword(self, index: int) -> tuple[int, ...]:
         out = (ctypes.c_int32 * 24)()
-        check(self._lib.llvq_codeword_host(self.handle, int(index), out), "llvq_codeword_host")
+        check(self._lib.llvq_codeword_host(self.handle, as_int64(index), out), "llvq_codeword_host")
         return tuple(out)
 
     def codeword_batch(self, indices) -> tuple[np.ndarray, int]:
@@ -173,7 +180,7 @@ class NativeCodebook:
         v = (ctypes.c_int32 * 24)(*[int(a) for a in vector])
         idx = ctypes.c_int64()
         check(self._lib.llvq_encode_host(self.handle, v, ctypes.byref(idx)), "llvq_encode_host")
-        return idx.value
+        return idx.value & ((1 << 64) - 1)
 
     # ---- device paths (raw pointers; the callers own allocation and streams)
     def quantize(self, x_ptr: int, n: int, idx_ptr: int, pair_ptr: int, score_ptr: int, stream: int,

@@ -263,10 +263,12 @@ int build(llvq::Codebook& cb, int32_t n, const int32_t* shell, const int32_t* pa
     c.start = (int64_t)cursor;
     cb.class_start[k] = c.start;
     cursor += count;
-    if (cursor >> 63) return fail(LLVQ_ERR_UNSUPPORTED, "codebook has 2^63 or more codewords");
+    // indices are unsigned 64-bit (stored as the two's-complement int64
+    // image above 2^63); all ones stays the invalid index
+    if (cursor >= ((u128)1 << 64) - 1) return fail(LLVQ_ERR_UNSUPPORTED, "codebook has 2^64 - 1 or more codewords");
     build_chain(c, L);
   }
-  cb.total = (int64_t)cursor;
+  cb.total = (int64_t)(uint64_t)cursor;
   // window constants of the table-driven chains
   float l1max = 0, mg = 0, am = 0;
   for (const DevClass& c : cb.cls) {
@@ -619,7 +621,8 @@ int llvq_quantize_gain(const llvq_codebook* h, const float* x, int64_t n, int64_
   if (gain_bits < 1 || gain_bits > 16 || (row_sigma && blocks_per_row <= 0))
     return fail(LLVQ_ERR_INVALID_ARGUMENT, "gain code: need 1 <= gain_bits <= 16 and blocks_per_row > 0");
   if (!h) return fail(LLVQ_ERR_INVALID_ARGUMENT, "null codebook");
-  if (pack && (h->cb.total > 0 ? 64 - __builtin_clzll((unsigned long long)(h->cb.total - 1)) : 1) + gain_bits > 63)
+  if (pack && ((uint64_t)h->cb.total > 1 ? 64 - __builtin_clzll((unsigned long long)h->cb.total - 1ull) : 1) +
+                      gain_bits > 63)
     return fail(LLVQ_ERR_UNSUPPORTED, "packed shape-gain index exceeds 63 bits");
   llvq::GainCode gc;
   gc.thr = gain_thresholds;
@@ -849,13 +852,13 @@ int llvq_hadamard(const void* in, int32_t in_is_half, float* out, int64_t rows, 
 int llvq_codeword_host(const llvq_codebook* h, int64_t index, int32_t* out24) {
   if (!h || !out24) return fail(LLVQ_ERR_INVALID_ARGUMENT, "null argument");
   const llvq::Codebook& cb = h->cb;
-  if (index < 0 || index >= cb.total) return fail(LLVQ_ERR_INDEX_RANGE, "index outside codebook range");
+  if ((uint64_t)index >= (uint64_t)cb.total) return fail(LLVQ_ERR_INDEX_RANGE, "index outside codebook range");
   const int k = llvq::find_class(cb.class_start.data(), (int)cb.cls.size(), index);
   const llvq::DevClass& c = cb.cls[k];
   int y[llvq::kDim];
   const int wbase = cb.weight_start[c.even_weight];
   const bool ok = llvq::unrank_codeword(
-      c, (uint64_t)(index - c.start),
+      c, (uint64_t)index - (uint64_t)c.start,
       [&](int g) { return c.parity ? cb.golay[g] : cb.golay[cb.by_weight[wbase + g]]; }, y);
   if (!ok) return fail(LLVQ_ERR_INDEX_RANGE, "index does not decode");
   for (int d = 0; d < llvq::kDim; ++d) out24[d] = y[d];
@@ -907,7 +910,7 @@ int llvq_encode_host(const llvq_codebook* h, const int32_t* v, int64_t* index) {
       return fail(LLVQ_ERR_NOT_A_CODEWORD, "Golay codeword is not compatible with this class");
     const int choice = parity ? lex : (int)cb.golay_wrank[lex];
     const int64_t r = rank_codeword(c, y, word, choice);
-    if (r < 0) return fail(LLVQ_ERR_NOT_A_CODEWORD, "sign pattern is outside the class");
+    if (r == -1) return fail(LLVQ_ERR_NOT_A_CODEWORD, "sign pattern is outside the class");
     *index = r;
     return LLVQ_OK;
   }

@@ -379,7 +379,9 @@ __global__ void pack_kernel(const int64_t* __restrict__ in, int64_t n, int bytes
   const uint64_t ones = ~0ull >> (64 - 8 * bytes);
   const int64_t v = in[i];
   uint64_t u = (uint64_t)v;
-  if (v < 0 || u >= ones) {  // -1 and anything that does not fit become all-ones
+  // -1 and anything that does not fit become all-ones; with 8 bytes every
+  // other value is an (unsigned) index
+  if (bytes < 8 ? (v < 0 || u >= ones) : u == ones) {
     if (v != -1 && error_count) atomicAdd(error_count, 1);
     u = ones;
   }

@@ -358,7 +358,7 @@ __device__ __forceinline__ int find_class_bucketed(const DevBook& book, const in
   int lo = __ldg(book.bucket + key), hi = __ldg(book.bucket + key + 1) + 1;
   while (lo + 1 < hi) {
     const int mid = (lo + hi) >> 1;
-    if (starts[mid] <= v) lo = mid; else hi = mid;
+    if ((uint64_t)starts[mid] <= (uint64_t)v) lo = mid; else hi = mid;
   }
   return lo;
 }
@@ -370,7 +370,7 @@ __device__ __forceinline__ int find_class_bucketed(const DevBook& book, const in
 // to its position in the thread's shared-memory row.  The rest (none up to
 // shell 32) use the general step and a nibble sequence.
 __device__ __forceinline__ bool decode_index(int64_t v, const DevBook& book, DecodeShared& sh, int (&y)[kDim]) {
-  bool ok = v >= 0 && v < book.total;
+  bool ok = (uint64_t)v < (uint64_t)book.total;  // indices are unsigned (codebooks past 2^63)
   if (ok) {
     const int k = find_class_bucketed(book, book.n_classes <= kMaxSmemClasses ? sh.starts : book.class_start, v);
     const uint4* rp = reinterpret_cast<const uint4*>(book.dcls + k);
@@ -671,7 +671,7 @@ __device__ __forceinline__ int64_t load_index_stream(IndexSource src, int64_t i)
 // outside the codebook.
 template <bool SMEM>
 __device__ __forceinline__ bool tab_decode_any(const TabCtx& tc, int64_t v, uint32_t (&mag)[6], uint32_t& neg) {
-  bool ok = v >= 0 && v < tc.total;
+  bool ok = (uint64_t)v < (uint64_t)tc.total;
   neg = 0;
   if (ok) ok = tab_decode_mn<SMEM>(tc, v, tab_find_class<SMEM>(tc, v), mag, neg);
   if (!ok) {

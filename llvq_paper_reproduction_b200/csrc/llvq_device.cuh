@@ -297,7 +297,7 @@ LLVQ_HD int64_t rank_codeword(const DevClass& c, const int* y, uint32_t word, in
     if (r == UINT64_MAX) return -1;
     local = (uint64_t)golay_choice * c.perm_count + r;
   }
-  return c.start + (int64_t)local;
+  return (int64_t)((uint64_t)c.start + local);
 }
 
 // Decompose a class-local index and build the integer codeword.
@@ -353,7 +353,7 @@ LLVQ_HD int find_class(const int64_t* starts, int n, int64_t index) {
   int lo = 0, hi = n;
   while (lo + 1 < hi) {
     const int mid = (lo + hi) >> 1;
-    if (starts[mid] <= index) lo = mid; else hi = mid;
+    if ((uint64_t)starts[mid] <= (uint64_t)index) lo = mid; else hi = mid;
   }
   return lo;
 }

@@ -322,7 +322,7 @@ LLVQ_HD int tab_find_class(const TabCtx& tc, int64_t v) {
   }
   while (lo + 1 < hi) {
     const int mid = (lo + hi) >> 1;
-    if (tc.starts[mid] <= v) lo = mid; else hi = mid;
+    if ((uint64_t)tc.starts[mid] <= (uint64_t)v) lo = mid; else hi = mid;
   }
   return lo;
 }
@@ -330,7 +330,7 @@ LLVQ_HD int tab_find_class(const TabCtx& tc, int64_t v) {
 // Class and decode shape of an index (kShapeInvalid outside the codebook).
 template <bool SMEM>
 LLVQ_HD int tab_classify(const TabCtx& tc, int64_t v, int& k) {
-  if (!(v >= 0 && v < tc.total)) {
+  if (!((uint64_t)v < (uint64_t)tc.total)) {
     k = 0;
     return kShapeInvalid;
   }

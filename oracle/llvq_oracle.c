@@ -338,7 +338,7 @@ oracle_book* oracle_create(int min_shell, int max_shell) {
     }
     i128* theta = calloc((size_t)max_shell + 1, sizeof(i128));
     theta_counts(max_shell, theta);
-    int64_t cursor = 0;
+    uint64_t cursor = 0;
     u128 total = 0;
     gen_state s;
     memset(&s, 0, sizeof s);
@@ -361,15 +361,17 @@ oracle_book* oracle_create(int min_shell, int max_shell) {
         qsort(s.buf + first, (size_t)(s.n - first), sizeof(ocls), cmp_cls);
         u128 shell_total = 0;
         for (int k = first; k < s.n; ++k) {
-            s.buf[k].start = cursor + (int64_t)shell_total;
+            s.buf[k].start = (int64_t)(cursor + (uint64_t)shell_total);
             shell_total += s.buf[k].count;
         }
         if ((i128)shell_total != theta[m]) { s.overflow = 2; break; }
-        b->shell_offset[m] = cursor;
+        b->shell_offset[m] = (int64_t)cursor;
         b->shell_count[m] = (uint64_t)shell_total;
         total += shell_total;
-        if (total >> 63) { s.overflow = 1; break; }
-        cursor = (int64_t)total;
+        /* indices are unsigned 64-bit (two's-complement int64 images above
+           2^63); all ones stays free for "no index" */
+        if (total >= ((u128)1 << 64) - 1) { s.overflow = 1; break; }
+        cursor = (uint64_t)total;
     }
     free(theta);
     if (s.overflow) { free(s.buf); free(b); return NULL; }
@@ -731,7 +733,7 @@ int64_t oracle_encode(const oracle_book* b, const int32_t* yin) {
         if (!ok) return -1;
         local = (u128)g * c->perm_count + perm;
     }
-    return c->start + (int64_t)local;
+    return (int64_t)((uint64_t)c->start + (uint64_t)local);
 }
 
 /* apply_even_signs(): the sign_rank-th valid sign mask in increasing mask
@@ -756,12 +758,13 @@ static int apply_even_signs(int* v, u128 rank) {
 
 /* codeword(): index -> integer Leech vector (before the 1/sqrt(8) scale). */
 int oracle_codeword(const oracle_book* b, int64_t index, int32_t* out) {
-    if (index < 0 || (uint64_t)index >= b->total) return -1;
+    const uint64_t u = (uint64_t)index;  /* unsigned: codebooks past 2^63 use the full range */
+    if (u >= b->total) return -1;
     int ci = -1;
     for (int k = 0; k < b->ncls; ++k)
-        if (b->cls[k].start <= index) ci = k;
+        if ((uint64_t)b->cls[k].start <= u) ci = k;
     const ocls* c = &b->cls[ci];
-    u128 local = (u128)(index - c->start);
+    u128 local = (u128)(u - (uint64_t)c->start);
     u128 perm = local % c->perm_count;
     u128 cur = local / c->perm_count;
     u128 sign = cur % c->sign_count;

@@ -161,8 +161,11 @@ class OracleBook:
         return idx, g, k, s
 
     def codeword(self, index: int) -> tuple[int, ...]:
+        """Indices are unsigned 64-bit: pass a Python int below total_count
+        (or its two's-complement int64 image)."""
         y = np.zeros(DIM, dtype=np.int32)
-        if self._lib.oracle_codeword(self._h, int(index), y.ctypes.data):
+        i = int(index) & ((1 << 64) - 1)
+        if self._lib.oracle_codeword(self._h, i - (1 << 64) if i >> 63 else i, y.ctypes.data):
             raise IndexError(index)
         return tuple(int(v) for v in y)
 

@@ -190,3 +190,25 @@ def test_host_input_pipeline_matches_device_path(monkeypatch):
     pinned = x.pin_memory()
     outs = [q.quantize(pinned) for _ in range(4)]
     assert all(torch.equal(o, want) for o in outs)
+
+
+def test_shells_2_32_unsigned_indices():
+    """Shells 2..32 (1.09e19 codewords, past int64): indices are unsigned
+    64-bit, carried in int64 tensors as their two's-complement image.  Noisy
+    lattice points drawn above 2^63 quantize back to themselves, Gaussian rows
+    to the oracle's indices; dequantize_lattice across the unsigned range
+    against the oracle's codewords."""
+    q = api(32)
+    ob = oracle_book(32)
+    assert q.total_count == ob.total_count == 10918909325316807360
+    rng = np.random.default_rng(2032)
+    high = rng.integers(2**63, q.total_count, 12, dtype=np.uint64).view(np.int64)
+    y = ob.codeword_batch(high).astype(np.float64)
+    x = np.concatenate([y / np.sqrt(8.0) + 0.02 * rng.standard_normal(y.shape),
+                        1.6 * rng.standard_normal((12, 24))]).astype(np.float32)
+    got, _, _ = run(q, x)
+    np.testing.assert_array_equal(got[:12], high)
+    np.testing.assert_array_equal(got, ob.quantize_batch(x, mode=1)[0])
+    idx = rng.integers(0, q.total_count, 4000, dtype=np.uint64).view(np.int64)
+    lat = q.dequantize_lattice(torch.from_numpy(idx).cuda()).cpu().numpy()
+    np.testing.assert_array_equal(lat, ob.codeword_batch(idx, threads=0))

@@ -66,11 +66,27 @@ def test_error_mapping():
                                [c.leader for c in cls][::-1])
 
 
-def test_unsupported_codebook_size():
-    # shells 2..32 have more than 2^63 codewords: int64 indices cannot hold them
-    with pytest.raises(ValueError):
-        _book(32)
+def test_unsigned_indices_shells_2_32():
+    """Shells 2..32 have 1.09e19 codewords: more than int64 holds (the
+    reference's torch.long overflows) but fewer than 2^64 - 1, so indices are
+    unsigned 64-bit (int64 arguments carry their two's-complement image, -1
+    stays invalid).  Host decode and encode against the oracle, across 2^63."""
+    from conftest import oracle_book
+
     assert _book(31).total_count == 7501022209994367600
+    hb = _book(32)
+    assert hb.total_count == 10918909325316807360
+    ob = oracle_book(32)
+    rng = np.random.default_rng(32)
+    idx = [int(v) for v in rng.integers(0, 2**63, 10, dtype=np.uint64)]
+    idx += [int(v) + 2**63 for v in rng.integers(0, hb.total_count - 2**63, 30, dtype=np.uint64)]
+    idx += [2**63 - 1, 2**63, hb.total_count - 1]
+    for i in idx:
+        y = hb.codeword(i)
+        assert y == ob.codeword(i)
+        assert hb.encode(y) == i
+    with pytest.raises(IndexError):
+        hb.codeword(hb.total_count)
 
 
 def test_api_class_host_paths():
