@@ -145,6 +145,77 @@ def cpu_reference_rate(x: np.ndarray, max_shell: int, mode: int = 0) -> tuple[fl
     return x.shape[0] / (time.perf_counter() - t0), threads
 
 
+def reference_gpu_bench(blocks: int = 2048, n_dequant: int = 1 << 20) -> dict:
+    """The reference's own GPU path (its NVRTC kernels, through its unmodified
+    LeechLatticeVectorQuantizerGpu installed in baseline/_ref) timed on this
+    GPU beside this library on the same inputs: quantize (shells 2..13) of
+    N(0,1) blocks and dequantize_lattice of random valid indices (int64
+    codewords, the reference's output kind).  Index agreement is counted:
+    this library returns the reference CPU quantizer's indices; the NVRTC
+    kernel scores in fp32 and may differ on near-ties."""
+    import torch
+
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "impl" / "leech_lattice_vector_quantizer_gpu.py").exists():
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    if str(ref_root) not in sys.path:
+        sys.path.insert(0, str(ref_root))
+    try:
+        from impl.leech_lattice_vector_quantizer_gpu import LeechLatticeVectorQuantizerGpu as RefGpu
+    except Exception as exc:  # the reference's optional CUDA imports failed
+        return {"unavailable": f"reference import failed: {exc!r}"[:200]}
+    from llvq_paper_reproduction_b200 import LeechLatticeVectorQuantizerGpu
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    with tempfile.TemporaryDirectory() as cache:
+        ref = RefGpu(max_shell=13, cache_dir=cache, use_cache=False, device=dev)
+    ours = LeechLatticeVectorQuantizerGpu(max_shell=13, use_cache=False, device=dev)
+
+    def timed(fn, reps: int) -> float:
+        fn()  # first call: NVRTC compile / codebook upload
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1000.0 / reps
+
+    x = torch.randn((blocks, 24), generator=torch.Generator().manual_seed(1), dtype=torch.float32).to(dev)
+    t_ref = timed(lambda: ref.quantize_cuda(x), 3)
+    t_ours = timed(lambda: ours.quantize(x), 3)
+    equal = int((ref.quantize_cuda(x) == ours.quantize(x)).sum().item())
+    g = torch.Generator(device=dev).manual_seed(3)
+    idx = torch.randint(0, ours.total_count, (n_dequant,), generator=g, device=dev)
+    td_ref = timed(lambda: ref.dequantize_lattice_cuda(idx), 5)
+    td_ours = timed(lambda: ours.dequantize_lattice(idx), 5)
+    ref_cw, our_cw = ref.dequantize_lattice_cuda(idx), ours.dequantize_lattice(idx)
+    differ = (ref_cw != our_cw.view_as(ref_cw)).any(dim=1)
+    n_differ = int(differ.sum().item())
+    # where the two disagree, ask the reference's own CPU codeword() (pure Python)
+    sample = idx[differ][:16].tolist()
+    ref_cpu_agrees = {"b200": 0, "reference_gpu": 0, "checked": len(sample)}
+    for i, v in zip(sample, torch.nonzero(differ).view(-1)[:16].tolist()):
+        truth = tuple(ref.codeword(int(i)))
+        ref_cpu_agrees["b200"] += tuple(our_cw.view_as(ref_cw)[v].tolist()) == truth
+        ref_cpu_agrees["reference_gpu"] += tuple(ref_cw[v].tolist()) == truth
+    nbytes = n_dequant * (8 + 24 * 8)
+    return {
+        "workload": f"quantize: {blocks} N(0,1) blocks (torch CPU generator seed 1), shells 2..13; "
+                    f"dequantize_lattice: {n_dequant} indices uniform over [0, total) (seed 3), int64 codewords",
+        "kernels": "reference NVRTC kernels (compute_100 PTX, JIT) through its LeechLatticeVectorQuantizerGpu, "
+                   "against this library's sm_100a kernels, same GPU, same inputs",
+        "quantize": {"reference_blocks_per_s": blocks / t_ref, "b200_blocks_per_s": blocks / t_ours,
+                     "speedup": t_ref / t_ours, "index_equal": equal, "blocks": blocks},
+        "dequantize_lattice": {"reference_gbs": nbytes / td_ref / 1e9, "b200_gbs": nbytes / td_ours / 1e9,
+                               "speedup": td_ref / td_ours, "rows_differing": n_differ,
+                               "reference_cpu_codeword_agrees_on_differing_sample": ref_cpu_agrees,
+                               "indices": n_dequant},
+    }
+
+
 def run_reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -172,6 +243,14 @@ def run_reference_arm(args) -> None:
         "cpu_baseline": {"value": value, "unit": "blocks/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "blocks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.skip_reference_gpu:
+        try:
+            import torch
+
+            line["reference_gpu"] = (reference_gpu_bench() if torch.cuda.is_available()
+                                     else {"unavailable": "no CUDA device"})
+        except Exception as exc:  # keep the CPU baseline line whatever the GPU comparison does
+            line["reference_gpu"] = {"unavailable": f"{exc!r}"[:200]}
     print(json.dumps(line), flush=True)
 
 
@@ -637,6 +716,8 @@ def main():
     ap.add_argument("--cpu-dequant-sample", type=int, default=200_000)
     ap.add_argument("--skip-gemm", action="store_true")
     ap.add_argument("--skip-config1", action="store_true")
+    ap.add_argument("--skip-reference-gpu", action="store_true",
+                    help="--impl reference: skip timing the reference's NVRTC kernels on the GPU")
     ap.add_argument("--model-layers", type=int, default=32,
                     help="Llama-2-7B layers of the whole-model quantization section (0 skips it)")
     ap.add_argument("--sweep-rows", type=int, default=4_194_304,
