@@ -6,8 +6,10 @@ Seeding sys.modules with this library's shims under those module names makes
 the unmodified reference class run on the sm_100a kernels; its quantize and
 dequantize must then equal the oracle.
 
-Needs a GPU and a checkout of the reference whose root directory is given in
-the environment variable LLVQ_REFERENCE_ROOT (skipped otherwise)."""
+Needs a GPU and the reference: its copy installed in baseline/_ref (pip
+install --target of a checkout copy whose pyproject.toml declares packages =
+["impl"]), or a checkout whose root directory is given in the environment
+variable LLVQ_REFERENCE_ROOT (skipped when neither exists)."""
 from __future__ import annotations
 
 import os
@@ -20,13 +22,14 @@ import torch
 from conftest import oracle_book
 
 pytestmark = pytest.mark.gpu
-ROOT = os.environ.get("LLVQ_REFERENCE_ROOT", "")
+_INSTALLED = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+ROOT = os.environ.get("LLVQ_REFERENCE_ROOT") or (_INSTALLED if os.path.isdir(_INSTALLED) else "")
 
 
 @pytest.fixture(scope="module")
 def reference_gpu_module():
     if not ROOT or not os.path.isdir(os.path.join(ROOT, "impl")):
-        pytest.skip("LLVQ_REFERENCE_ROOT does not name a reference checkout")
+        pytest.skip("no reference: neither baseline/_ref nor LLVQ_REFERENCE_ROOT")
     from llvq_paper_reproduction_b200 import llvq_cuda_dequantize, llvq_cuda_quantize
 
     sys.modules["impl.llvq_cuda_quantize"] = llvq_cuda_quantize
