@@ -462,6 +462,13 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
         t = torch.tensor([mean_rate], dtype=torch.float64, device=device)
         dist.all_reduce(t)
         mean_rate = float(t.item()) / world
+    if world > 1:  # set up the point-to-point connections of the gather outside the timed region
+        import torch.distributed as dist
+
+        probe = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.gather(probe, [torch.empty_like(probe) for _ in range(world)] if rank == 0 else None, dst=0)
+        torch.cuda.synchronize()
+        barrier()
     t0 = time.perf_counter()
     local = {k: (r["indices"], r["row_scale"]) for k, r in results.items()}  # stay on the device
     index_bytes = (mq.sg.bits + 7) // 8  # 48-bit shape-gain index -> 6 bytes per block on the wire
