@@ -200,6 +200,63 @@ class _Emitter:
         return self.lines
 
 
+class _PackedEmitter:
+    """The same tries for a word pair (c, ~c) held in the two lanes of float2
+    operands: FFMA2 below the roots (one instruction for both words, each lane
+    rounded exactly like the scalar FFMA), two scalar FFMAs at a root (its
+    addend, the shell offset, is a scalar), and per-lane 3-input maxima."""
+
+    def __init__(self, min_shell, angular=False):
+        self.min_shell = min_shell
+        self.angular = angular
+        self.lines = []
+        self.tmp = 0
+        self.pending = False
+
+    def leaf(self, name, indent):
+        if not self.pending:
+            self.pending = True
+            self.lines.append(f"{indent}pend = {name};")
+        else:
+            self.lines.append(f"{indent}b.x = llvq_max3(b.x, pend.x, {name}.x); "
+                              f"b.y = llvq_max3(b.y, pend.y, {name}.y);")
+            self.pending = False
+
+    def run(self, items):
+        trie = {}
+        for k, shell, chain in items:
+            node = trie.setdefault(shell, {"kids": {}, "ends": []})
+            for t in chain:
+                node = node["kids"].setdefault(t, {"kids": {}, "ends": []})
+            node["ends"].append(k)
+
+        def visit(node, parent, indent, shell, root):
+            for term, child in node["kids"].items():
+                arr, coef, idx = term
+                operand = f"{arr}p" if arr.startswith("P") else f"{arr}p[{idx}]"
+                self.tmp += 1
+                name = f"t{self.tmp}"
+                c = scaled(coef, shell, self.angular)
+                if root:
+                    self.lines.append(f"{indent}{{ const float2 {name} = make_float2(fmaf({c!r}f, {operand}.x, {parent}), "
+                                      f"fmaf({c!r}f, {operand}.y, {parent}));")
+                else:
+                    self.lines.append(f"{indent}{{ const float2 {name} = __ffma2_rn(make_float2({c!r}f, {c!r}f), "
+                                      f"{operand}, {parent});")
+                for _ in child["ends"]:
+                    self.leaf(name, indent + "  ")
+                visit(child, name, indent + "  ", shell, False)
+                self.lines.append(f"{indent}}}")
+
+        for shell, root in trie.items():
+            assert not root["ends"]
+            visit(root, "0.0f" if self.angular else f"nmk[{shell - self.min_shell}]", "    ", shell, True)
+        if self.pending:
+            self.lines.append("    b.x = fmaxf(b.x, pend.x); b.y = fmaxf(b.y, pend.y);")
+            self.pending = False
+        return self.lines
+
+
 # Golay words per weight; the scoring code a word runs is the odd classes'
 # plus the even classes' of its weight.
 WORDS_BY_WEIGHT = {0: 1, 8: 759, 12: 2576, 16: 759, 24: 1}
@@ -285,6 +342,22 @@ def emit_spec(name, classes, angular=False):
     L("    float b = -INFINITY;" + (" float pend;" if body else ""))
     lines.extend(body)
     L("    (void)R; (void)nmk;")
+    L("    return b;")
+    L("  }")
+    L("  __device__ __forceinline__ static float2 odd_max2(const float2 (&Rp)[25], const float* nmk) {")
+    body = _PackedEmitter(min_shell, angular).run(items(1))
+    L("    float2 b = make_float2(-INFINITY, -INFINITY);" + (" float2 pend;" if body else ""))
+    lines.extend(body)
+    L("    (void)Rp; (void)nmk;")
+    L("    return b;")
+    L("  }")
+    # both words of a weight-12 pair run the weight-12 classes
+    L("  __device__ __forceinline__ static float2 even_max2_w12(const float2 (&R0p)[25], const float2 (&R1p)[25], "
+      "float2 P0p, float2 P1p, const float* nmk) {")
+    body = _PackedEmitter(min_shell, angular).run(items(0, 12))
+    L("    float2 b = make_float2(-INFINITY, -INFINITY);" + (" float2 pend;" if body else ""))
+    lines.extend(body)
+    L("    (void)R0p; (void)R1p; (void)P0p; (void)P1p; (void)nmk;")
     L("    return b;")
     L("  }")
     L("  template <class F>")
