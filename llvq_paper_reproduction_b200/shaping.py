@@ -19,7 +19,10 @@ but the package does not exist); it is defined here as:
   * gain: g = <x, u> (the least-squares gain for that direction), coded with
     a b-bit Lloyd-Max quantizer designed for the chi(24) density scaled by
     sigma (the norm of a 24-D N(0, sigma^2 I) block);
-  * index = shape_index * 2^b + gain_index, reconstruction g_q * u.
+  * index = shape_index * 2^b + gain_index, reconstruction g_q * u;
+  * optional post-shape gain code (fit_gain_code): the levels refitted as the
+    mean projection <x, u> of each gain cell on a sample, given the shapes
+    the quantizer picked -- the MSE-optimal scale of every cell's blocks.
 The shape search and the gain code run in one library call
 (llvq_quantize_gain): the finalize kernel that ranks the winning codeword
 also forms g = <x, y> / |y| in fp64 (the compensated projection of the
@@ -122,6 +125,40 @@ def chi_lloyd_max(bits: int, dof: int = DIM, iters: int = 400) -> tuple[np.ndarr
     return levels, 0.5 * (levels[:-1] + levels[1:])
 
 
+def lloyd_max_empirical(sample: np.ndarray, levels0: np.ndarray, iters: int = 500,
+                        tol: float = 1e-13) -> tuple[np.ndarray, np.ndarray]:
+    """Lloyd-Max levels and thresholds (ascending) for the empirical
+    distribution of a 1-D sample, started from levels0.
+
+    Cells follow the gain coder's rule: code i holds the values in
+    (thr[i-1], thr[i]] (the number of thresholds strictly below the value).
+    Each iteration places the thresholds at the midpoints of the levels and
+    moves every level with a non-empty cell to the mean of the sample values
+    in it, with sorted data and prefix sums (O(levels log n) per iteration).
+    The result is the last iteration's pair: thresholds at the midpoints of
+    the previous levels and levels at the means of the cells they bound, so
+    every non-empty cell's level is exactly its mean even when the iteration
+    stops before it converges."""
+    s = np.sort(np.asarray(sample, dtype=np.float64).ravel())
+    if s.size == 0:
+        raise ValueError("empty sample")
+    prefix = np.concatenate([[0.0], np.cumsum(s)])
+    levels = np.sort(np.asarray(levels0, dtype=np.float64))
+    thr = 0.5 * (levels[:-1] + levels[1:])
+    for _ in range(max(1, iters)):
+        thr = 0.5 * (levels[:-1] + levels[1:])
+        bounds = np.concatenate([[0], np.searchsorted(s, thr, side="right"), [s.size]])
+        count = np.diff(bounds)
+        mean = (prefix[bounds[1:]] - prefix[bounds[:-1]]) / np.maximum(count, 1)
+        new = np.where(count > 0, mean, levels)
+        new = np.maximum.accumulate(new)  # an empty cell keeps its level; stay ordered
+        done = np.max(np.abs(new - levels)) <= tol * max(1.0, float(np.max(np.abs(levels))))
+        levels = new
+        if done:
+            break
+    return levels, thr
+
+
 @dataclass(frozen=True)
 class RateSplit:
     shell: int
@@ -186,6 +223,63 @@ class ShapeGainQuantizer:
             return cls(hi, gb, sigma, device, min_shell=lo)
         split = rate_split(bits_per_dim)
         return cls(split.shell, split.gain_bits, sigma, device)
+
+    @classmethod
+    def for_rate_post_shape(cls, bits_per_dim: float, sigma: float = 1.0, device="cuda", multi_shell: bool = False,
+                            design_blocks: int = 65536, design_seed: int = 7) -> "ShapeGainQuantizer":
+        """for_rate with the gain code fitted after the shape quantizer
+        (fit_gain_code) on design_blocks N(0, sigma^2) blocks from a seeded
+        generator."""
+        sg = cls.for_rate(bits_per_dim, sigma, device, multi_shell)
+        g = torch.Generator().manual_seed(design_seed)
+        sg.fit_gain_code(torch.randn((design_blocks, DIM), generator=g, dtype=torch.float32) * sigma)
+        return sg
+
+    def projections(self, x: torch.Tensor, shape_idx: torch.Tensor,
+                    row_sigma: torch.Tensor | None = None) -> torch.Tensor:
+        """<x, y> / |y| (fp64) of every block with its shape codeword y,
+        divided by row_sigma when given: the value the gain code codes."""
+        dev = self.shape.device
+        x = torch.as_tensor(x, device=dev).reshape(-1, DIM).to(torch.float64)
+        y = self.shape.dequantize_lattice(shape_idx.reshape(-1).to(dev)).to(torch.float64)
+        c = (x * y).sum(dim=-1) / y.pow(2).sum(dim=-1).sqrt()
+        if row_sigma is not None:
+            sig = torch.broadcast_to(torch.as_tensor(row_sigma, dtype=torch.float32, device=dev),
+                                     shape_idx.shape).reshape(-1).to(torch.float64)
+            c = c / sig
+        return c
+
+    def fit_gain_code(self, x: torch.Tensor, row_sigma: torch.Tensor | None = None, iters: int = 500) -> dict:
+        """Optimal post-shape gain scales: refit the gain code to the
+        projections c = <x, u> of sample blocks on the directions u that the
+        shape quantizer picks for them.
+
+        Given the shapes, the reconstruction of a block with gain code i is
+        l_i u, and sum |x - l_i u|^2 = sum |x|^2 - 2 l_i c + l_i^2 over the
+        blocks of cell i is smallest at l_i = mean(c | cell i); the best
+        thresholds for given levels are their midpoints.  The code designed
+        for chi(24) (the norm |x|) ignores that c = |x| cos(theta) is smaller
+        than |x| by the shape's angular error; a Lloyd-Max iteration on the
+        sample of c, started from the chi(24) levels, fixes both conditions.
+        The shape search does not depend on the gain code (below), so one
+        pass of the shape quantizer over the sample suffices.
+
+        Joint (shape, gain) choice: with positive levels, min over (u, l) of
+        |x|^2 - 2 l <x, u> + l^2 takes, for every l, the u with the largest
+        <x, u>, so the sequential choice (largest correlation per unit norm,
+        then the nearest level to c) is the joint optimum (Sabin and Gray,
+        IEEE Trans. ASSP 32(3), 1984)."""
+        sidx, _ = self.quantize_parts(x, row_sigma)
+        ok = sidx.reshape(-1) >= 0
+        c = self.projections(x, sidx, row_sigma)[ok].cpu().numpy()
+        start = self.levels.double().cpu().numpy()
+        levels, thr = lloyd_max_empirical(c, start, iters=iters)
+        if np.any(levels <= 0):
+            raise ValueError("the fitted gain code has a non-positive level")
+        self.levels = torch.tensor(levels, dtype=torch.float32, device=self.shape.device)
+        self.thresholds = torch.tensor(thr, dtype=torch.float64, device=self.shape.device)
+        return {"blocks": int(c.size), "levels": levels, "thresholds": thr,
+                "mean_projection": float(c.mean()), "chi_levels": start}
 
     @property
     def bits(self) -> int:
