@@ -54,8 +54,9 @@ namespace llvq {
 // shells 2..13 and shell 23 codes 3 CTAs of 256 threads (8 pairs each); the
 // shell 32 code one CTA of 512 (4 pairs each).  The search is issue-bound and
 // the resident warps outweigh a few spilled bytes.  In the larger shapes the
-// CTA's warps realign at every pair (a barrier), so they run the same stretch
-// of the generated scoring code and share the instruction cache: 128 threads
+// warps realign at every pair (a barrier per four warps in 256-thread CTAs,
+// one for the whole 512-thread CTA), so they run the same stretch of the
+// generated scoring code and share the instruction cache: 128 threads
 // without the barrier ran 3.6% slower on shells 2..13, 26% slower on shell 23
 // and 37% slower on shell 32; on shell 32, 512 threads gain another 44% over
 // 256.  On the small codes the barrier costs about 2%.
@@ -622,10 +623,12 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Stage one block: x, validity, scale, sorted |x| order and the word tables.
-__device__ void stage_row(const float* __restrict__ x, int64_t row, RowShared& sh) {
+// The row's 24 values come from warp 0 (lane d holds x[row, d], loaded one
+// row ahead by the caller so that the load's latency overlaps the previous
+// row's search).
+__device__ void stage_row(float v, RowShared& sh) {
   const int tid = threadIdx.x, lane = tid & 31;
   if (tid < 32) {
-    const float v = lane < kDim ? x[row * kDim + lane] : 0.f;
     if (lane < kDim) sh.x[lane] = v;
     const unsigned bad = __ballot_sync(0xffffffffu, lane < kDim && !isfinite(v));
     const unsigned neg = __ballot_sync(0xffffffffu, lane < kDim && v < 0.f);
@@ -685,8 +688,10 @@ __global__ void __launch_bounds__(Ops<S>::kThreads, Ops<S>::kMinBlocks) search_k
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NS = Ops<S>::kNumShells;
   const int min_shell = Ops<S>::kMinShellC >= 0 ? Ops<S>::kMinShellC : book.min_shell;
+  float xv = (tid < kDim && blockIdx.x < n) ? x[(int64_t)blockIdx.x * kDim + tid] : 0.f;
   for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
-    stage_row(x, row, sh);
+    stage_row(xv, sh);
+    if (tid < kDim && row + gridDim.x < n) xv = x[(row + gridDim.x) * kDim + tid];  // next row
     if (sh.invalid) {
       if (tid == 0) {
         tag_out[row] = -1;
@@ -713,7 +718,14 @@ __global__ void __launch_bounds__(Ops<S>::kThreads, Ops<S>::kMinBlocks) search_k
       }
     };
     for (int i = 0; i < kPairsPerThread; ++i) {
-      if constexpr (Ops<S>::kRealign) __syncthreads();  // realign the CTA's warps (instruction cache)
+      // realign the warps (instruction cache): 256-thread CTAs in two groups
+      // of four warps (named barriers 1 and 2; +2% on shells 2..13 over one
+      // barrier for all eight), 512-thread CTAs all together (groups of four
+      // ran 15% slower on shell 32)
+      if constexpr (Ops<S>::kRealign) {
+        if constexpr (T == 256) asm volatile("bar.sync %0, 128;" ::"r"(1 + (warp >> 2)) : "memory");
+        else __syncthreads();
+      }
       const int j = i * T + tid;
       const uint32_t c = __ldg(book.plist_word + j);
       const int lex = __ldg(book.plist_lex + j);
