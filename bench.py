@@ -46,10 +46,10 @@ SMS = 148
 FP32_LANES = 128
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) measured with ncu
 # on smaller launches of the same kernels, per unit, for the roofline
-# `traffic` entry: the search kernel on 65,536 blocks (6,622,720 + 663,040 B)
+# `traffic` entry: the search kernel on 65,536 blocks (6,630,144 + 2,780,160 B)
 # and the table-driven bf16 dequant kernel on 9,797,632 indices
 # (131,759,104 + 414,060,544 B).
-SEARCH_DRAM_BYTES_PER_BLOCK = (6_622_720 + 663_040) / 65_536
+SEARCH_DRAM_BYTES_PER_BLOCK = (6_630_144 + 2_780_160) / 65_536
 DEQUANT_DRAM_BYTES_PER_INDEX = (131_759_104 + 414_060_544) / 9_797_632
 
 
