@@ -200,6 +200,25 @@ def _residue_counts(leader: ClassLeader, modulus: int, residues: tuple[int, ...]
 
 # ------------------------------------------------------------- class leaders
 
+# Word positions by weight (and all positions) of a Golay word list, shared by
+# every class built from the same list: one pass over the 4096 words instead
+# of one per class, and one tuple per weight instead of one per class.
+_WORDS_BY_WEIGHT: dict[int, tuple[Sequence[tuple[int, ...]], dict[int, tuple[int, ...]]]] = {}
+
+
+def _words_by_weight(golay_codewords: Sequence[tuple[int, ...]]) -> dict[int, tuple[int, ...]]:
+    hit = _WORDS_BY_WEIGHT.get(id(golay_codewords))
+    if hit is not None and hit[0] is golay_codewords:
+        return hit[1]
+    groups: dict[int, list[int]] = {}
+    for i, c in enumerate(golay_codewords):
+        groups.setdefault(sum(c), []).append(i)
+    table = {w: tuple(ix) for w, ix in groups.items()}
+    table[-1] = tuple(range(len(golay_codewords)))
+    _WORDS_BY_WEIGHT[id(golay_codewords)] = (golay_codewords, table)  # keeps the list alive: ids stay unique
+    return table
+
+
 def build_local_structure(shell: int, class_index: int, leader: ClassLeader,
                           golay_codewords: Sequence[tuple[int, ...]]) -> ClassLocalStructure:
     """Compatible Golay words, sign count and permutation count of one class.
@@ -209,9 +228,10 @@ def build_local_structure(shell: int, class_index: int, leader: ClassLeader,
     none when it is 0 and the leader sum is not 0 mod 8); magnitudes permuted
     independently inside and outside the word.  Odd class: every word, one sign
     pattern, all magnitude orderings."""
+    words = _words_by_weight(golay_codewords)
     if leader.parity == "even":
         w = leader.even_weight
-        golay = tuple(i for i, c in enumerate(golay_codewords) if sum(c) == w)
+        golay = words.get(w, ())
         if w == 0 and sum(leader.leader) % 8:
             signs = 0
         else:
@@ -219,7 +239,7 @@ def build_local_structure(shell: int, class_index: int, leader: ClassLeader,
         perms = multiset_permutation_count(_residue_counts(leader, 4, (0,))) * \
             multiset_permutation_count(_residue_counts(leader, 4, (2,)))
     elif leader.parity == "odd":
-        golay = tuple(range(len(golay_codewords)))
+        golay = words[-1]
         signs = 1
         perms = multiset_permutation_count(_residue_counts(leader, 2, (1,)))
     else:
