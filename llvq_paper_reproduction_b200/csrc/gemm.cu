@@ -66,10 +66,16 @@ constexpr int kAccCols = kMaxAct;  // fp32 columns per accumulator
 constexpr size_t kTmaBarOff = (size_t)kStages * kStageBytes;
 constexpr size_t kTmaSmem = kTmaBarOff + 8 * (2 * kStages + 5) + 16 + 1024;
 
+// Units are (weight tile, activation tile of kMaxAct rows, K split).  When
+// the units do not fill the last wave of CTAs, the units of that wave may be
+// split into two units of kMaxAct / 2 activation rows each (items from
+// full_units on: the activation map `ta_half`, MMA N = 128), so the last wave
+// takes half as long; a unit's outputs keep their K order.
 __global__ void __launch_bounds__(kTmaThreads, 1)
-    gemm_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ta, int kc_total,
-                    int w_rows, int n_base, int n_out, const uint16_t* __restrict__ rscale, int m_act,
-                    float* __restrict__ Y, int splits, int* error_flag) {
+    gemm_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ta,
+                    const __grid_constant__ CUtensorMap ta_half, int kc_total, int w_rows, int n_base, int n_out,
+                    const uint16_t* __restrict__ rscale, int m_act, float* __restrict__ Y, int splits,
+                    int full_units, int* error_flag) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -100,13 +106,20 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *holder;
   const int tn = (w_rows + kTileW - 1) / kTileW, tm = (m_act + kMaxAct - 1) / kMaxAct;
-  const int units = tn * tm * splits;
+  const int units = full_units + 2 * (tn * tm * splits - full_units);
   bool failed = false;
-  // unit -> (weight tile, activation tile, K split), splits fastest
-  auto unit_of = [&](int item, int& row0, int& m0, int& c_begin, int& c_end) {
+  // item -> (weight tile, activation rows m0 .. m0 + width, K split), splits fastest
+  auto unit_of = [&](int item, int& row0, int& m0, int& c_begin, int& c_end, int& width) {
+    int half = 0;
+    width = kMaxAct;
+    if (item >= full_units) {
+      half = (item - full_units) & 1;
+      item = full_units + ((item - full_units) >> 1);
+      width = kMaxAct / 2;
+    }
     const int split = item % splits, tile = item / splits;
     row0 = (tile / tm) * kTileW;
-    m0 = (tile % tm) * kMaxAct;
+    m0 = (tile % tm) * kMaxAct + half * (kMaxAct / 2);
     c_begin = kc_total * split / splits;
     c_end = kc_total * (split + 1) / splits;
   };
@@ -115,8 +128,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (lane == 0) {  // TMA producer
       uint32_t g = 0;
       for (int item = blockIdx.x; item < units && !failed; item += gridDim.x) {
-        int row0, m0, c_begin, c_end;
-        unit_of(item, row0, m0, c_begin, c_end);
+        int row0, m0, c_begin, c_end, width;
+        unit_of(item, row0, m0, c_begin, c_end, width);
+        const bool half = width < kMaxAct;
         for (int c = c_begin; c < c_end; ++c, ++g) {
           const int st = (int)(g % kStages);
           const uint32_t use = g / kStages;
@@ -125,9 +139,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             break;
           }
           const uint32_t sw = sbase + st * kStageBytes;
-          tc::mbar_arrive_expect_tx(full(st), kStageBytes);
+          tc::mbar_arrive_expect_tx(full(st), half ? kStageW + kStageA / 2 : kStageBytes);
           tc::tma_load_2d(sw, &tw, c * 64, row0, full(st));
-          tc::tma_load_2d(sw + kStageW, &ta, c * 64, m0, full(st));
+          tc::tma_load_2d(sw + kStageW, half ? &ta_half : &ta, c * 64, m0, full(st));
         }
       }
       // no copy may still be in flight when the block exits (after a timeout
@@ -137,12 +151,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
-      const uint32_t idesc = tc::idesc_bf16_f32(kTileW, kMaxAct);
+      const uint32_t idesc_full = tc::idesc_bf16_f32(kTileW, kMaxAct);
+      const uint32_t idesc_half = tc::idesc_bf16_f32(kTileW, kMaxAct / 2);
       uint32_t g = 0;
       int it = 0;
       for (int item = blockIdx.x; item < units && !failed; item += gridDim.x, ++it) {
-        int row0, m0, c_begin, c_end;
-        unit_of(item, row0, m0, c_begin, c_end);
+        int row0, m0, c_begin, c_end, width;
+        unit_of(item, row0, m0, c_begin, c_end, width);
+        const uint32_t idesc = width < kMaxAct ? idesc_half : idesc_full;
         const int a = it & 1;
         const uint32_t use_acc = (uint32_t)it >> 1;
         if (use_acc > 0 && !tc::mbar_wait(acc_empty(a), (use_acc - 1) & 1u, kWaitLimit)) {
@@ -176,8 +192,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const int q = warp & 3;
     int it = 0;
     for (int item = blockIdx.x; item < units && !failed; item += gridDim.x, ++it) {
-      int row0, m0, c_begin, c_end;
-      unit_of(item, row0, m0, c_begin, c_end);
+      int row0, m0, c_begin, c_end, width;
+      unit_of(item, row0, m0, c_begin, c_end, width);
       const int a = it & 1;
       if (!tc::mbar_wait(acc_full(a), ((uint32_t)it >> 1) & 1u, kWaitLimit)) {
         failed = true;
@@ -189,7 +205,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       float scale = kLatticeScaleF;
       if (rscale && live) scale = __fmul_rn(kLatticeScaleF, __half2float(__ushort_as_half(rscale[n])));
       const uint32_t t0 = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kAccCols);
-      for (int col0 = 0; col0 < kAccCols; col0 += 16) {
+      for (int col0 = 0; col0 < width; col0 += 16) {
         float v[16];
         tc::tmem_ld16(t0 + (uint32_t)col0, v);
         if (live) {
@@ -331,8 +347,10 @@ cudaError_t gemm_staged_launch(const Codebook& cb, IndexSource idx, int64_t n_ou
     configured[dev].store(true, std::memory_order_release);
   }
   const int ldw = (int)gemm_staging_ldw(bpr);
-  CUtensorMap ta;
+  CUtensorMap ta, ta_half;
   e = encode_bf16_map(&ta, a, (uint64_t)k, (uint64_t)m, (uint64_t)k, kMaxAct);
+  if (e != cudaSuccess) return e;
+  e = encode_bf16_map(&ta_half, a, (uint64_t)k, (uint64_t)m, (uint64_t)k, kMaxAct / 2);
   if (e != cudaSuccess) return e;
   int64_t chunk = std::min<int64_t>(n_out, staging_bytes / ((int64_t)ldw * 2));
   if (chunk < n_out) chunk = chunk / kTileW * kTileW;
@@ -352,11 +370,18 @@ cudaError_t gemm_staged_launch(const Codebook& cb, IndexSource idx, int64_t n_ou
     e = decode_rows_bf16_launch(cb, part, rows, (int)bpr, ldw, staging, stream);
     if (e != cudaSuccess) return e;
     const int items = ((rows + kTileW - 1) / kTileW) * (int)((m + kMaxAct - 1) / kMaxAct) * splits;
+    // halve the units of a partial last wave when the halves fit in one wave
+    int full_units = items;
+    if (splits == 1 && items > sms) {
+      const int tail = items % sms;
+      if (tail > 0 && 2 * tail <= sms) full_units = items - tail;
+    }
+    const int launch_items = full_units + 2 * (items - full_units);
     CUtensorMap tw;
     e = encode_bf16_map(&tw, staging, (uint64_t)ldw, (uint64_t)rows, (uint64_t)ldw, kTileW);
     if (e != cudaSuccess) return e;
-    gemm_tma_kernel<<<std::min(items, sms), kTmaThreads, kTmaSmem, stream>>>(
-        tw, ta, ldw / 64, rows, (int)n0, (int)n_out, rscale, (int)m, y, splits, error_flag);
+    gemm_tma_kernel<<<std::min(launch_items, sms), kTmaThreads, kTmaSmem, stream>>>(
+        tw, ta, ta_half, ldw / 64, rows, (int)n0, (int)n_out, rscale, (int)m, y, splits, full_units, error_flag);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

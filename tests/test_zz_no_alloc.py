@@ -48,9 +48,11 @@ def _run(q, fn_name, idx, a, scale):
 
 # (m, n, bpr, k): one with weights wider than the 16 MiB array holds at once
 # (K = 14336: 512 rows per chunk, 3 chunks), one with enough output tiles to
-# run without the K split, and small batches.
+# run without the K split, one whose single launch (llvq_gemm) splits the
+# tiles of its partial last wave into half-width tiles while the chunked
+# launches (no partial wave) do not, and small batches.
 CASES = [(300, 1300, 598, 14336), (513, 384, 171, 4096), (1100, 131, 3, 56), (1024, 4736, 8, 192),
-         (64, 256, 171, 4096), (1, 700, 40, 960)]
+         (4096, 1280, 598, 14336), (64, 256, 171, 4096), (1, 700, 40, 960)]
 
 
 @pytest.mark.parametrize("m,n,bpr,k", CASES)
