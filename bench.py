@@ -416,7 +416,8 @@ def run_gpu_arm(args) -> None:
                      "traffic_unit": "bytes per launch (ncu on 65,536 blocks, scaled by blocks)",
                      "note": f"{ops / 1e6:.3f} M algorithmic ops/block (2 per distinct nonzero leader value per "
                              "evaluated pair + 2x4096x24 prefix adds); peak = 148 SMs x 128 FP32 lanes x 2 x "
-                             "max SM clock (FFMA)"},
+                             "max SM clock (FFMA); achieved over the whole quantize step (search + finalize "
+                             "kernels; the search kernel is 97% of its device time in the launch list)"},
         "clocks": clk,
     }
     if cpu:
