@@ -33,12 +33,14 @@ def rel_err(y, ref):
 
 
 # the K range is split in two while the output has fewer 128 x 256 tiles
-# than SMs; (1024, 4736, 8, 192) has 148 tiles (no split); (300, 2500, 598,
-# 14336) is one staging chunk here and three in the no-allocation variant
+# than SMs; (1024, 4736, 8, 192) has 148 tiles (no split); (1100, 4736, 8,
+# 192) has 185 (148 + 37: the last wave's tiles are split into half-width
+# tiles, some of them wholly beyond the 1100 activation rows); (300, 2500,
+# 598, 14336) is one staging chunk here and three in the no-allocation variant
 @pytest.mark.parametrize("m_act,n,bpr,k", [(1, 128, 8, 192), (8, 300, 20, 472), (64, 256, 171, 4096),
                                            (200, 130, 25, 600), (256, 200, 12, 288), (300, 257, 9, 216),
                                            (16, 1024, 598, 14336), (513, 384, 171, 4096), (300, 2500, 598, 14336),
-                                           (1100, 131, 3, 56), (1024, 4736, 8, 192)])
+                                           (1100, 131, 3, 56), (1024, 4736, 8, 192), (1100, 4736, 8, 192)])
 def test_gemm_matches_dequantize_matmul(m_act, n, bpr, k):
     q = api()
     g = torch.Generator(device="cuda").manual_seed(4)
