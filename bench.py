@@ -16,7 +16,7 @@ scales); dequant-GEMM TFLOP/s on the Llama-3-8B MLP shapes at
 M = 1 ... 4096; shape-gain quantization at 1.0 ... 3.0 bits/dim and the
 spherical-shaping variant (blocks/s, SQNR).
 At every N: whole-model quantization of the Llama-2-7B-shaped linears,
-sharded by matrix over the ranks (blocks/s, plus the all-gather to rank 0).
+sharded by matrix over the ranks (blocks/s, plus the gather to rank 0).
 
 --impl reference times the reference algorithm on the host cores instead:
 the oracle's restatement of LeechLatticeVectorQuantizer.quantize (per-pair
@@ -431,8 +431,8 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
     --model-layers layers; seed 2): each rank quantizes its greedy share of
     whole matrices (synthetic fp16 weights, Hadamard rotation, row scales,
     shape-gain at 2 bits/dim) with no inter-GPU traffic, timed with CUDA
-    events on the launching stream (max over ranks); then one all-gather
-    brings every index tensor and row scale to rank 0, timed separately."""
+    events on the launching stream (max over ranks); then one gather brings
+    every index tensor and row scale to rank 0, timed separately the same way."""
     import torch
 
     from llvq_paper_reproduction_b200.model_quant import (MatrixQuantizer, MatrixSpec, gather_to_rank0,
@@ -470,12 +470,16 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
         dist.gather(probe, [torch.empty_like(probe) for _ in range(world)] if rank == 0 else None, dst=0)
         torch.cuda.synchronize()
         barrier()
-    t0 = time.perf_counter()
+    # the gather timed on the device (CUDA events on the stream its packing,
+    # NCCL gather and unpacking are ordered on), max over ranks
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
     local = {k: (r["indices"], r["row_scale"]) for k, r in results.items()}  # stay on the device
     index_bytes = (mq.sg.bits + 7) // 8  # 48-bit shape-gain index -> 6 bytes per block on the wire
     gathered = gather_to_rank0(specs, local, rank, world, device, index_bytes) if world > 1 else local
+    g1.record(stream)
     torch.cuda.synchronize()
-    gather_s = max_over_ranks(time.perf_counter() - t0)
+    gather_s = max_over_ranks(g0.elapsed_time(g1) / 1000.0)
     total = sum(s.blocks for s in specs)
     if rank == 0 and len(gathered) != len(specs):
         raise RuntimeError("gather lost matrices")
