@@ -471,15 +471,21 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
         torch.cuda.synchronize()
         barrier()
     # the gather timed on the device (CUDA events on the stream its packing,
-    # NCCL gather and unpacking are ordered on), max over ranks
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record(stream)
+    # NCCL gather and unpacking are ordered on), max over ranks, twice: the
+    # first includes NCCL's one-time setup of its large point-to-point
+    # transfers (about 50 ms at 2 GPUs), the second is the steady state
     local = {k: (r["indices"], r["row_scale"]) for k, r in results.items()}  # stay on the device
     index_bytes = (mq.sg.bits + 7) // 8  # 48-bit shape-gain index -> 6 bytes per block on the wire
-    gathered = gather_to_rank0(specs, local, rank, world, device, index_bytes) if world > 1 else local
-    g1.record(stream)
-    torch.cuda.synchronize()
-    gather_s = max_over_ranks(g0.elapsed_time(g1) / 1000.0)
+    times = []
+    for _ in range(2):
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        gathered = gather_to_rank0(specs, local, rank, world, device, index_bytes) if world > 1 else local
+        g1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        times.append(max_over_ranks(g0.elapsed_time(g1) / 1000.0))
+    gather_first_s, gather_s = times
     total = sum(s.blocks for s in specs)
     if rank == 0 and len(gathered) != len(specs):
         raise RuntimeError("gather lost matrices")
@@ -487,7 +493,8 @@ def model_quant_bench(rank, world, device, stream, args, barrier, max_over_ranks
                         "sharded by matrix (strong scaling)", "n_gpus": world, "seconds": secs,
             "blocks_per_s": total / secs, "mean_gpu_blocks_per_s": mean_rate,
             "strong_efficiency": (total / secs) / (world * mean_rate),
-            "gather_seconds": gather_s, "gather_bytes": total * index_bytes + sum(s.out_features for s in specs) * 4}
+            "gather_seconds": gather_s, "gather_first_seconds": gather_first_s,
+            "gather_bytes": total * index_bytes + sum(s.out_features for s in specs) * 4}
 
 
 def rate_sweep_bench(q, x, device, stream, args) -> dict:
