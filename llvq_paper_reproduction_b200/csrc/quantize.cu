@@ -335,15 +335,23 @@ struct Ops<RuntimeSpec> {
 // exactly one per coordinate; the t largest are the top t set bits.
 template <class Row>
 __device__ __forceinline__ void odd_sums(const Row& sh, uint32_t cA, float (&R)[25]) {
+  // positives (ranks of posA, largest first: lval[24 + r]) then negatives
+  // (ranks of the rest, smallest first: bit 23 - r of lo, lval[23 - r]); the
+  // two sets cover all 24 ranks, so w is never zero.  Two 32-bit halves
+  // with a select per step: +1.3% on shells 2..13 and +2% on shell 11 over
+  // one 64-bit mask with a 64-bit scan and clear.
   const uint32_t posA = cA ^ sh.nposA;
-  const uint32_t negA = ~posA & kFull24;
-  uint64_t m = ((uint64_t)posA << 24) | (uint64_t)(__brev(negA) >> 8);
+  uint32_t hi = posA, lo = __brev(~posA & kFull24) >> 8;
   R[0] = 0.f;
 #pragma unroll
   for (int t = 1; t <= kDim; ++t) {
-    const int j = 63 - __clzll((long long)m);
-    R[t] = R[t - 1] + sh.lval[j];
-    m ^= 1ull << j;
+    const bool h = hi != 0u;
+    const uint32_t w = h ? hi : lo;
+    const int b = 31 - __clz(w);
+    R[t] = R[t - 1] + sh.lval[b + (h ? 24 : 0)];
+    const uint32_t bit = 1u << b;
+    hi = h ? hi ^ bit : hi;
+    lo = h ? lo : lo ^ bit;
   }
 }
 
